@@ -1,0 +1,480 @@
+"""Benchmark of train.cpp's quantized-weight hot path on B200 (one JSON line on rank 0).
+
+Headline (the metric's configuration): GGUF legacy-block dequantization bandwidth, one
+4096 x 11008 tensor in each of Q4_0, Q4_1, Q5_0, Q5_1 and Q8_0 per step (1.07 GB of algorithmic
+traffic: packed bytes read + F32 bytes written). value = algorithmic GB/s of the whole job.
+With N GPUs (torchrun, one process per GPU) every rank dequantizes its own five-tensor set: the
+path shards by tensor with no collective, so per-GPU work is fixed ("scaling": "weak").
+
+Secondary (same line, key "mul_mat"): the F32 mul_mat of the fused Linear step (Q5_0 weight
+4096 x 14336, 2048 tokens: fused dequant forward, dX through transpose(W), dW) and of the GQA
+batched broadcast (A [128,2048,8,8] . B [128,2048,32,8], forward + composed backward, planes of
+ne[3] sharded across ranks), as TFLOP/s counting 2*K*M*N once per product.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-secondary]
+
+--impl reference times train.cpp's own CPU dequantizer (gguf_tensor_to_f32 of the reference,
+compiled from its sources into oracle/_ref) on the host cores, on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "train.cpp_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+import synth  # noqa: E402
+
+FORMATS = [synth.TYPE_Q4_0, synth.TYPE_Q4_1, synth.TYPE_Q5_0, synth.TYPE_Q5_1, synth.TYPE_Q8_0]
+NE0, NE1 = 4096, 11008
+N_BLOCKS = NE0 * NE1 // 32
+METRIC = "dequant HBM GB/s; F32 mul_mat TFLOP/s (roofline %) at 1/2/4/8 B200 vs CPU"
+
+
+def algorithmic_bytes(qtype: int, n_blocks: int) -> int:
+    return n_blocks * (synth.BLOCK_BYTES[qtype] + 128)
+
+
+STEP_BYTES = sum(algorithmic_bytes(t, N_BLOCKS) for t in FORMATS)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_value(name: str, key: str):
+    """A figure recorded from an ncu capture in profiles/<name> ("key: value" lines), or None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith(key + ":"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks sampler
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of this rank's GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ CPU baseline (reference code)
+def write_cfg2_gguf(path: Path, blocks: dict, chunks: int = 1) -> list[tuple[str, int, int]]:
+    """The five cfg2 tensors as a GGUF file, each split into `chunks` row ranges (separate GGUF
+    tensors, identical bytes) so several host threads can run the reference's per-tensor
+    dequantizer at once. Returns (name, type, n_elements) per GGUF tensor."""
+    tensors, names = [], []
+    rows_per = NE1 // chunks
+    for t in FORMATS:
+        bb = synth.BLOCK_BYTES[t]
+        raw = blocks[t]
+        for c in range(chunks):
+            r0 = c * rows_per
+            r1 = NE1 if c == chunks - 1 else r0 + rows_per
+            part = raw[r0 * (NE0 // 32) * bb: r1 * (NE0 // 32) * bb]
+            name = f"w.{t}.{c}"
+            tensors.append((name, t, (NE0, r1 - r0), part))
+            names.append((name, t, NE0 * (r1 - r0)))
+    synth.write_gguf(path, tensors)
+    return names
+
+
+def reference_dequant_rate(blocks: dict, threads: int, reps: int, kind_hint: str = "reference") -> dict:
+    """Times train.cpp's gguf_tensor_to_f32 (host dequant) over the cfg2 workload; one thread per
+    chunk, `threads` at a time. Falls back to the oracle restatement if oracle/_ref is absent."""
+    import oracle
+
+    chunks = max(1, threads // len(FORMATS)) if threads > len(FORMATS) else 1
+    use_ref = oracle.ref_available()
+    with tempfile.TemporaryDirectory() as td:
+        path = Path(td) / "cfg2.gguf"
+        names = write_cfg2_gguf(path, blocks, chunks)
+        outs = {n: np.empty(ne, dtype=np.float32) for n, _, ne in names}
+        if use_ref:
+            L = oracle.ref_lib()
+            handle = L.ref_gguf_open(str(path).encode())
+
+            def work(item):
+                n, _, ne = item
+                L.ref_gguf_tensor_to_f32(handle, n.encode(), outs[n].ctypes.data, ne)
+        else:
+            O = oracle.oracle_lib()
+            raw = {}
+            for t in FORMATS:
+                raw[t] = blocks[t]
+
+            def work(item):
+                n, t, ne = item
+                c = int(n.split(".")[2])
+                bb = synth.BLOCK_BYTES[t]
+                nb = ne // 32
+                start = c * (NE1 // chunks) * (NE0 // 32) * bb
+                src = raw[t][start: start + nb * bb]
+                O.oracle_dequant(t, src.ctypes.data, nb, outs[n].ctypes.data)
+
+        def run_once():
+            items = list(names)
+            lock = threading.Lock()
+
+            def worker():
+                while True:
+                    with lock:
+                        if not items:
+                            return
+                        it = items.pop(0)
+                    work(it)
+
+            ths = [threading.Thread(target=worker) for _ in range(min(threads, len(names)))]
+            t0 = time.perf_counter()
+            for th in ths:
+                th.start()
+            for th in ths:
+                th.join()
+            return time.perf_counter() - t0
+
+        run_once()  # warm (page in)
+        times = [run_once() for _ in range(reps)]
+        if use_ref:
+            oracle.ref_lib().ref_gguf_close(handle)
+    med = statistics.median(times)
+    return {"value": STEP_BYTES / med / 1e9, "unit": "GB/s", "cores": min(threads, len(names)),
+            "kind": "reference" if use_ref else "port",
+            "sample": f"full dequant workload (5 x 4096x11008 tensors, {STEP_BYTES/1e9:.3f} GB algorithmic), "
+                      f"median of {reps} passes, {len(names)} GGUF tensors over {min(threads, len(names))} threads",
+            "seconds_per_step": med}
+
+
+def make_blocks(seed_base: int) -> dict:
+    return {t: synth.random_blocks(t, N_BLOCKS, seed=seed_base + t) for t in FORMATS}
+
+
+# ------------------------------------------------------------------ the reference arm
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    blocks = make_blocks(1000)
+    threads = os.cpu_count() or 1
+    # each step is one pass over the workload; warmup passes run untimed
+    import oracle  # noqa: F401
+
+    res = reference_dequant_rate(blocks, threads, reps=max(1, args.steps) + max(0, args.warmup) - max(0, args.warmup))
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(res["value"], 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(res["seconds_per_step"] * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8->f32", "data": "synthetic (seeded PCG64 blocks per the configs)",
+        "config": {"workload": "dequant sweep: Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, one 4096x11008 tensor each",
+                   "step_bytes": STEP_BYTES, "device": "host CPU"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(res["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import trc_cuda as tc
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    tc.lib()
+    stream = torch.cuda.current_stream()
+    peaks = measured_peaks()
+
+    # ---- inputs: this rank's five tensors (weak scaling: a different seed per rank)
+    blocks = make_blocks(1000 + 97 * rank)
+    d_blocks = {t: torch.from_numpy(blocks[t]).cuda() for t in FORMATS}
+    d_out = {t: torch.empty(N_BLOCKS * 32, dtype=torch.float32, device="cuda") for t in FORMATS}
+    pinned = {t: torch.from_numpy(blocks[t]).pin_memory() for t in FORMATS}
+    staging = {t: torch.empty_like(d_blocks[t]) for t in FORMATS}
+    readback = torch.empty(len(FORMATS) * 32, dtype=torch.float32).pin_memory()
+
+    def step(events=None):
+        for i, t in enumerate(FORMATS):
+            if events is not None:
+                events[i][0].record(stream)
+            tc.gguf_tensor_to_f32(t, d_blocks[t], out=d_out[t])
+            if events is not None:
+                events[i][1].record(stream)
+
+    # correctness guard for the measured configuration (first tensor of each format, a slice)
+    step()
+    torch.cuda.synchronize()
+    import oracle
+
+    for t in FORMATS:
+        nb = 4096
+        want = oracle.dequant(t, blocks[t][: nb * synth.BLOCK_BYTES[t]], nb)
+        got = d_out[t][: nb * 32].cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"dequant mismatch for type {t}"
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in FORMATS]
+          for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = tc.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for k in range(args.steps):
+            step([ev[k][i] for i in range(len(FORMATS))])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    launches = tc.launch_count() - launches0
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(stop)) / args.steps
+    per_launch_ms = {t: statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(args.steps))
+                     for i, t in enumerate(FORMATS)}
+    value = world * STEP_BYTES / (ms * 1e-3) / 1e9
+
+    # roofline of the dominant kernel (dequant_kernel): bytes per launch / mean launch time
+    total_launch_ms = sum(per_launch_ms.values())
+    achieved = STEP_BYTES / (total_launch_ms * 1e-3) / 1e9
+    per_format = {synth_name(t): {"us": round(per_launch_ms[t] * 1e3, 2),
+                                  "GBps": round(algorithmic_bytes(t, N_BLOCKS) / (per_launch_ms[t] * 1e-3) / 1e9, 1)}
+                  for t in FORMATS}
+    traffic = profile_value("dequant_cfg2_ncu.txt", "dram_bytes_per_launch_mean")
+
+    # ---- end to end through the public API with host buffers: H2D packed bytes (pinned) +
+    # dequant (trc_cuda_load_quant) + D2H readback of the first block of each result
+    def e2e_step():
+        for i, t in enumerate(FORMATS):
+            tc.gguf_load_tensor(t, pinned[t], d_out[t], staging[t])
+        for i, t in enumerate(FORMATS):
+            readback[i * 32:(i + 1) * 32].copy_(d_out[t][:32], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    h2d = sum(blocks[t].nbytes for t in FORMATS)
+    e2e = {"value": round(world * STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": readback.numel() * 4,
+           "ms_per_step": round(e2e_ms, 4), "api": "trc_cuda_load_quant (host packed -> device F32)"}
+
+    # ---- secondary: the mul_mat workloads (tensor cores)
+    secondary = None
+    if not args.no_secondary:
+        secondary = run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = reference_dequant_rate(blocks, threads=1, reps=3)
+        cpu.pop("seconds_per_step", None)
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8->f32", "data": "synthetic (seeded PCG64 blocks per the configs)",
+            "config": {"workload": "dequant sweep: Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, one 4096x11008 tensor each per rank",
+                       "step_bytes_per_rank": STEP_BYTES, "parallelism": f"shard-by-tensor x{world}",
+                       "l2": "no flush needed: 1.07 GB touched per step > 126 MB L2, each tensor revisited "
+                             "only after the other four"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "peak_source": peaks["source"], "kernel": "dequant_kernel", "per_format": per_format},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "gpu_launches": launches,
+        }
+        if secondary is not None:
+            line["mul_mat"] = secondary
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def synth_name(t: int) -> str:
+    return {v: k for k, v in synth.TYPE_BY_NAME.items()}[t]
+
+
+def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args) -> dict:
+    """Fused Linear step (Q5_0 4096x14336, 2048 tokens) per rank, and the GQA batched broadcast
+    forward + backward with ne[3] planes sharded across ranks. TFLOP/s count 2*K*M*N once."""
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda").manual_seed(11 + rank)
+    reps, warm = max(3, min(args.steps, 10)), max(3, args.warmup)
+    tf32x3_peak = None  # derived: TF32 = half the bf16 rate, 3 passes
+    if peaks.get("bf16_tflops"):
+        tf32x3_peak = peaks["bf16_tflops"] / 2 / 3
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(a.elapsed_time(b)) / reps
+
+    out = {}
+    # --- fused Linear step
+    K, M, N = 4096, 14336, 2048
+    wq = torch.from_numpy(synth.random_blocks(synth.TYPE_Q5_0, K * M // 32, seed=21 + rank)).cuda()
+    X = torch.randn((N, K), generator=gen, device="cuda")
+    dY = torch.randn((N, M), generator=gen, device="cuda") * 1e-2
+    Y = torch.empty((N, M), device="cuda")
+    dX = torch.empty((N, K), device="cuda")
+    dW = torch.zeros((M, K), device="cuda")
+    flops = 2.0 * K * M * N
+    t_fwd = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y))
+    t_dx = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX))
+    # dW for an F32 LoRA-style copy: dW^T = mul_mat(T(dY), T(X)) accumulated into the grad buffer
+    t_dw = timed(lambda: tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True))
+    step_ms = t_fwd + t_dx + t_dw
+    out["linear_q5_0"] = {
+        "fwd_tflops": round(flops / t_fwd / 1e9, 2), "dx_tflops": round(flops / t_dx / 1e9, 2),
+        "dw_tflops": round(flops / t_dw / 1e9, 2), "step_ms": round(step_ms, 4),
+        "step_tflops": round(world * 3 * flops / step_ms / 1e9, 2),
+        "frac_of_3xtf32_peak": round(3 * flops / step_ms / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
+        "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
+    }
+    del wq, X, dY, Y, dX, dW
+    # --- GQA batched broadcast, planes of ne[3] sharded across ranks
+    p3 = max(1, 8 // world)
+    A = torch.randn((p3, 8, 2048, 128), generator=gen, device="cuda")
+    B = torch.randn((p3, 32, 2048, 128), generator=gen, device="cuda")
+    G = torch.randn((p3, 32, 2048, 2048), generator=gen, device="cuda")
+    D = torch.empty((p3, 32, 2048, 2048), device="cuda")
+    dA_pre = torch.empty((p3, 32, 128, 2048), device="cuda")
+    dA = torch.empty((p3, 8, 2048, 128), device="cuda")
+    dB = torch.empty((p3, 32, 2048, 128), device="cuda")
+    gflop = 2.0 * 128 * 2048 * 2048 * 32 * p3
+    t_f = timed(lambda: tc.mul_mat(A, B, out=D))
+    t_a = timed(lambda: (tc.mul_mat(G.transpose(-1, -2), B.transpose(-1, -2), out=dA_pre),
+                         tc.repeat_back(dA_pre.transpose(-1, -2), [128, 2048, 8, p3], out=dA)))
+    t_b = timed(lambda: tc.mul_mat(A.transpose(-1, -2), G, out=dB))
+    out["gqa_bcast"] = {
+        "fwd_tflops": round(world * gflop / t_f / 1e9, 2), "da_tflops": round(world * gflop / t_a / 1e9, 2),
+        "db_tflops": round(world * gflop / t_b / 1e9, 2), "step_ms": round(t_f + t_a + t_b, 4),
+        "step_tflops": round(world * 3 * gflop / (t_f + t_a + t_b) / 1e9, 2),
+        "frac_of_3xtf32_peak": round(3 * gflop / (t_f + t_a + t_b) / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
+        "shape": f"A [128,2048,8,{p3}] . B [128,2048,32,{p3}] per rank (ne[3] sharded over {world})",
+    }
+    out["peak_3xtf32_tflops"] = round(tf32x3_peak, 1) if tf32x3_peak else None
+    out["peak_note"] = "TF32 dense taken as half the measured bf16 burst rate; 3 passes"
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/* trc_cuda.h -- C ABI of libtrc_cuda.so: B200 (sm_100a) kernels for train.cpp's quantized-weight
+ * hot path (GGUF legacy-block dequantization + ggml-semantics F32 mul_mat and the graph ops of its
+ * composed backward).
+ *
+ * This is the drop-in boundary. train.cpp's abstract backend interface
+ * (include/traincpp/trc_backend.h:33-88: BufferType / Buffer / Device) is implemented in C++ by
+ * train.cpp_b200/backend/trc_cuda_backend.cpp, which calls only the functions below. Each entry
+ * point names the reference code it replaces. Paths are relative to the train.cpp source tree.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, and a `void* stream` that is a cudaStream_t (NULL = legacy stream).
+ *   - Every function returns an int status: TRC_CUDA_OK (0) or a negative TRC_CUDA_E* code. No
+ *     function aborts; the C++ backend maps a failure to train.cpp's TRC_ABORT with the message of
+ *     trc_cuda_status_string(), mirroring how the reference backends report fatal errors
+ *     (src/core/trc_impl.h:118-125).
+ *   - Device pointers are device-local memory of the current CUDA device. Kernels are enqueued on
+ *     `stream` and return without synchronising, except where a function says otherwise.
+ *   - Tensor views follow ggml: ne[0] is the innermost extent, nb[] are byte strides
+ *     (include/traincpp/trc_tensor.h:1-5, 37-70).
+ *   - There is no CPU fallback. Every compute entry point runs a kernel of this library.
+ */
+#ifndef TRC_CUDA_H
+#define TRC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TRC_CUDA_ABI_VERSION 1
+
+/* ------------------------------------------------------------------ status codes */
+enum {
+    TRC_CUDA_OK           = 0,
+    TRC_CUDA_EINVAL       = -1, /* null pointer, bad size, or a shape rule of the reference violated */
+    TRC_CUDA_EUNSUPPORTED = -2, /* element type or layout this library does not compute */
+    TRC_CUDA_EDEVICE      = -3, /* a kernel hit its wait limit; see trc_cuda_device_error() */
+    TRC_CUDA_ECUDA        = -4, /* a CUDA runtime call failed; see trc_cuda_last_cuda_error() */
+    TRC_CUDA_ENOMEM       = -5  /* a device allocation failed */
+};
+
+/* ggml / GGUF type ids of the legacy quantized blocks (include/traincpp/trc_types.h:11-49). */
+enum {
+    TRC_CUDA_TYPE_F32  = 0,
+    TRC_CUDA_TYPE_Q4_0 = 2,
+    TRC_CUDA_TYPE_Q4_1 = 3,
+    TRC_CUDA_TYPE_Q5_0 = 6,
+    TRC_CUDA_TYPE_Q5_1 = 7,
+    TRC_CUDA_TYPE_Q8_0 = 8
+};
+
+/* One ggml tensor view in device memory (the fields of Tensor that the kernels need:
+ * include/traincpp/trc_tensor.h:37-70; data = buffer base + Tensor::data_offset). */
+typedef struct trc_cuda_view {
+    void*   data;  /* device address of element (0,0,0,0) */
+    int64_t ne[4]; /* extents, ne[0] innermost */
+    int64_t nb[4]; /* byte strides */
+} trc_cuda_view;
+
+/* ------------------------------------------------------------------ library / diagnostics */
+
+/* TRC_CUDA_ABI_VERSION of the loaded library. */
+int trc_cuda_abi_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* trc_cuda_status_string(int status);
+
+/* The cudaError_t of the last failed CUDA runtime call in this thread (0 if none). */
+int trc_cuda_last_cuda_error(void);
+
+/* Reads (and, if reset != 0, clears) the device-side error word of the current device. A nonzero
+ * *code means a kernel gave up a bounded wait; its results are not valid. Synchronous. */
+int trc_cuda_device_error(int* code, int reset);
+
+/* Number of kernels this library has launched in this process (all devices). The bench reports
+ * the difference across its timed region as the count of native launches. */
+uint64_t trc_cuda_launch_count(void);
+
+/* Number of SMs of the current device (148 on B200). */
+int trc_cuda_sm_count(void);
+
+/* ------------------------------------------------------------------ GGUF legacy-block dequant */
+
+/* Bytes of one 32-weight block: Q4_0 18, Q4_1 20, Q5_0 22, Q5_1 24, Q8_0 34; 0 for other types.
+ * Replaces the block-size column of the type table (src/core/trc_types.cpp:22-32). */
+size_t trc_cuda_block_bytes(int type);
+
+/* Dequantize n_blocks consecutive blocks at `blocks` into 32*n_blocks floats at `out`, bit-exact
+ * with the reference. Replaces the Q* branch of gguf_tensor_to_f32 (src/io/trc_gguf.cpp:1040-1044)
+ * -> dequantize_q4_0 .. dequantize_q8_0 (src/io/trc_gguf.cpp:320-417).
+ * EUNSUPPORTED for a type that is not one of the five legacy formats (the reference rejects the
+ * others too: src/io/trc_gguf.cpp:1045-1047). */
+int trc_cuda_dequant(int type, const void* blocks, int64_t n_blocks, float* out, void* stream);
+
+/* One tensor of a batched dequantization. */
+typedef struct trc_cuda_dequant_job {
+    const void* blocks;   /* device address of the packed blocks */
+    float*      out;      /* device address of 32*n_blocks floats */
+    int64_t     n_blocks; /* >= 0 */
+    int32_t     type;     /* TRC_CUDA_TYPE_Q* */
+    int32_t     reserved;
+} trc_cuda_dequant_job;
+
+/* Dequantize many tensors (a whole model's shard) in as few launches as possible. `jobs` is a
+ * HOST array; it is passed to the kernel by value, 256 jobs per launch. Equivalent to calling
+ * gguf_load_tensor (src/io/trc_gguf.cpp:1051-1094) for each tensor, minus the host F32 copy. */
+int trc_cuda_dequant_many(const trc_cuda_dequant_job* jobs, int n_jobs, void* stream);
+
+/* Device-side gguf_load_tensor for a quantized tensor with an F32 destination
+ * (src/io/trc_gguf.cpp:1082-1089): copies the packed blocks from HOST memory `host_blocks` into
+ * the caller's device staging buffer (>= n_blocks*block_bytes bytes, 16-byte aligned), then
+ * dequantizes into `out`. Only the packed bytes cross PCIe (the reference copies the 4-8x larger
+ * F32 result). Pinned host memory makes the copy asynchronous; pageable memory is also accepted. */
+int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
+                        void* stream);
+
+/* ------------------------------------------------------------------ mul_mat */
+
+enum {
+    TRC_CUDA_MM_ACCUMULATE = 1u, /* d += a*b instead of d = a*b */
+    TRC_CUDA_MM_SIMT       = 2u  /* force the fp32 SIMT kernel (exact reference summation order);
+                                    the default picks the tcgen05 3xTF32 kernel when the layout allows */
+};
+
+/* ggml mul_mat: for every plane (i2, i3) of b,
+ *     d[i, j, i2, i3] (+)= sum_k a[k, i, i2 % a.ne2, i3 % a.ne3] * b[k, j, i2, i3]
+ * with a.ne0 == b.ne0 == K, d.ne = {a.ne1, b.ne1, b.ne2, b.ne3}, b.ne2 % a.ne2 == 0 and
+ * b.ne3 % a.ne3 == 0 (the rules of the constructor, src/ops/trc_ops.cpp:366-385). Any byte strides
+ * are accepted, including the transposed views the composed backward builds
+ * (src/core/trc_autograd.cpp:487-503). F32 in, F32 out.
+ * Replaces compute_mul_mat (src/backends/cpu/trc_cpu_ops.cpp:182-216).
+ * Accuracy: the tcgen05 kernel splits each operand into a TF32 head and tail (3xTF32) and stays
+ * within 1e-5 normwise (max|gpu - cpu| / max|cpu|) of the reference. The SIMT kernel reproduces
+ * the reference's summation bit for bit. */
+int trc_cuda_mul_mat(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags,
+                     void* stream);
+
+enum { TRC_CUDA_KERNEL_TCGEN05 = 1, TRC_CUDA_KERNEL_SIMT = 2 };
+
+/* Which kernel trc_cuda_mul_mat would run for these views and flags: TRC_CUDA_KERNEL_TCGEN05 (the
+ * TMA-fed 3xTF32 tensor-core kernel) or TRC_CUDA_KERNEL_SIMT; a negative status if the call would be
+ * rejected. Host-only; launches nothing. */
+int trc_cuda_mul_mat_kernel(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags);
+
+/* Fused dequant + mul_mat: like trc_cuda_mul_mat, but operand a is a frozen quantized weight held
+ * as packed blocks. The weight's logical F32 tensor W has ne = {w_ne0, w_ne1, 1, 1} (blocks run
+ * along ne0, rows are contiguous). a_transposed = 0 uses a = W, a_transposed = 1 uses
+ * a = transpose(W) (the dX = W^T dY product of the backward). The dequantized weight is never
+ * written to HBM: blocks are decoded into shared memory in the GEMM's producer stage.
+ * Results equal trc_cuda_mul_mat on the dequantized weight within the same tolerance. */
+int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                       const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags, void* stream);
+
+/* ------------------------------------------------------------------ graph ops of the backward */
+
+/* dst = src (same shape, any strides). Replaces compute_dup for OP_CONT / OP_DUP
+ * (src/backends/cpu/trc_cpu_ops.cpp:219-236). Bit-exact. */
+int trc_cuda_cont(const trc_cuda_view* src, const trc_cuda_view* dst, void* stream);
+
+/* In-place acc: for every element (i0..i3) of b,
+ *     dst_bytes[offset + i0*4 + i1*nb1 + i2*nb2 + i3*nb3] += b[i0, i1, i2, i3]
+ * where dst points at the contiguous destination tensor of total size dst_bytes bytes. The caller
+ * guarantees the region fits (the constructor asserts it, src/core/trc_tensor.cpp:322-360).
+ * Replaces compute_acc with inplace=1 (src/backends/cpu/trc_cpu_ops.cpp:954-998). Bit-exact. */
+int trc_cuda_acc(void* dst, int64_t dst_bytes, const trc_cuda_view* b, int64_t nb1, int64_t nb2, int64_t nb3,
+                 int64_t offset, void* stream);
+
+/* dst (contiguous) = sum of src over the dimensions it repeats: element i of src adds into element
+ * (i0 % dst.ne0, ..., i3 % dst.ne3), in the reference's order. Replaces compute_repeat_back
+ * (src/backends/cpu/trc_cpu_ops.cpp:932-951). Bit-exact. */
+int trc_cuda_repeat_back(const trc_cuda_view* src, const trc_cuda_view* dst, void* stream);
+
+/* dst = src tiled to dst's shape (index i_d % src.ne_d). Replaces compute_repeat (OP_REPEAT). */
+int trc_cuda_repeat(const trc_cuda_view* src, const trc_cuda_view* dst, void* stream);
+
+enum { TRC_CUDA_BIN_ADD = 0, TRC_CUDA_BIN_SUB = 1, TRC_CUDA_BIN_MUL = 2, TRC_CUDA_BIN_DIV = 3 };
+
+/* dst = a (op) b with b broadcast onto a's shape by index modulo (ggml_can_repeat(b, a)).
+ * Replaces the F32 cases of OP_ADD / OP_SUB / OP_MUL / OP_DIV. Bit-exact. */
+int trc_cuda_binary(int op, const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* dst, void* stream);
+
+/* Bytes of device workspace trc_cuda_sum needs for a tensor of n elements (at most 8 KiB). */
+size_t trc_cuda_sum_workspace_bytes(int64_t n);
+
+/* *dst (one float, device) = sum of every element of src, accumulated in double like the
+ * reference and rounded once to float. Deterministic two-pass reduction: the first pass writes one
+ * partial per thread block into the caller's device `workspace` (>= trc_cuda_sum_workspace_bytes,
+ * 8-byte aligned), the second pass adds the partials in a fixed order.
+ * Replaces compute_sum (OP_SUM, src/backends/cpu/trc_cpu_ops.cpp:302-315); agrees with it within
+ * double-precision summation error before the final rounding. */
+int trc_cuda_sum(const trc_cuda_view* src, float* dst, void* workspace, size_t workspace_bytes, void* stream);
+
+/* dst[0..n) = value. Replaces the host fill of Device::fill_tensors
+ * (src/core/trc_backend_reg.cpp:539-544) for device-local F32 tensors. */
+int trc_cuda_fill(float* dst, int64_t n, float value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRC_CUDA_H */

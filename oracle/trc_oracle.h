@@ -1,0 +1,67 @@
+/* trc_oracle.h -- TEST INFRASTRUCTURE: CPU restatement of train.cpp's quantized-weight hot path.
+ *
+ * This library is the parity checker for the CUDA path. It is never linked into, called by, or
+ * shipped with the product (libtrc_cuda.so). Only tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg load it.
+ *
+ * Every function restates one reference function (paths relative to the train.cpp source tree):
+ *   oracle_fp16_to_fp32   src/core/trc_float.h:23-40      (written from the IEEE-754 binary16
+ *                                                          definition, pinned bit-for-bit against
+ *                                                          the reference over all 65536 inputs)
+ *   oracle_fp32_to_fp16   src/core/trc_float.h:42-63      (round-to-nearest-even encoder)
+ *   oracle_dequant        src/io/trc_gguf.cpp:320-417     (dequantize_q4_0 .. dequantize_q8_0)
+ *   oracle_mul_mat        src/backends/cpu/trc_cpu_ops.cpp:182-216 (compute_mul_mat)
+ *   oracle_cont           src/backends/cpu/trc_cpu_ops.cpp:219-236 (compute_dup)
+ *   oracle_repeat_back    src/backends/cpu/trc_cpu_ops.cpp:932-951
+ *   oracle_acc            src/backends/cpu/trc_cpu_ops.cpp:954-998
+ *
+ * Parity status: pinned. tests/test_oracle.py checks this library against the reference's own
+ * known-answer tests (tests/test_gguf.cpp:355-444 of the reference) and against the reference
+ * compiled from its sources (oracle/_ref/libtrc_ref.so), bit-for-bit.
+ */
+#ifndef TRC_ORACLE_H
+#define TRC_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids (the values are the GGUF on-disk type ids). */
+enum { ORACLE_Q4_0 = 2, ORACLE_Q4_1 = 3, ORACLE_Q5_0 = 6, ORACLE_Q5_1 = 7, ORACLE_Q8_0 = 8 };
+
+float    oracle_fp16_to_fp32(uint16_t h);
+uint16_t oracle_fp32_to_fp16(float f);
+
+/* Bytes per 32-weight block (18/20/22/24/34), 0 for an unknown type. */
+size_t oracle_block_bytes(int type);
+
+/* Dequantize n_blocks consecutive blocks into 32*n_blocks floats. 0 = ok, -1 = unknown type. */
+int oracle_dequant(int type, const uint8_t* src, int64_t n_blocks, float* out);
+
+/* ggml mul_mat over byte-strided views: d[i,j,p2,p3] = sum_k a[k,i,p2%a2,p3%a3] * b[k,j,p2,p3],
+ * one float accumulator, k ascending (the reference's order, so results are bit-identical).
+ * ne/nb follow ggml: ne[0] innermost, nb[] in bytes. n_threads > 1 splits output columns. */
+int oracle_mul_mat(const void* a, const int64_t a_ne[4], const size_t a_nb[4],
+                   const void* b, const int64_t b_ne[4], const size_t b_nb[4],
+                   void* d, const int64_t d_ne[4], const size_t d_nb[4], int n_threads);
+
+/* dst (contiguous, ne = a_ne) = a (any strides). */
+void oracle_cont(const void* a, const int64_t a_ne[4], const size_t a_nb[4], float* dst);
+
+/* dst (contiguous, shape dst_ne) = sum of a over the dims it repeats (index i -> i % dst_ne). */
+void oracle_repeat_back(const void* a, const int64_t a_ne[4], const size_t a_nb[4],
+                        float* dst, const int64_t dst_ne[4]);
+
+/* In-place acc: for every element of b (any strides), dst_bytes[offset + i0*4 + i1*nb1 + i2*nb2
+ * + i3*nb3] += b[i]. dst is the byte base of the contiguous destination tensor. */
+void oracle_acc(void* dst, const void* b, const int64_t b_ne[4], const size_t b_nb[4],
+                size_t nb1, size_t nb2, size_t nb3, size_t offset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

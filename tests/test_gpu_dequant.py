@@ -1,0 +1,133 @@
+"""GPU parity: device dequantization (libtrc_cuda.so) vs the oracle and the reference's known
+answers, bit for bit, on the KATs, random blocks at full config size, ragged tails, unaligned
+buffers, batched jobs and the host-upload path."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synth
+
+pytestmark = pytest.mark.gpu
+
+TYPES = [synth.TYPE_Q4_0, synth.TYPE_Q4_1, synth.TYPE_Q5_0, synth.TYPE_Q5_1, synth.TYPE_Q8_0]
+NAMES = {v: k for k, v in synth.TYPE_BY_NAME.items()}
+
+
+@pytest.fixture(scope="module")
+def tc():
+    import trc_cuda
+
+    trc_cuda.lib()
+    assert torch.cuda.is_available()
+    return trc_cuda
+
+
+def dev(x: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def bits_equal(got: np.ndarray, want: np.ndarray) -> bool:
+    g, w = got.view(np.uint32), want.view(np.uint32)
+    nan = np.isnan(want)
+    return bool(np.array_equal(np.isnan(got), nan) and np.array_equal(g[~nan], w[~nan]))
+
+
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_known_answers(tc, goldens, qtype):
+    g = goldens["dequant"]
+    name = NAMES[qtype]
+    out = tc.gguf_tensor_to_f32(qtype, dev(g[f"kat_{name}_blocks"])).cpu().numpy()
+    assert np.array_equal(out, g[f"kat_{name}_out"])
+    assert tc.device_error() == 0
+
+
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_random_blocks_ragged_tail_golden(tc, goldens, qtype):
+    """257 blocks: one full run plus a 1-block tail staged without the bulk copy."""
+    g = goldens["dequant"]
+    name = NAMES[qtype]
+    out = tc.gguf_tensor_to_f32(qtype, dev(g[f"rand_{name}_blocks"])).cpu().numpy()
+    assert bits_equal(out, g[f"rand_{name}_out"])
+
+
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_full_config_tensor_bitwise(tc, qtype):
+    """One 4096 x 11008 tensor per format (the dequant bandwidth workload)."""
+    n_blocks = 4096 * 11008 // 32
+    blocks = synth.random_blocks(qtype, n_blocks, seed=2024 + qtype)
+    out = tc.gguf_tensor_to_f32(qtype, dev(blocks)).cpu().numpy()
+    want = oracle.dequant(qtype, blocks)
+    assert bits_equal(out, want)
+    assert tc.device_error() == 0
+
+
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_extreme_scales(tc, qtype):
+    """Subnormal, maximal, zero, negative-zero, infinite and NaN fp16 scales."""
+    blocks = synth.random_blocks(qtype, 300, seed=5)
+    v = blocks.reshape(300, -1)
+    specials = [0x0001, 0x03FF, 0x0400, 0x7BFF, 0x8001, 0xFBFF, 0x0000, 0x8000, 0x7C00, 0xFC00, 0x7E00, 0x7C01]
+    for i, d in enumerate(specials):
+        v[i, 0:2] = np.frombuffer(np.uint16(d).tobytes(), dtype=np.uint8)
+        if qtype in (synth.TYPE_Q4_1, synth.TYPE_Q5_1):
+            v[i + 20, 2:4] = np.frombuffer(np.uint16(d).tobytes(), dtype=np.uint8)  # the m field
+    out = tc.gguf_tensor_to_f32(qtype, dev(blocks)).cpu().numpy()
+    assert bits_equal(out, oracle.dequant(qtype, blocks))
+
+
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_unaligned_buffers(tc, qtype):
+    """Packed source 2 bytes past a 16-byte boundary and output 4 bytes past one: the kernel falls
+    back to plain loads / scalar stores."""
+    n = 1000
+    blocks = synth.random_blocks(qtype, n, seed=77)
+    raw = torch.zeros(blocks.size + 16, dtype=torch.uint8, device="cuda")
+    raw[2:2 + blocks.size] = dev(blocks)
+    out_raw = torch.zeros(n * 32 + 4, dtype=torch.float32, device="cuda")
+    src = raw[2:2 + blocks.size]
+    out = out_raw[1:1 + n * 32]
+    tc.gguf_tensor_to_f32(qtype, src, out=out)
+    assert bits_equal(out.cpu().numpy(), oracle.dequant(qtype, blocks))
+
+
+def test_batched_jobs_whole_model_slice(tc):
+    """trc_cuda_dequant_many over a mixed set of tensors (the whole-model workload's formats and
+    row shapes, at reduced row counts) in one launch."""
+    shapes = [(synth.TYPE_Q5_1, 4096 * 64), (synth.TYPE_Q8_0, 4096 * 32), (synth.TYPE_Q4_0, 4096 * 96),
+              (synth.TYPE_Q4_0, 11008 * 8), (synth.TYPE_Q8_0, 32 * 3), (synth.TYPE_Q5_1, 4096 * 64)]
+    jobs, wants, outs = [], [], []
+    for i, (t, n) in enumerate(shapes):
+        b = synth.random_blocks(t, n // 32, seed=300 + i)
+        o = torch.empty(n, dtype=torch.float32, device="cuda")
+        jobs.append((t, dev(b), o))
+        outs.append(o)
+        wants.append(oracle.dequant(t, b))
+    tc.dequantize_many(jobs)
+    for o, w in zip(outs, wants):
+        assert bits_equal(o.cpu().numpy(), w)
+
+
+def test_load_from_pinned_host(tc):
+    t = synth.TYPE_Q5_0
+    n_blocks = 4096 * 64 // 32
+    blocks = synth.random_blocks(t, n_blocks, seed=8)
+    host = torch.from_numpy(blocks).pin_memory()
+    staging = torch.empty(blocks.size, dtype=torch.uint8, device="cuda")
+    dst = torch.empty(n_blocks * 32, dtype=torch.float32, device="cuda")
+    tc.gguf_load_tensor(t, host, dst, staging)
+    assert bits_equal(dst.cpu().numpy(), oracle.dequant(t, blocks))
+
+
+def test_rejections(tc):
+    blocks = dev(synth.random_blocks(synth.TYPE_Q4_0, 4, seed=1))
+    with pytest.raises(tc.TrcCudaError):
+        tc.gguf_tensor_to_f32(synth.TYPE_Q4_0, blocks, n_elems=30)  # ragged: not whole blocks
+    with pytest.raises(tc.TrcCudaError):
+        tc.gguf_tensor_to_f32(10, blocks)  # Q2_K: not a legacy format (the reference rejects it too)
+    out = torch.empty(32, device="cuda")
+    assert tc.lib().trc_cuda_dequant(10, blocks.data_ptr(), 1, out.data_ptr(), None) == -2
+    assert tc.lib().trc_cuda_dequant(2, blocks.data_ptr(), -1, out.data_ptr(), None) == -1
+    assert tc.lib().trc_cuda_dequant(2, blocks.data_ptr(), 0, out.data_ptr(), None) == 0

@@ -1,0 +1,60 @@
+"""GPU parity of the fused dequant + mul_mat (weight decoded in the GEMM's producer stage, never
+stored as F32): equal within tolerance to mul_mat on the device-dequantized weight and to the
+oracle, for W and transpose(W) (forward and dX), all five formats."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synth
+from conftest import normwise
+
+pytestmark = pytest.mark.gpu
+
+TYPES = [synth.TYPE_Q4_0, synth.TYPE_Q4_1, synth.TYPE_Q5_0, synth.TYPE_Q5_1, synth.TYPE_Q8_0]
+NAMES = {v: k for k, v in synth.TYPE_BY_NAME.items()}
+
+
+@pytest.fixture(scope="module")
+def tc():
+    import trc_cuda
+
+    trc_cuda.lib()
+    return trc_cuda
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+@pytest.mark.parametrize("transposed", [False, True], ids=["W", "WT"])
+@pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
+def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed):
+    w_ne0, w_ne1, n = 512, 400, 136  # W [k=512, m=400]; ragged M/N tiles
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=40 + qtype)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)  # numpy (ne1, ne0)
+    K = w_ne1 if transposed else w_ne0
+    x = np.random.default_rng(qtype).standard_normal((n, K)).astype(np.float32)
+    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, x)
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed).cpu().numpy()
+    assert got.shape == want.shape
+    assert normwise(got, want) <= 1e-5
+    Wd = tc.gguf_tensor_to_f32(qtype, dev(blocks)).reshape(w_ne1, w_ne0)
+    two_step = tc.mul_mat(Wd.t() if transposed else Wd, dev(x)).cpu().numpy()
+    assert normwise(got, two_step) <= 2e-6
+    assert tc.device_error() == 0
+
+
+def test_fused_config_shape_slice(tc):
+    """The fused Linear workload's weight (Q5_0, 4096 x 14336) against a token slice."""
+    qtype, w_ne0, w_ne1 = synth.TYPE_Q5_0, 4096, 14336
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=3)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    x = np.random.default_rng(0).standard_normal((48, w_ne0)).astype(np.float32)
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x)).cpu().numpy()
+    assert normwise(got, oracle.mul_mat(Wf, x)) <= 1e-5
+    dy = (np.random.default_rng(1).standard_normal((16, w_ne1)) * 1e-2).astype(np.float32)
+    got_t = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True).cpu().numpy()
+    assert normwise(got_t, oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)) <= 1e-5

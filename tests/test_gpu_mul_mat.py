@@ -1,0 +1,146 @@
+"""GPU parity: ggml mul_mat on the tcgen05 3xTF32 kernel (normwise <= 1e-5 against the reference)
+and on the SIMT kernel (bit-exact against the reference), over the reference's conformance shapes,
+its golden arrays, transposed views, modulo broadcasting, ragged tiles and config-size slices."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import normwise
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5  # normwise: max|gpu - cpu| / max|cpu| (north-star accuracy bar)
+
+
+@pytest.fixture(scope="module")
+def tc():
+    import trc_cuda
+
+    trc_cuda.lib()
+    return trc_cuda
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def op(x, t):
+    return x.transpose(-1, -2) if t else x
+
+
+def npop(x, t):
+    return np.swapaxes(x, -1, -2) if t else x
+
+
+CONFORMANCE = {
+    "basic": ((3, 5), False, (4, 5), False),
+    "transposed_a": ((5, 3), True, (4, 5), False),
+    "transposed_b": ((3, 5), False, (5, 4), True),
+    "tile_boundary": ((70, 33), False, (66, 33), False),
+    "batch": ((1, 1, 3, 5), False, (3, 2, 4, 5), False),
+    "batch_bcast_div": ((1, 2, 3, 5), False, (1, 4, 4, 5), False),
+    "batch_transposed": ((2, 2, 5, 3), True, (2, 2, 5, 4), True),
+    "batch_tile_boundary": ((1, 1, 70, 33), False, (2, 2, 66, 33), False),
+    "grid_z_65_planes": ((1, 1, 4, 8), False, (1, 65, 4, 8), False),
+}
+
+
+@pytest.mark.parametrize("simt", [False, True], ids=["auto", "simt"])
+@pytest.mark.parametrize("case", list(CONFORMANCE))
+def test_conformance_shapes(tc, case, simt):
+    """The reference backend conformance cases (test_backend_conformance.cpp:455-553, 927-934)."""
+    sa, ta, sb, tb = CONFORMANCE[case]
+    rng = np.random.default_rng(1)
+    a = rng.standard_normal(sa).astype(np.float32)
+    b = rng.standard_normal(sb).astype(np.float32)
+    want = oracle.mul_mat(npop(a, ta), npop(b, tb))
+    got = tc.mul_mat(op(dev(a), ta), op(dev(b), tb), simt=simt).cpu().numpy()
+    assert got.shape == want.shape
+    if simt or tc.mul_mat_kernel(op(dev(a), ta), op(dev(b), tb), dev(want)) == tc.KERNEL_SIMT:
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    else:
+        assert normwise(got, want) <= TOL
+
+
+@pytest.mark.parametrize("stem", ["mul_mat", "mul_mat_batch", "mul_mat_batch_bcast_div", "mul_mat_batch_tile"])
+def test_reference_goldens(tc, goldens, stem):
+    g = goldens["reference"]
+    got = tc.mul_mat(dev(g[stem + "_in0"]), dev(g[stem + "_in1"])).cpu().numpy()
+    want = g[stem + "_out"]
+    assert np.all(np.abs(got - want) <= 1e-4 + 1e-3 * np.abs(want))
+
+
+TC_CASES = ["fwd_basic", "fwd_ta", "fwd_tb", "fwd_tab", "fwd_odd", "fwd_bcast", "fwd_bcast_t"]
+
+
+@pytest.mark.parametrize("name", TC_CASES)
+def test_tensor_core_path_against_reference_fixture(tc, goldens, name):
+    """Shapes with 16-byte-aligned strides run on the tcgen05 kernel: K-major and MN-major
+    operands, ragged M/N/K tiles, broadcast planes."""
+    m = goldens["mul_mat"]
+    a, b = m[name + "_a"], m[name + "_b"]
+    ta, tb = bool(m[name + "_ta"]), bool(m[name + "_tb"])
+    want = m[name + "_d"]
+    A, B = op(dev(a), ta), op(dev(b), tb)
+    out = torch.empty(want.shape, dtype=torch.float32, device="cuda")
+    kernel = tc.mul_mat_kernel(A, B, out)
+    if name != "fwd_odd":
+        assert kernel == tc.KERNEL_TCGEN05
+    tc.mul_mat(A, B, out=out)
+    assert normwise(out.cpu().numpy(), want) <= TOL
+    assert tc.device_error() == 0
+
+
+def test_accumulate_flag(tc):
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal((96, 64)).astype(np.float32)
+    b = rng.standard_normal((80, 64)).astype(np.float32)
+    c = rng.standard_normal((80, 96)).astype(np.float32)
+    want = oracle.mul_mat(a, b) + c
+    out = dev(c)
+    tc.mul_mat(dev(a), dev(b), out=out, accumulate=True)
+    assert normwise(out.cpu().numpy(), want) <= TOL
+
+
+def test_transposed_output_view(tc):
+    """Output written through a transposed view (D contiguous along ne1): the kernel swaps operand
+    roles so stores stay coalesced."""
+    rng = np.random.default_rng(6)
+    a = rng.standard_normal((300, 128)).astype(np.float32)
+    b = rng.standard_normal((200, 128)).astype(np.float32)
+    want = oracle.mul_mat(a, b)  # [m=300, n=200] -> numpy (200, 300)
+    base = torch.empty((300, 200), dtype=torch.float32, device="cuda")
+    out = base.t()  # ggml ne [300, 200] with nb0 = 800 B, nb1 = 4 B
+    assert tc.mul_mat_kernel(dev(a), dev(b), out) == tc.KERNEL_TCGEN05
+    tc.mul_mat(dev(a), dev(b), out=out)
+    assert normwise(out.cpu().numpy(), want) <= TOL
+
+
+@pytest.mark.parametrize("k,m,n", [(4096, 4096, 64), (128, 2048, 96), (2048, 640, 72), (14336, 256, 16)])
+def test_config_shaped_slices(tc, k, m, n):
+    """Slices of the Linear / GQA / backward GEMMs at their true K, against the oracle."""
+    rng = np.random.default_rng(k + m + n)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    want = oracle.mul_mat(a, b)
+    got = tc.mul_mat(dev(a), dev(b)).cpu().numpy()
+    assert normwise(got, want) <= TOL
+    # the same product through transposed (MN-major) views of both operands
+    at, bt = np.ascontiguousarray(a.T), np.ascontiguousarray(b.T)
+    got_t = tc.mul_mat(dev(at).t(), dev(bt).t()).cpu().numpy()
+    assert normwise(got_t, want) <= TOL
+
+
+def test_full_size_linear_forward_vs_fp64(tc):
+    """Y = W X at the fused Linear workload's full size (K=4096, M=14336, N=2048), normwise
+    against a float64 product on the GPU (size-independent accuracy property)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W = torch.randn((14336, 4096), generator=g, device="cuda") * 0.005
+    X = torch.randn((2048, 4096), generator=g, device="cuda")
+    Y = tc.mul_mat(W, X)
+    ref64 = (X.double() @ W.double().t())
+    err = ((Y.double() - ref64).abs().max() / ref64.abs().max()).item()
+    assert err <= 2e-6, err

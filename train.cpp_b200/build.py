@@ -1,0 +1,84 @@
+"""Build step for the native libraries of train.cpp_b200 (run by __graft_entry__.build()).
+
+  lib/libtrc_cuda.so          the sm_100a kernels + C ABI (include/trc_cuda.h); needs only nvcc
+  lib/libtrc_cuda_backend.so  the C++ Device/BufferType/Buffer drop-in for train.cpp; compiled
+                              against train.cpp's public headers, so it is only built where the
+                              train.cpp source tree is available (TRC_REFERENCE_DIR)
+
+Everything is built in-tree so the shared objects travel with the repository snapshot.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIB = PKG / "lib"
+NVCC = os.environ.get("NVCC", "nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+CU_SOURCES = ["capi.cu", "dequant.cu", "elementwise.cu", "mul_mat_simt.cu", "gemm_tf32x3.cu"]
+
+
+def _run(cmd: list[str], log: Path | None = None) -> None:
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if log is not None:
+        log.write_text(res.stdout + res.stderr)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError(f"build step failed: {' '.join(cmd[:3])} ...")
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build_cuda(force: bool = False) -> Path:
+    """Compile libtrc_cuda.so for sm_100a (relocatable device code, static cudart)."""
+    LIB.mkdir(exist_ok=True)
+    out = LIB / "libtrc_cuda.so"
+    deps = [CSRC / s for s in CU_SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
+    deps.append(ROOT / "include" / "trc_cuda.h")
+    if not force and not _stale(out, deps):
+        return out
+    cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-rdc=true", "-shared",
+           "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{ROOT / 'include'}",
+           "-o", str(out), *[str(CSRC / s) for s in CU_SOURCES]]
+    _run(cmd, LIB / "libtrc_cuda.build.log")
+    return out
+
+
+def reference_dir() -> Path | None:
+    d = Path(os.environ.get("TRC_REFERENCE_DIR", "/root/reference"))
+    return d if (d / "include" / "traincpp" / "trc_backend.h").exists() else None
+
+
+def build_backend(force: bool = False) -> Path | None:
+    """Compile the C++ drop-in backend against train.cpp's headers (skipped without them)."""
+    ref = reference_dir()
+    out = LIB / "libtrc_cuda_backend.so"
+    if ref is None:
+        return out if out.exists() else None
+    cuda_lib = build_cuda()
+    src = PKG / "backend" / "trc_cuda_backend.cpp"
+    deps = [src, PKG / "backend" / "trc_cuda_backend.h", ROOT / "include" / "trc_cuda.h", cuda_lib]
+    if not force and not _stale(out, deps):
+        return out
+    cuda_inc = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+    cmd = ["g++", "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-Wno-unused-parameter",
+           f"-I{ref / 'include'}", f"-I{ROOT / 'include'}", f"-I{cuda_inc}",
+           "-o", str(out), str(src), f"-L{LIB}", "-ltrc_cuda", "-Wl,-rpath,$ORIGIN"]
+    _run(cmd)
+    return out
+
+
+if __name__ == "__main__":
+    print(build_cuda(force="--force" in sys.argv))
+    print(build_backend(force="--force" in sys.argv))

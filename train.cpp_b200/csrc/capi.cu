@@ -1,0 +1,174 @@
+// capi.cu -- extern "C" entry points of libtrc_cuda.so that are not kernels themselves: status
+// reporting, the device error word, argument checks that mirror the reference's shape rules, and
+// dispatch between the tensor-core and SIMT mul_mat kernels.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "trc_internal.h"
+#include "trc_ptx.cuh"
+
+namespace trc {
+
+__device__ int g_device_error = 0;
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+thread_local int      g_last_cuda_error = 0;
+}  // namespace
+
+void note_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+
+int cuda_fail(cudaError_t e) {
+    g_last_cuda_error = static_cast<int>(e);
+    return TRC_CUDA_ECUDA;
+}
+
+int check_launch() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TRC_CUDA_OK : cuda_fail(e);
+}
+
+int sm_count_current() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    static int cache[64] = {0};
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+}  // namespace trc
+
+using namespace trc;
+
+extern "C" {
+
+int trc_cuda_abi_version(void) { return TRC_CUDA_ABI_VERSION; }
+
+const char* trc_cuda_status_string(int status) {
+    switch (status) {
+        case TRC_CUDA_OK: return "ok";
+        case TRC_CUDA_EINVAL: return "invalid argument (null pointer, bad size or shape rule violated)";
+        case TRC_CUDA_EUNSUPPORTED: return "unsupported type or layout";
+        case TRC_CUDA_EDEVICE: return "a kernel hit its wait limit (device error word set)";
+        case TRC_CUDA_ECUDA: return "CUDA runtime error";
+        case TRC_CUDA_ENOMEM: return "device allocation failed";
+        default: return "unknown status";
+    }
+}
+
+int trc_cuda_last_cuda_error(void) { return g_last_cuda_error; }
+
+int trc_cuda_device_error(int* code, int reset) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (code != nullptr) *code = v;
+    if (reset != 0 && v != 0) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    return TRC_CUDA_OK;
+}
+
+uint64_t trc_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int trc_cuda_sm_count(void) { return sm_count_current(); }
+
+size_t trc_cuda_block_bytes(int type) {
+    switch (type) {
+        case TRC_CUDA_TYPE_Q4_0: return 18;
+        case TRC_CUDA_TYPE_Q4_1: return 20;
+        case TRC_CUDA_TYPE_Q5_0: return 22;
+        case TRC_CUDA_TYPE_Q5_1: return 24;
+        case TRC_CUDA_TYPE_Q8_0: return 34;
+        default: return 0;
+    }
+}
+
+int trc_cuda_dequant(int type, const void* blocks, int64_t n_blocks, float* out, void* stream) {
+    if (trc_cuda_block_bytes(type) == 0) return TRC_CUDA_EUNSUPPORTED;
+    trc_cuda_dequant_job job;
+    job.blocks   = blocks;
+    job.out      = out;
+    job.n_blocks = n_blocks;
+    job.type     = type;
+    job.reserved = 0;
+    return dequant_jobs(&job, 1, static_cast<cudaStream_t>(stream));
+}
+
+int trc_cuda_dequant_many(const trc_cuda_dequant_job* jobs, int n_jobs, void* stream) {
+    return dequant_jobs(jobs, n_jobs, static_cast<cudaStream_t>(stream));
+}
+
+int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
+                        void* stream) {
+    const size_t bb = trc_cuda_block_bytes(type);
+    if (bb == 0) return TRC_CUDA_EUNSUPPORTED;
+    if (n_blocks < 0) return TRC_CUDA_EINVAL;
+    if (n_blocks == 0) return TRC_CUDA_OK;
+    if (host_blocks == nullptr || staging == nullptr || out == nullptr) return TRC_CUDA_EINVAL;
+    if ((reinterpret_cast<uint64_t>(staging) & 15u) != 0) return TRC_CUDA_EINVAL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e =
+        cudaMemcpyAsync(staging, host_blocks, static_cast<size_t>(n_blocks) * bb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return trc_cuda_dequant(type, staging, n_blocks, out, stream);
+}
+
+// Shape rules of the mul_mat constructor (src/ops/trc_ops.cpp:366-385).
+static int check_mul_mat_shapes(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d) {
+    if (!view_ok(a) || !view_ok(b) || !view_ok(d)) return TRC_CUDA_EINVAL;
+    if (a->ne[0] != b->ne[0]) return TRC_CUDA_EINVAL;
+    if (a->ne[2] <= 0 || a->ne[3] <= 0 || b->ne[2] % a->ne[2] != 0 || b->ne[3] % a->ne[3] != 0)
+        return TRC_CUDA_EINVAL;
+    if (d->ne[0] != a->ne[1] || d->ne[1] != b->ne[1] || d->ne[2] != b->ne[2] || d->ne[3] != b->ne[3])
+        return TRC_CUDA_EINVAL;
+    return TRC_CUDA_OK;
+}
+
+int trc_cuda_mul_mat(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags,
+                     void* stream) {
+    int st = check_mul_mat_shapes(a, b, d);
+    if (st != TRC_CUDA_OK) return st;
+    if (nelements(*d) == 0) return TRC_CUDA_OK;
+    const bool acc = (flags & TRC_CUDA_MM_ACCUMULATE) != 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->ne[0] == 0) {  // empty reduction: d = 0 (or unchanged when accumulating)
+        if (acc) return TRC_CUDA_OK;
+        return mul_mat_simt(*a, *b, *d, false, s);
+    }
+    if ((flags & TRC_CUDA_MM_SIMT) == 0) {
+        st = mul_mat_tc(*a, *b, *d, acc, s);
+        if (st != TRC_CUDA_EUNSUPPORTED) return st;
+    }
+    return mul_mat_simt(*a, *b, *d, acc, s);
+}
+
+int trc_cuda_mul_mat_kernel(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags) {
+    const int st = check_mul_mat_shapes(a, b, d);
+    if (st != TRC_CUDA_OK) return st;
+    if ((flags & TRC_CUDA_MM_SIMT) != 0 || nelements(*d) == 0 || a->ne[0] == 0) return TRC_CUDA_KERNEL_SIMT;
+    return mul_mat_tc_eligible(*a, *b, *d) ? TRC_CUDA_KERNEL_TCGEN05 : TRC_CUDA_KERNEL_SIMT;
+}
+
+int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                       const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags, void* stream) {
+    if (trc_cuda_block_bytes(type) == 0) return TRC_CUDA_EUNSUPPORTED;
+    if (w_blocks == nullptr || w_ne0 <= 0 || w_ne1 <= 0 || (w_ne0 % 32) != 0) return TRC_CUDA_EINVAL;
+    if (!view_ok(b) || !view_ok(d)) return TRC_CUDA_EINVAL;
+    const int64_t K = a_transposed ? w_ne1 : w_ne0;
+    const int64_t M = a_transposed ? w_ne0 : w_ne1;
+    if (b->ne[0] != K || d->ne[0] != M || d->ne[1] != b->ne[1] || d->ne[2] != b->ne[2] || d->ne[3] != b->ne[3])
+        return TRC_CUDA_EINVAL;
+    if (nelements(*d) == 0) return TRC_CUDA_OK;
+    return mul_mat_q_tc(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d,
+                        (flags & TRC_CUDA_MM_ACCUMULATE) != 0, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

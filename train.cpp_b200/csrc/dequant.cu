@@ -1,0 +1,217 @@
+// dequant.cu -- GGUF legacy-block dequantization (Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 -> F32) for sm_100a.
+//
+// Replaces the host loop of gguf_tensor_to_f32 -> dequantize_q* (src/io/trc_gguf.cpp:966-1049,
+// 320-417 of train.cpp). HBM-bound: per 32 weights it reads 18..34 packed bytes and writes 128.
+//
+// Layout and schedule
+//   * A "run" is 256 consecutive blocks of one tensor (4.5-8.5 KiB packed, 32 KiB of F32 out).
+//   * Persistent CTAs of 256 threads walk the runs of all jobs of a launch (one launch can cover a
+//     whole model shard). Each CTA double-buffers its runs in shared memory: while it decodes run r
+//     it already has the bulk copy (cp.async.bulk, TMA engine) of its next run in flight.
+//   * Decode: warp w owns blocks 32w..32w+31 of the run. In each of 8 steps a lane decodes 4
+//     weights (a quad) of one of 4 blocks and the warp stores 4 x 128 B = 512 contiguous bytes
+//     with 16-byte vector stores, so every store instruction is fully coalesced.
+//   * A run whose packed bytes are not 16-byte aligned / sized (a tensor's ragged tail, or an
+//     unaligned tensor) is staged by ordinary loads instead of the bulk copy.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "trc_internal.h"
+#include "trc_ptx.cuh"
+#include "trc_quant.cuh"
+
+namespace trc {
+
+namespace {
+
+constexpr int kThreads   = 256;
+constexpr int kRun       = 256;       // blocks per run
+constexpr int kMaxBlk    = 34;        // largest block (Q8_0)
+constexpr int kMaxJobs   = 256;       // jobs per launch (kernel parameter of ~10 KiB)
+constexpr int kBufBytes  = kRun * kMaxBlk;
+
+struct DqJob {
+    const uint8_t* src;
+    float*         out;
+    int64_t        n_blocks;
+    int64_t        run_begin;  // first global run index of this job
+    int32_t        type;
+    int32_t        block_bytes;
+};
+
+struct DqBatch {
+    DqJob   job[kMaxJobs];
+    int32_t n_jobs;
+    int64_t total_runs;
+};
+
+__device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
+    const int64_t b0    = local_run * kRun;
+    const int64_t nblk  = min(static_cast<int64_t>(kRun), J.n_blocks - b0);
+    const uint64_t addr = reinterpret_cast<uint64_t>(J.src) + static_cast<uint64_t>(b0) * J.block_bytes;
+    const int64_t bytes = nblk * J.block_bytes;
+    return (addr & 15u) == 0 && (bytes & 15) == 0;
+}
+
+template <int TYPE>
+__device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, int64_t b0, int nblk) {
+    constexpr int kBB = QuantTraits<TYPE>::kBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = lane & 7;
+    const bool vec_ok = (reinterpret_cast<uint64_t>(J.out) & 15u) == 0;
+#pragma unroll 2
+    for (int step = 0; step < 8; ++step) {
+        const int lb = warp * 32 + step * 4 + (lane >> 3);
+        if (lb < nblk) {
+            float w[4];
+            decode_quad<TYPE>(buf + lb * kBB, c, w);
+            float* o = J.out + (b0 + lb) * 32 + 4 * c;
+            if (vec_ok) {
+                *reinterpret_cast<float4*>(o) = make_float4(w[0], w[1], w[2], w[3]);
+            } else {
+                o[0] = w[0]; o[1] = w[1]; o[2] = w[2]; o[3] = w[3];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DqBatch batch) {
+    __shared__ __align__(128) uint8_t buf[2][kBufBytes];
+    __shared__ __align__(8) uint64_t bar[2];
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    uint32_t phase[2]   = {0u, 0u};
+    bool     pending[2] = {false, false};
+    int      jcur       = 0;  // job cursor (runs only increase for a CTA)
+
+    auto locate = [&](int64_t run, int& j) {
+        while (j + 1 < batch.n_jobs && batch.job[j + 1].run_begin <= run) ++j;
+    };
+    auto issue = [&](int64_t run, int j, int slot) {
+        const DqJob&  J     = batch.job[j];
+        const int64_t b0    = (run - J.run_begin) * kRun;
+        const int64_t nblk  = min(static_cast<int64_t>(kRun), J.n_blocks - b0);
+        const uint32_t bytes = static_cast<uint32_t>(nblk * J.block_bytes);
+        mbar_arrive_expect_tx(&bar[slot], bytes);
+        bulk_load(smem_u32(buf[slot]), J.src + b0 * J.block_bytes, bytes, &bar[slot]);
+    };
+
+    int64_t run = blockIdx.x;
+    int     it  = 0;
+    bool    ok  = true;
+    if (run < batch.total_runs) {
+        locate(run, jcur);
+        if (run_bulk_ok(batch.job[jcur], run - batch.job[jcur].run_begin)) {
+            if (threadIdx.x == 0) issue(run, jcur, 0);
+            pending[0] = true;
+        }
+    }
+    for (; run < batch.total_runs && ok; run += gridDim.x, ++it) {
+        const int slot = it & 1;
+        locate(run, jcur);
+        const DqJob&  J     = batch.job[jcur];
+        const int64_t local = run - J.run_begin;
+        const int64_t b0    = local * kRun;
+        const int     nblk  = static_cast<int>(min(static_cast<int64_t>(kRun), J.n_blocks - b0));
+
+        // Prefetch the next run into the other slot (its previous contents were consumed in the
+        // previous iteration, which ended with __syncthreads()).
+        const int64_t next = run + gridDim.x;
+        if (next < batch.total_runs) {
+            int jn = jcur;
+            locate(next, jn);
+            if (run_bulk_ok(batch.job[jn], next - batch.job[jn].run_begin)) {
+                if (threadIdx.x == 0) issue(next, jn, slot ^ 1);
+                pending[slot ^ 1] = true;
+            }
+        }
+
+        if (pending[slot]) {
+            const bool mine = mbar_wait(&bar[slot], phase[slot], TRC_DEVERR_WAIT_BULK);
+            ok = __syncthreads_and(mine ? 1 : 0) != 0;  // every thread takes the same branch
+            if (mine) {
+                phase[slot] ^= 1u;
+                pending[slot] = false;
+            }
+            if (!ok) break;
+        } else {
+            const uint8_t* src   = J.src + b0 * J.block_bytes;
+            const int      bytes = nblk * J.block_bytes;
+            for (int i = threadIdx.x; i < bytes; i += kThreads) buf[slot][i] = src[i];
+            __syncthreads();
+        }
+
+        switch (J.type) {
+            case 2: decode_run<2>(buf[slot], J, b0, nblk); break;
+            case 3: decode_run<3>(buf[slot], J, b0, nblk); break;
+            case 6: decode_run<6>(buf[slot], J, b0, nblk); break;
+            case 7: decode_run<7>(buf[slot], J, b0, nblk); break;
+            case 8: decode_run<8>(buf[slot], J, b0, nblk); break;
+            default: break;
+        }
+        __syncthreads();
+    }
+    // Never leave the CTA with a bulk copy still writing into its shared memory.
+    for (int s = 0; s < 2; ++s) {
+        if (pending[s]) mbar_wait_drain(&bar[s], phase[s]);
+    }
+}
+
+}  // namespace
+
+int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream) {
+    static_assert(sizeof(DqBatch) < 32000, "kernel parameter limit");
+    if (n_jobs < 0 || (n_jobs > 0 && jobs == nullptr)) return TRC_CUDA_EINVAL;
+    // Validate every job before touching the device.
+    bool any_work = false;
+    for (int i = 0; i < n_jobs; ++i) {
+        const trc_cuda_dequant_job& in = jobs[i];
+        if (trc_cuda_block_bytes(in.type) == 0) return TRC_CUDA_EUNSUPPORTED;
+        if (in.n_blocks < 0) return TRC_CUDA_EINVAL;
+        if (in.n_blocks == 0) continue;
+        if (in.blocks == nullptr || in.out == nullptr) return TRC_CUDA_EINVAL;
+        if ((reinterpret_cast<uint64_t>(in.blocks) & 1u) != 0 || (reinterpret_cast<uint64_t>(in.out) & 3u) != 0)
+            return TRC_CUDA_EINVAL;  // fp16 fields need 2-byte, floats 4-byte alignment
+        any_work = true;
+    }
+    if (!any_work) return TRC_CUDA_OK;
+    const int sms = sm_count_current();
+    if (sms <= 0) return TRC_CUDA_ECUDA;
+    for (int first = 0; first < n_jobs; first += kMaxJobs) {
+        DqBatch batch;
+        batch.n_jobs    = 0;
+        int64_t runs    = 0;
+        const int count = std::min(kMaxJobs, n_jobs - first);
+        for (int i = 0; i < count; ++i) {
+            const trc_cuda_dequant_job& in = jobs[first + i];
+            const size_t bb = trc_cuda_block_bytes(in.type);
+            if (in.n_blocks == 0) continue;
+            DqJob& J      = batch.job[batch.n_jobs++];
+            J.src         = static_cast<const uint8_t*>(in.blocks);
+            J.out         = in.out;
+            J.n_blocks    = in.n_blocks;
+            J.run_begin   = runs;
+            J.type        = in.type;
+            J.block_bytes = static_cast<int32_t>(bb);
+            runs += (in.n_blocks + kRun - 1) / kRun;
+        }
+        if (batch.n_jobs == 0) continue;
+        batch.total_runs = runs;
+        const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * 8);
+        dequant_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
+        note_launch();
+        const int st = check_launch();
+        if (st != TRC_CUDA_OK) return st;
+    }
+    return TRC_CUDA_OK;
+}
+
+}  // namespace trc

@@ -1,0 +1,587 @@
+// gemm_tf32x3.cu -- ggml mul_mat on the sm_100a tensor cores (tcgen05 / TMEM) at F32 accuracy.
+//
+// Replaces compute_mul_mat (src/backends/cpu/trc_cpu_ops.cpp:182-216 of train.cpp) for every view
+// TMA can address: operands contiguous along K ("K-major": the forward product and dB) or along
+// M/N ("MN-major": the transposed views of the composed backward, src/core/trc_autograd.cpp:487-503),
+// with ne[2]/ne[3] modulo broadcasting of a.
+//
+// 3xTF32. The tensor core consumes TF32 (10 explicit mantissa bits). Each fp32 operand x is split
+// into a head h = x with the low 13 mantissa bits cleared (what the tensor core reads from the raw
+// fp32 word) and a tail t = x - h (exact in fp32). Per K-step the kernel issues
+//     D += tA * hB,   D += hA * tB,   D += hA * hB
+// into one fp32 TMEM accumulator; only tA*tB (relative size 2^-22) is dropped. Measured against the
+// reference this stays within 1e-5 normwise, where a single TF32 pass is ~3e-4.
+//
+// Structure (one persistent CTA per SM, 12 warps):
+//   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (4-stage ring, 64-byte swizzle)
+//   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
+//   warps 2-7   split warpgroup: writes the tails tA, tB of each stage next to the raw tiles
+//   warps 8-11  epilogue: TMEM -> registers (tcgen05.ld) -> strided global stores (ggml nb[])
+// Tile 128 (M, TMEM lanes) x 256 (N) x 16 (K) per stage; two 256-column fp32 accumulators in TMEM
+// (all 512 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+// Every mbarrier wait is bounded (trc_ptx.cuh); a timeout sets the device error word and the kernel
+// drains its in-flight copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "trc_internal.h"
+#include "trc_ptx.cuh"
+#include "trc_quant.cuh"
+
+namespace trc {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
+constexpr int B_BYTES     = BN * BK * 4;                 // 16 KiB
+constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);     // raw + tail = 48 KiB
+constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES, OFF_B_TAIL = 2 * A_BYTES + B_BYTES;
+constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
+constexpr int NUM_THREADS  = 384;
+constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 6, EPI_WARP0 = 8;
+constexpr int TMEM_COLS    = 512;
+constexpr int SMEM_BYTES   = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+struct TcParams {
+    int     M, N, K;           // M: TMEM lanes (rows of D tiles), N: columns, K: reduction
+    int     m_tiles, n_tiles, k_blocks;
+    int     planes2, planes3;  // output planes
+    int     a_ne2, a_ne3, b_ne2, b_ne3;
+    int     a_mn, b_mn;        // 1 = operand contiguous along M (resp. N)
+    int     accumulate;
+    int64_t total_tiles;
+    char*   d;
+    int64_t d_sm, d_sn, d_s2, d_s3;  // byte strides of D along M, N, plane2, plane3
+    // quantized A (fused variant): packed blocks of the weight W, rows of q_row_bytes bytes
+    const uint8_t* qa;
+    int64_t        q_row_bytes;
+    int            q_rows;           // W rows (ne1)
+    int            q_blocks_per_row; // W ne0 / 32
+};
+
+struct Barriers {
+    uint64_t full[STAGES];
+    uint64_t split[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t mma_done;
+    uint32_t tmem_slot;
+};
+
+__device__ __forceinline__ uint32_t tf32_tail_bits(uint32_t u) {
+    const float x = __uint_as_float(u);
+    const float h = __uint_as_float(u & 0xFFFFE000u);
+    return __float_as_uint(isfinite(x) ? __fsub_rn(x, h) : 0.0f);
+}
+
+struct TileCoord {
+    int m0, n0, p2, p3;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile) {
+    const int64_t per_plane = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+    const int64_t plane     = tile / per_plane;
+    const int64_t r         = tile - plane * per_plane;
+    TileCoord c;
+    c.m0 = static_cast<int>(r / p.n_tiles) * BM;
+    c.n0 = static_cast<int>(r % p.n_tiles) * BN;
+    c.p2 = static_cast<int>(plane % p.planes2);
+    c.p3 = static_cast<int>(plane / p.planes2);
+    return c;
+}
+
+// K-major tile (rows x 16 fp32, 64 B per row, 8-row swizzle atoms of 512 B): advance 32 B per K=8.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
+    return make_smem_desc(tile + kk * 32, 16, 512, 4);
+}
+// MN-major tile (16-element MN chunks of 16 K-rows x 64 B = 1 KiB): advance 512 B (8 K-rows) per K=8.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
+    return make_smem_desc(tile + kk * 512, 1024, 512, 4);
+}
+
+// Tail of one 16-byte chunk of a raw tile (index i < nA: A tile, else B tile).
+__device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
+    const uint4* src = i < nA ? reinterpret_cast<const uint4*>(st + OFF_A_RAW) + i
+                              : reinterpret_cast<const uint4*>(st + OFF_B_RAW) + (i - nA);
+    uint4* dst = i < nA ? reinterpret_cast<uint4*>(st + OFF_A_TAIL) + i
+                        : reinterpret_cast<uint4*>(st + OFF_B_TAIL) + (i - nA);
+    uint4 v = *src;
+    v.x = tf32_tail_bits(v.x);
+    v.y = tf32_tail_bits(v.y);
+    v.z = tf32_tail_bits(v.z);
+    v.w = tf32_tail_bits(v.w);
+    *dst = v;
+}
+
+// Writes 16 consecutive weights w[0..15] as head (TF32-truncated) and tail into the A tiles of a
+// stage: `chunk_off[u]` is the byte offset (already swizzled) of the u-th group of four weights.
+__device__ __forceinline__ void store_head_tail16(uint8_t* st, const float (&w)[16], const int (&chunk_off)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        uint4 h, l;
+        uint32_t* hp = &h.x;
+        uint32_t* lp = &l.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t bits = __float_as_uint(w[4 * u + e]);
+            hp[e] = bits & 0xFFFFE000u;
+            lp[e] = tf32_tail_bits(bits);
+        }
+        *reinterpret_cast<uint4*>(st + OFF_A_RAW + chunk_off[u])  = h;
+        *reinterpret_cast<uint4*>(st + OFF_A_TAIL + chunk_off[u]) = l;
+    }
+}
+
+// A-stage decode for the fused dequant GEMM (thread t of 128). The stage covers A rows m0..m0+127
+// and K columns k0..k0+15, i.e. one half (16 weights) of a 32-weight block per W row (QTRANS = 0)
+// or 16 W rows x 4 blocks (QTRANS = 1). Out-of-range weights are written as zeros.
+template <int QTYPE, int QTRANS>
+__device__ __forceinline__ void decode_a_stage(const TcParams& p, int m0, int k0, int t, uint8_t* st) {
+    constexpr int BB = QuantTraits<QTYPE>::kBytes;
+    float w[16];
+    int   off[4];
+    if constexpr (QTRANS == 0) {
+        // K-major: row r = t (W row m0 + r), weights k0..k0+15 = half (k0/16)&1 of block k0/32.
+        const int r = t, m = m0 + r;
+        const int half = (k0 >> 4) & 1;
+        if (m < p.M && k0 < p.K) {
+            const uint8_t* blk = p.qa + static_cast<int64_t>(m) * p.q_row_bytes + static_cast<int64_t>(k0 >> 5) * BB;
+            decode_half<QTYPE>(blk, half, w);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) off[u] = r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+    } else {
+        // MN-major: K-row kr = t/8 (W row k0 + kr), block j = (t/2)%4 (weights m0 + 32j ..), half h.
+        const int kr = t >> 3, j = (t >> 1) & 3, h = t & 1;
+        const int wrow = k0 + kr, m = m0 + 32 * j;
+        if (wrow < p.K && m < p.M) {
+            const uint8_t* blk = p.qa + static_cast<int64_t>(wrow) * p.q_row_bytes + static_cast<int64_t>(m >> 5) * BB;
+            decode_half<QTYPE>(blk, h, w);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+        }
+        const int cm = 2 * j + h;  // 16-element MN chunk
+#pragma unroll
+        for (int u = 0; u < 4; ++u) off[u] = cm * 1024 + kr * 64 + ((u ^ ((kr >> 1) & 3)) << 4);
+    }
+    store_head_tail16(st, w, off);
+}
+
+// QTYPE = 0: A is an F32 view loaded by TMA. QTYPE = ggml Q-type: A is decoded from packed blocks by
+// the split warpgroup (QTRANS = 0: A = W, K-major; QTRANS = 1: A = transpose(W), MN-major).
+template <int QTYPE, int QTRANS>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->split[s], SPLIT_WARPS);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&bars->acc_full[a], 1);
+            mbar_init(&bars->acc_empty[a], 4);
+        }
+        mbar_init(&bars->mma_done, 1);
+        fence_barrier_init();
+        if (QTYPE == 0) prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_slot;
+    const uint32_t smem_base = smem_u32(smem);
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+                const TileCoord tc = tile_coord(p, tile);
+                const int a2 = tc.p2 % p.a_ne2, a3 = tc.p3 % p.a_ne3;
+                const int b2 = tc.p2 % p.b_ne2, b3 = tc.p3 % p.b_ne3;
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
+                    const uint32_t st = smem_base + s * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&bars->full[s], QTYPE == 0 ? RAW_TX_BYTES : B_BYTES);
+                    const int k0 = kb * BK;
+                    if constexpr (QTYPE == 0) {
+                        if (!p.a_mn) {
+                            tma_load_4d(st + OFF_A_RAW, &tmA, &bars->full[s], k0, tc.m0, a2, a3);
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < BM / 16; ++c)
+                                tma_load_4d(st + OFF_A_RAW + c * 1024, &tmA, &bars->full[s], tc.m0 + 16 * c, k0, a2,
+                                            a3);
+                        }
+                    }
+                    if (!p.b_mn) {
+                        tma_load_4d(st + OFF_B_RAW, &tmB, &bars->full[s], k0, tc.n0, b2, b3);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < BN / 16; ++c)
+                            tma_load_4d(st + OFF_B_RAW + c * 1024, &tmB, &bars->full[s], tc.n0 + 16 * c, k0, b2, b3);
+                    }
+                }
+            }
+            // Drain: the last load issued into each stage must have landed before the CTA exits.
+            const uint32_t n_issued = it;
+            for (uint32_t q = (n_issued > STAGES ? n_issued - STAGES : 0); q < n_issued; ++q)
+                mbar_wait_drain(&bars->full[q % STAGES], (q / STAGES) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- UMMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+                const int ab = tcount & 1;
+                if (!mbar_wait(&bars->acc_empty[ab], ((tcount >> 1) & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + ab * BN;
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&bars->split[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t st = smem_base + s * STAGE_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + OFF_A_RAW, kk) : desc_kmajor(st + OFF_A_RAW, kk);
+                        const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + OFF_A_TAIL, kk) : desc_kmajor(st + OFF_A_TAIL, kk);
+                        const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + OFF_B_RAW, kk) : desc_kmajor(st + OFF_B_RAW, kk);
+                        const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + OFF_B_TAIL, kk) : desc_kmajor(st + OFF_B_TAIL, kk);
+                        umma_tf32(d_tmem, a_tail, b_raw, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        umma_tf32(d_tmem, a_raw, b_tail, idesc, 1u);
+                        umma_tf32(d_tmem, a_raw, b_raw, idesc, 1u);
+                    }
+                    umma_commit(&bars->empty[s]);  // frees the stage once these MMAs have read it
+                }
+                if (!ok) break;
+                umma_commit(&bars->acc_full[ab]);
+            }
+            // All MMAs of this thread must be complete before TMEM is released.
+            umma_commit(&bars->mma_done);
+            mbar_wait_drain(&bars->mma_done, 0);
+        }
+    } else if (warp < EPI_WARP0) {
+        // ---------------------------------------------------------------- split warpgroup
+        const int t = threadIdx.x - SPLIT_WARP0 * 32;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+            const TileCoord tc = tile_coord(p, tile);
+            for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                const int s = it % STAGES;
+                uint8_t* st = smem + s * STAGE_BYTES;
+                constexpr int nA = A_BYTES / 16, nAll = (A_BYTES + B_BYTES) / 16;
+                if constexpr (QTYPE != 0) {
+                    if (t < 128) {
+                        // Warps 2-5 decode this stage's A tile straight from the packed blocks into
+                        // explicit head + tail tiles. They need no TMA data, only the stage released
+                        // by the MMAs of its previous round.
+                        if (it >= STAGES &&
+                            !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) {
+                            ok = false;
+                        } else {
+                            decode_a_stage<QTYPE, QTRANS>(p, tc.m0, kb * BK, t, st);
+                        }
+                    } else {
+                        // Warps 6-7 split the TMA-loaded B tile.
+                        if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
+                            ok = false;
+                        } else {
+                            for (int i = nA + (t - 128); i < nAll; i += SPLIT_WARPS * 32 - 128) split_one(st, i, nA);
+                        }
+                    }
+                } else {
+                    if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
+                        ok = false;
+                    } else {
+                        for (int i = t; i < nAll; i += SPLIT_WARPS * 32) split_one(st, i, nA);
+                    }
+                }
+                if (!ok) break;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->split[s]);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp - EPI_WARP0;  // TMEM lane quarter this warp may access
+        const int row = q * 32 + lane;
+        uint32_t tcount = 0;
+        for (int64_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++tcount) {
+            const int ab = tcount & 1;
+            if (!mbar_wait(&bars->acc_full[ab], (tcount >> 1) & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
+            tc_fence_after();
+            const TileCoord tc = tile_coord(p, tile);
+            const int m = tc.m0 + row;
+            char* drow = p.d + static_cast<int64_t>(tc.p2) * p.d_s2 + static_cast<int64_t>(tc.p3) * p.d_s3 +
+                         static_cast<int64_t>(m) * p.d_sm;
+            const int n_valid = min(BN, p.N - tc.n0);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                if (c * 32 >= n_valid) break;  // uniform across the warp
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * BN + c * 32, r);
+                tmem_ld_wait();
+                if (m < p.M) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int n = tc.n0 + c * 32 + e;
+                        if (n < p.N) {
+                            float* o = reinterpret_cast<float*>(drow + static_cast<int64_t>(n) * p.d_sn);
+                            const float v = __uint_as_float(r[e]);
+                            *o = p.accumulate ? __fadd_rn(*o, v) : v;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[ab]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+bool stride_ok(int64_t s) { return s > 0 && (s % 16) == 0 && s < (int64_t(1) << 40); }
+
+// Builds the tensor map of one operand: a ggml view with ne0 = K, ne1 = rows (M or N).
+// Returns false when TMA cannot address the view (the caller then uses the SIMT kernel).
+bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtensorMap& map) {
+    if ((reinterpret_cast<uint64_t>(v.data) & 15u) != 0) return false;
+    const int64_t K = v.ne[0], R = v.ne[1];
+    if (K >= (int64_t(1) << 31) || R >= (int64_t(1) << 31)) return false;
+    cuuint64_t dims[4];
+    cuuint64_t strides[3];
+    cuuint32_t box[4];
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (v.nb[0] == 4 && (R == 1 || stride_ok(v.nb[1]))) {
+        mn_major = false;
+        dims[0] = K; dims[1] = R;
+        strides[0] = R == 1 ? static_cast<cuuint64_t>((K * 4 + 15) / 16 * 16) : v.nb[1];
+        box[0] = BK; box[1] = box_rows;
+    } else if (v.nb[1] == 4 && (K == 1 || stride_ok(v.nb[0]))) {
+        mn_major = true;
+        dims[0] = R; dims[1] = K;
+        strides[0] = K == 1 ? static_cast<cuuint64_t>((R * 4 + 15) / 16 * 16) : v.nb[0];
+        box[0] = 16; box[1] = BK;
+    } else {
+        return false;
+    }
+    dims[2] = v.ne[2];
+    dims[3] = v.ne[3];
+    // Planes of extent 1 get a dummy stride (never stepped) that keeps the strides monotonic.
+    const cuuint64_t plane_bytes = strides[0] * dims[1];
+    if (v.ne[2] > 1) {
+        if (!stride_ok(v.nb[2])) return false;
+        strides[1] = v.nb[2];
+    } else {
+        strides[1] = (plane_bytes + 15) / 16 * 16;
+    }
+    if (v.ne[3] > 1) {
+        if (!stride_ok(v.nb[3])) return false;
+        strides[2] = v.nb[3];
+    } else {
+        strides[2] = (strides[1] * dims[2] + 15) / 16 * 16;
+    }
+    if (strides[1] >= (cuuint64_t(1) << 40) || strides[2] >= (cuuint64_t(1) << 40)) return false;
+    box[2] = 1;
+    box[3] = 1;
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.data, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Launches one instantiation; the >48 KiB dynamic shared memory opt-in is set once per device.
+template <int QTYPE, int QTRANS>
+int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& p, cudaStream_t stream) {
+    static std::mutex mu;
+    static uint64_t   configured = 0;  // bit per device ordinal
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+        if (bit == 0 || (configured & bit) == 0) {
+            e = cudaFuncSetAttribute(tf32x3_gemm_kernel<QTYPE, QTRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SMEM_BYTES);
+            if (e != cudaSuccess) return cuda_fail(e);
+            configured |= bit;
+        }
+    }
+    const int sms = sm_count_current();
+    if (sms <= 0) return TRC_CUDA_ECUDA;
+    const int64_t grid = std::min<int64_t>(p.total_tiles, sms);
+    tf32x3_gemm_kernel<QTYPE, QTRANS><<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
+    note_launch();
+    return check_launch();
+}
+
+}  // namespace
+
+bool mul_mat_tc_eligible(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d) {
+    const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
+    const trc_cuda_view& A = swap ? b_in : a_in;
+    const trc_cuda_view& B = swap ? a_in : b_in;
+    const int64_t M = A.ne[1], N = B.ne[1], K = a_in.ne[0];
+    if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return false;
+    if (b_in.ne[2] >= (1 << 30) || b_in.ne[3] >= (1 << 30)) return false;
+    CUtensorMap tm;
+    bool mn = false;
+    return encode_operand(A, BM, mn, tm) && encode_operand(B, BN, mn, tm);
+}
+
+int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
+               cudaStream_t stream) {
+    // Put D's unit-stride dimension on the TMEM lanes so that epilogue stores coalesce: if D is
+    // contiguous along ggml's j (ne1) rather than i (ne0), compute D^T = b^T a with roles swapped.
+    const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
+    const trc_cuda_view& A = swap ? b_in : a_in;  // MMA-A: rows = M
+    const trc_cuda_view& B = swap ? a_in : b_in;  // MMA-B: rows = N
+    const int64_t M = A.ne[1], N = B.ne[1], K = a_in.ne[0];
+    const int64_t planes2 = b_in.ne[2], planes3 = b_in.ne[3];
+    if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
+    if (planes2 >= (1 << 30) || planes3 >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
+
+    CUtensorMap tmA, tmB;
+    bool a_mn = false, b_mn = false;
+    if (!encode_operand(A, BM, a_mn, tmA)) return TRC_CUDA_EUNSUPPORTED;
+    if (!encode_operand(B, BN, b_mn, tmB)) return TRC_CUDA_EUNSUPPORTED;
+
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.m_tiles  = static_cast<int>((M + BM - 1) / BM);
+    p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
+    p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+    p.planes2 = static_cast<int>(planes2);
+    p.planes3 = static_cast<int>(planes3);
+    p.a_ne2 = static_cast<int>(A.ne[2]);
+    p.a_ne3 = static_cast<int>(A.ne[3]);
+    p.b_ne2 = static_cast<int>(B.ne[2]);
+    p.b_ne3 = static_cast<int>(B.ne[3]);
+    p.a_mn = a_mn ? 1 : 0;
+    p.b_mn = b_mn ? 1 : 0;
+    p.accumulate = accumulate ? 1 : 0;
+    p.total_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * planes2 * planes3;
+    p.d    = static_cast<char*>(d.data);
+    p.d_sm = swap ? d.nb[1] : d.nb[0];
+    p.d_sn = swap ? d.nb[0] : d.nb[1];
+    p.d_s2 = d.nb[2];
+    p.d_s3 = d.nb[3];
+
+    return launch_tc<0, 0>(tmA, tmB, p, stream);
+}
+
+int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                 const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, cudaStream_t stream) {
+    const int64_t M = a_transposed ? w_ne0 : w_ne1;
+    const int64_t K = a_transposed ? w_ne1 : w_ne0;
+    const int64_t N = b.ne[1];
+    if (M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30) || N <= 0) return TRC_CUDA_EUNSUPPORTED;
+    if ((reinterpret_cast<uint64_t>(w_blocks) & 1u) != 0) return TRC_CUDA_EINVAL;
+    CUtensorMap tmA, tmB;
+    std::memset(&tmA, 0, sizeof(tmA));
+    bool b_mn = false;
+    if (!encode_operand(b, BN, b_mn, tmB)) return TRC_CUDA_EUNSUPPORTED;
+    const size_t bb = trc_cuda_block_bytes(type);
+
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.m_tiles  = static_cast<int>((M + BM - 1) / BM);
+    p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
+    p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+    p.planes2 = static_cast<int>(b.ne[2]);
+    p.planes3 = static_cast<int>(b.ne[3]);
+    p.a_ne2 = 1;
+    p.a_ne3 = 1;
+    p.b_ne2 = static_cast<int>(b.ne[2]);
+    p.b_ne3 = static_cast<int>(b.ne[3]);
+    p.a_mn = a_transposed ? 1 : 0;
+    p.b_mn = b_mn ? 1 : 0;
+    p.accumulate = accumulate ? 1 : 0;
+    p.total_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * b.ne[2] * b.ne[3];
+    p.d    = static_cast<char*>(d.data);
+    p.d_sm = d.nb[0];
+    p.d_sn = d.nb[1];
+    p.d_s2 = d.nb[2];
+    p.d_s3 = d.nb[3];
+    p.qa = static_cast<const uint8_t*>(w_blocks);
+    p.q_blocks_per_row = static_cast<int>(w_ne0 / 32);
+    p.q_row_bytes = static_cast<int64_t>(w_ne0 / 32) * static_cast<int64_t>(bb);
+    p.q_rows = static_cast<int>(w_ne1);
+
+#define TRC_Q_CASE(T)                                                                   \
+    case T:                                                                             \
+        return a_transposed ? launch_tc<T, 1>(tmA, tmB, p, stream) : launch_tc<T, 0>(tmA, tmB, p, stream);
+    switch (type) {
+        TRC_Q_CASE(2)
+        TRC_Q_CASE(3)
+        TRC_Q_CASE(6)
+        TRC_Q_CASE(7)
+        TRC_Q_CASE(8)
+        default: return TRC_CUDA_EUNSUPPORTED;
+    }
+#undef TRC_Q_CASE
+}
+
+}  // namespace trc

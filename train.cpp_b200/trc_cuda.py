@@ -1,0 +1,376 @@
+"""Python host mirror of train.cpp's quantized-weight hot path on the B200 (libtrc_cuda.so).
+
+The functions keep the reference's names and argument meaning (paths relative to the train.cpp
+source tree):
+
+  gguf_tensor_to_f32(type, blocks)        src/io/trc_gguf.cpp:966-1049 (Q* branch :1040-1044)
+  gguf_load_tensor(type, host_blocks, dst) src/io/trc_gguf.cpp:1051-1094 (F32 destination)
+  mul_mat(a, b)                            src/ops/trc_ops.cpp:366-385 + trc_cpu_ops.cpp:182-216
+  mul_mat_q(type, w_blocks, ...)           fused dequant + mul_mat (no reference counterpart:
+                                           the reference must materialise the F32 weight)
+  cont / acc / repeat_back / repeat / add / sub / mul / div / sum
+                                           src/backends/cpu/trc_cpu_ops.cpp (compute_dup :219,
+                                           compute_acc :954, compute_repeat_back :932, ...)
+
+Tensors are torch CUDA tensors used purely as device memory. A ggml tensor with
+ne = [ne0, ne1, ne2, ne3] is a torch tensor of shape (ne3, ne2, ne1, ne0); any torch stride
+pattern maps to ggml byte strides nb (so `t.transpose(-1, -2)` is ggml's `transpose`).
+Every call goes through the C ABI of include/trc_cuda.h; there is no CPU fallback: if the
+library is missing or a call fails, TrcCudaError is raised, mirroring the reference's TRC_ABORT.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Sequence
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libtrc_cuda.so"
+
+# ggml type ids (include/traincpp/trc_types.h:11-49)
+TYPE_F32, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q5_0, TYPE_Q5_1, TYPE_Q8_0 = 0, 2, 3, 6, 7, 8
+TYPE_NAMES = {TYPE_Q4_0: "q4_0", TYPE_Q4_1: "q4_1", TYPE_Q5_0: "q5_0", TYPE_Q5_1: "q5_1", TYPE_Q8_0: "q8_0"}
+BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_Q8_0: 34}
+QK = 32  # weights per block
+
+MM_ACCUMULATE, MM_SIMT = 1, 2
+BIN_ADD, BIN_SUB, BIN_MUL, BIN_DIV = 0, 1, 2, 3
+
+
+class TrcCudaError(RuntimeError):
+    pass
+
+
+class View(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_int64 * 4)]
+
+
+class DequantJob(ctypes.Structure):
+    _fields_ = [("blocks", ctypes.c_void_p), ("out", ctypes.c_void_p), ("n_blocks", ctypes.c_int64),
+                ("type", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libtrc_cuda.so (built in-tree by build.py). Raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise TrcCudaError(f"{LIB_PATH} is missing: run train.cpp_b200/build.py (no CPU fallback exists)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    P, I, I64, U32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_uint32, ctypes.c_size_t
+    VP = ctypes.POINTER(View)
+    sig = {
+        "trc_cuda_abi_version": (I, []),
+        "trc_cuda_status_string": (ctypes.c_char_p, [I]),
+        "trc_cuda_last_cuda_error": (I, []),
+        "trc_cuda_device_error": (I, [ctypes.POINTER(I), I]),
+        "trc_cuda_launch_count": (ctypes.c_uint64, []),
+        "trc_cuda_sm_count": (I, []),
+        "trc_cuda_block_bytes": (SZ, [I]),
+        "trc_cuda_dequant": (I, [I, P, I64, P, P]),
+        "trc_cuda_dequant_many": (I, [ctypes.POINTER(DequantJob), I, P]),
+        "trc_cuda_load_quant": (I, [I, P, I64, P, P, P]),
+        "trc_cuda_mul_mat": (I, [VP, VP, VP, U32, P]),
+        "trc_cuda_mul_mat_q": (I, [I, P, I64, I64, I, VP, VP, U32, P]),
+        "trc_cuda_mul_mat_kernel": (I, [VP, VP, VP, U32]),
+        "trc_cuda_cont": (I, [VP, VP, P]),
+        "trc_cuda_acc": (I, [P, I64, VP, I64, I64, I64, I64, P]),
+        "trc_cuda_repeat_back": (I, [VP, VP, P]),
+        "trc_cuda_repeat": (I, [VP, VP, P]),
+        "trc_cuda_binary": (I, [I, VP, VP, VP, P]),
+        "trc_cuda_sum_workspace_bytes": (SZ, [I64]),
+        "trc_cuda_sum": (I, [VP, P, P, SZ, P]),
+        "trc_cuda_fill": (I, [P, I64, ctypes.c_float, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        L = lib()
+        msg = L.trc_cuda_status_string(status).decode()
+        cuda_err = L.trc_cuda_last_cuda_error()
+        raise TrcCudaError(f"{what}: {msg} (status {status}, cudaError {cuda_err})")
+
+
+def _stream(stream: torch.cuda.Stream | None = None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+# ------------------------------------------------------------------ ggml <-> torch views
+
+def ggml_ne(t: torch.Tensor) -> list[int]:
+    shape = list(t.shape)[::-1]
+    if len(shape) > 4:
+        raise TrcCudaError("ggml tensors have at most 4 dimensions")
+    return shape + [1] * (4 - len(shape))
+
+
+def view_of(t: torch.Tensor) -> View:
+    """ggml view (ne, byte strides nb) of a float32 CUDA tensor with any strides."""
+    if t.dtype != torch.float32:
+        raise TrcCudaError(f"expected float32, got {t.dtype}")
+    if not t.is_cuda:
+        raise TrcCudaError("expected a CUDA tensor (device memory)")
+    ne = ggml_ne(t)
+    st = [s * 4 for s in list(t.stride())[::-1]]
+    nb = st + [0] * (4 - len(st))
+    # strides of padded size-1 dimensions: the contiguous value, as ggml sets them
+    for d in range(len(st), 4):
+        nb[d] = nb[d - 1] * ne[d - 1] if d > 0 else 4
+    v = View()
+    v.data = t.data_ptr()
+    for i in range(4):
+        v.ne[i] = ne[i]
+        v.nb[i] = nb[i]
+    return v
+
+
+def ggml_empty(ne: Sequence[int], device="cuda") -> torch.Tensor:
+    """Contiguous F32 tensor with ggml extents ne (ne0 innermost)."""
+    ne = list(ne) + [1] * (4 - len(ne))
+    return torch.empty(ne[::-1], dtype=torch.float32, device=device)
+
+
+def transpose(t: torch.Tensor) -> torch.Tensor:
+    """ggml transpose = permute(1, 0, 2, 3): swaps ne0/ne1 (a strided view, no copy)."""
+    return t.transpose(-1, -2)
+
+
+# ------------------------------------------------------------------ dequantization
+
+def block_bytes(qtype: int) -> int:
+    return int(lib().trc_cuda_block_bytes(qtype))
+
+
+def gguf_tensor_to_f32(qtype: int, blocks: torch.Tensor, n_elems: int | None = None,
+                       out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Device dequantization of packed legacy blocks (uint8 CUDA tensor) to F32, bit-exact with the
+    reference's host dequantizers. Returns a flat float32 tensor of 32 * n_blocks weights."""
+    bb = block_bytes(qtype)
+    if bb == 0:
+        raise TrcCudaError(f"type {qtype} is not a legacy quantized type")
+    if blocks.dtype != torch.uint8 or not blocks.is_cuda or not blocks.is_contiguous():
+        raise TrcCudaError("blocks must be a contiguous uint8 CUDA tensor")
+    n_blocks = blocks.numel() // bb
+    if n_elems is not None:
+        if n_elems % QK != 0:
+            raise TrcCudaError(f"{n_elems} weights are not a whole number of 32-weight blocks")
+        n_blocks = n_elems // QK
+    if n_blocks * bb > blocks.numel():
+        raise TrcCudaError("packed buffer is smaller than the tensor")
+    if out is None:
+        out = torch.empty(n_blocks * QK, dtype=torch.float32, device=blocks.device)
+    _check(lib().trc_cuda_dequant(qtype, blocks.data_ptr(), n_blocks, out.data_ptr(), _stream(stream)),
+           "trc_cuda_dequant")
+    return out
+
+
+def dequantize_many(jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]], stream=None) -> None:
+    """Batched device dequantization: jobs of (qtype, packed uint8 CUDA tensor, F32 output)."""
+    arr = (DequantJob * max(1, len(jobs)))()
+    for i, (qtype, blocks, out) in enumerate(jobs):
+        bb = block_bytes(qtype)
+        arr[i].blocks = blocks.data_ptr()
+        arr[i].out = out.data_ptr()
+        arr[i].n_blocks = out.numel() // QK
+        arr[i].type = qtype
+        if blocks.numel() < arr[i].n_blocks * bb:
+            raise TrcCudaError("packed buffer is smaller than its output")
+    _check(lib().trc_cuda_dequant_many(arr, len(jobs), _stream(stream)), "trc_cuda_dequant_many")
+
+
+def gguf_load_tensor(qtype: int, host_blocks, dst: torch.Tensor, staging: torch.Tensor, stream=None) -> None:
+    """Device-side gguf_load_tensor for a quantized file tensor and an F32 destination: uploads the
+    packed HOST bytes (numpy array or CPU tensor, pinned for an asynchronous copy) into `staging`
+    and dequantizes into `dst`."""
+    if isinstance(host_blocks, torch.Tensor):
+        ptr, nbytes = host_blocks.data_ptr(), host_blocks.numel() * host_blocks.element_size()
+    else:
+        ptr, nbytes = host_blocks.ctypes.data, host_blocks.nbytes
+    n_blocks = dst.numel() // QK
+    if nbytes < n_blocks * block_bytes(qtype) or staging.numel() < n_blocks * block_bytes(qtype):
+        raise TrcCudaError("host or staging buffer smaller than the tensor")
+    _check(lib().trc_cuda_load_quant(qtype, ctypes.c_void_p(ptr), n_blocks, staging.data_ptr(), dst.data_ptr(),
+                                     _stream(stream)), "trc_cuda_load_quant")
+
+
+# ------------------------------------------------------------------ mul_mat
+
+def mul_mat_out_ne(a: torch.Tensor, b: torch.Tensor) -> list[int]:
+    na, nb_ = ggml_ne(a), ggml_ne(b)
+    return [na[1], nb_[1], nb_[2], nb_[3]]
+
+
+def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False,
+            simt: bool = False, stream=None) -> torch.Tensor:
+    """ggml mul_mat: out[i, j, i2, i3] = sum_k a[k, i, i2 % a2, i3 % a3] * b[k, j, i2, i3]."""
+    na, nb_ = ggml_ne(a), ggml_ne(b)
+    if na[0] != nb_[0]:
+        raise TrcCudaError(f"mul_mat: inner dims differ (a.ne0={na[0]}, b.ne0={nb_[0]})")
+    if nb_[2] % na[2] or nb_[3] % na[3]:
+        raise TrcCudaError("mul_mat: a's planes do not broadcast onto b's (b.ne % a.ne must be 0)")
+    if out is None:
+        out = ggml_empty(mul_mat_out_ne(a, b), device=a.device)
+    flags = (MM_ACCUMULATE if accumulate else 0) | (MM_SIMT if simt else 0)
+    va, vb, vd = view_of(a), view_of(b), view_of(out)
+    _check(lib().trc_cuda_mul_mat(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), flags, _stream(stream)),
+           "trc_cuda_mul_mat")
+    return out
+
+
+KERNEL_TCGEN05, KERNEL_SIMT = 1, 2
+
+
+def mul_mat_kernel(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, simt: bool = False) -> int:
+    """Which kernel mul_mat would run for these views: KERNEL_TCGEN05 or KERNEL_SIMT."""
+    va, vb, vd = view_of(a), view_of(b), view_of(out)
+    r = lib().trc_cuda_mul_mat_kernel(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), MM_SIMT if simt else 0)
+    if r < 0:
+        _check(r, "trc_cuda_mul_mat_kernel")
+    return r
+
+
+def mul_mat_q(qtype: int, w_blocks: torch.Tensor, w_ne0: int, w_ne1: int, b: torch.Tensor,
+              transposed: bool = False, out: torch.Tensor | None = None, accumulate: bool = False,
+              stream=None) -> torch.Tensor:
+    """Fused dequant + mul_mat with a = W (transposed=False) or a = transpose(W), W being the frozen
+    quantized weight of ggml shape [w_ne0, w_ne1] held as packed blocks on the device."""
+    K, M = (w_ne1, w_ne0) if transposed else (w_ne0, w_ne1)
+    nb_ = ggml_ne(b)
+    if nb_[0] != K:
+        raise TrcCudaError(f"mul_mat_q: inner dims differ ({K} vs {nb_[0]})")
+    if out is None:
+        out = ggml_empty([M, nb_[1], nb_[2], nb_[3]], device=b.device)
+    vb, vd = view_of(b), view_of(out)
+    _check(lib().trc_cuda_mul_mat_q(qtype, w_blocks.data_ptr(), w_ne0, w_ne1, 1 if transposed else 0,
+                                    ctypes.byref(vb), ctypes.byref(vd), MM_ACCUMULATE if accumulate else 0,
+                                    _stream(stream)), "trc_cuda_mul_mat_q")
+    return out
+
+
+# ------------------------------------------------------------------ graph ops
+
+def cont(src: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    if out is None:
+        out = ggml_empty(ggml_ne(src), device=src.device)
+    vs, vd = view_of(src), view_of(out)
+    _check(lib().trc_cuda_cont(ctypes.byref(vs), ctypes.byref(vd), _stream(stream)), "trc_cuda_cont")
+    return out
+
+
+def acc_(dst: torch.Tensor, b: torch.Tensor, nb1: int, nb2: int, nb3: int, offset: int, stream=None) -> torch.Tensor:
+    """In-place acc (inplace=1): dst's bytes [offset + i0*4 + i1*nb1 + i2*nb2 + i3*nb3] += b."""
+    if not dst.is_contiguous():
+        raise TrcCudaError("acc: destination must be contiguous")
+    vb = view_of(b)
+    _check(lib().trc_cuda_acc(dst.data_ptr(), dst.numel() * 4, ctypes.byref(vb), nb1, nb2, nb3, offset,
+                              _stream(stream)), "trc_cuda_acc")
+    return dst
+
+
+def repeat_back(src: torch.Tensor, dst_ne: Sequence[int], out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    if out is None:
+        out = ggml_empty(dst_ne, device=src.device)
+    vs, vd = view_of(src), view_of(out)
+    _check(lib().trc_cuda_repeat_back(ctypes.byref(vs), ctypes.byref(vd), _stream(stream)), "trc_cuda_repeat_back")
+    return out
+
+
+def repeat(src: torch.Tensor, dst_ne: Sequence[int], out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    if out is None:
+        out = ggml_empty(dst_ne, device=src.device)
+    vs, vd = view_of(src), view_of(out)
+    _check(lib().trc_cuda_repeat(ctypes.byref(vs), ctypes.byref(vd), _stream(stream)), "trc_cuda_repeat")
+    return out
+
+
+def _binary(op: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None, stream) -> torch.Tensor:
+    if out is None:
+        out = ggml_empty(ggml_ne(a), device=a.device)
+    va, vb, vd = view_of(a), view_of(b), view_of(out)
+    _check(lib().trc_cuda_binary(op, ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), _stream(stream)),
+           "trc_cuda_binary")
+    return out
+
+
+def add(a, b, out=None, stream=None):
+    return _binary(BIN_ADD, a, b, out, stream)
+
+
+def sub(a, b, out=None, stream=None):
+    return _binary(BIN_SUB, a, b, out, stream)
+
+
+def mul(a, b, out=None, stream=None):
+    return _binary(BIN_MUL, a, b, out, stream)
+
+
+def div(a, b, out=None, stream=None):
+    return _binary(BIN_DIV, a, b, out, stream)
+
+
+def sum_workspace_bytes(n: int) -> int:
+    return int(lib().trc_cuda_sum_workspace_bytes(n))
+
+
+def sum(src: torch.Tensor, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+        stream=None) -> torch.Tensor:  # noqa: A001 (mirrors the reference op name)
+    if out is None:
+        out = torch.empty(1, dtype=torch.float32, device=src.device)
+    need = sum_workspace_bytes(src.numel())
+    if workspace is None:
+        workspace = torch.empty((need + 7) // 8, dtype=torch.float64, device=src.device)
+    vs = view_of(src)
+    _check(lib().trc_cuda_sum(ctypes.byref(vs), out.data_ptr(), workspace.data_ptr(), workspace.numel() * 8,
+                              _stream(stream)), "trc_cuda_sum")
+    return out
+
+
+def fill_(dst: torch.Tensor, value: float, stream=None) -> torch.Tensor:
+    if not dst.is_contiguous() or dst.dtype != torch.float32:
+        raise TrcCudaError("fill: destination must be a contiguous float32 tensor")
+    _check(lib().trc_cuda_fill(dst.data_ptr(), dst.numel(), float(value), _stream(stream)), "trc_cuda_fill")
+    return dst
+
+
+# ------------------------------------------------------------------ diagnostics
+
+def device_error(reset: bool = True) -> int:
+    """Device error word of the current device: 0, or the code of a kernel that gave up a wait."""
+    code = ctypes.c_int(0)
+    _check(lib().trc_cuda_device_error(ctypes.byref(code), 1 if reset else 0), "trc_cuda_device_error")
+    return code.value
+
+
+def launch_count() -> int:
+    return int(lib().trc_cuda_launch_count())
+
+
+def sm_count() -> int:
+    return int(lib().trc_cuda_sm_count())
+
+
+def exported_symbols() -> list[str]:
+    """Names declared in include/trc_cuda.h (parsed), used by the CPU symbol test."""
+    hdr = PKG.parent / "include" / "trc_cuda.h"
+    import re
+    names = re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b(trc_cuda_\w+)\s*\(", hdr.read_text(), flags=re.M)
+    return sorted(set(names))
+
+
+if os.environ.get("TRC_CUDA_PRELOAD") == "1":  # opt-in eager load (used by smoke checks)
+    lib()
