@@ -387,6 +387,18 @@ def synth_name(t: int) -> str:
     return {v: k for k, v in synth.TYPE_BY_NAME.items()}[t]
 
 
+def run_only(args) -> None:
+    """One mul_mat workload on this GPU, printed as JSON (used for bounded profiling runs)."""
+    import torch
+
+    import trc_cuda as tc
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    tc.lib()
+    res = run_gemm_workloads(tc, torch, 0, 1, lambda: None, lambda x: x, measured_peaks(), args)
+    print(json.dumps({"only": args.only, "mul_mat": res}), flush=True)
+
+
 def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args) -> dict:
     """Fused Linear step (Q5_0 4096x14336, 2048 tokens) per rank, and the GQA batched broadcast
     forward + backward with ne[3] planes sharded across ranks. TFLOP/s count 2*K*M*N once."""
@@ -412,8 +424,13 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         return max_over_ranks(a.elapsed_time(b)) / reps
 
     out = {}
+    only = getattr(args, "only", None)
     # --- fused Linear step
     K, M, N = 4096, 14336, 2048
+    if only == "gqa":
+        K = 0
+    if K == 0:
+        return gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out)
     wq = torch.from_numpy(synth.random_blocks(synth.TYPE_Q5_0, K * M // 32, seed=21 + rank)).cuda()
     X = torch.randn((N, K), generator=gen, device="cuda")
     dY = torch.randn((N, M), generator=gen, device="cuda") * 1e-2
@@ -434,8 +451,14 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
     }
     del wq, X, dY, Y, dX, dW
-    # --- GQA batched broadcast, planes of ne[3] sharded across ranks
-    p3 = max(1, 8 // world)
+    if only == "linear":
+        return out
+    return gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out)
+
+
+def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> dict:
+    """GQA batched broadcast, planes of ne[3] sharded across ranks."""
+    p3 = args.gqa_p3 if getattr(args, "gqa_p3", 0) else max(1, 8 // world)
     A = torch.randn((p3, 8, 2048, 128), generator=gen, device="cuda")
     B = torch.randn((p3, 32, 2048, 128), generator=gen, device="cuda")
     G = torch.randn((p3, 32, 2048, 2048), generator=gen, device="cuda")
@@ -467,11 +490,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--only", choices=["linear", "gqa"], default=None,
+                    help="run only one mul_mat workload (bounded cases for profiling)")
+    ap.add_argument("--gqa-p3", type=int, default=0, help="ne[3] planes per rank for the GQA workload (0 = 8/N)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.only is not None:
+        run_only(args)
     else:
         run_ours(args)
 

@@ -1,0 +1,336 @@
+// test_dropin.cpp -- the CUDA backend as a drop-in train.cpp device.
+//
+// Everything above the backend is train.cpp's own code, unchanged (linked from the library that
+// oracle/Makefile compiles from its sources): contexts, op constructors, graph building, autograd,
+// buffer allocation, the GGUF reader and nn::Linear. Each case builds the same graph on the
+// reference CPU device and on the CUDA device and compares the results, the way the reference's
+// backend conformance suite compares its Vulkan device with the CPU
+// (tests/test_backend_conformance.cpp:43-128 of train.cpp).
+//
+// usage: test_dropin [all|alloc_fail] [path/to/quantized.gguf]
+// Exit status 0 when every case passes.
+#include "traincpp/traincpp.h"
+#include "trc_cuda_backend.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <random>
+#include <string>
+#include <vector>
+
+using namespace traincpp;
+
+namespace {
+
+int g_failures = 0;
+
+void fail(const std::string& msg) {
+    std::printf("    [FAIL] %s\n", msg.c_str());
+    ++g_failures;
+}
+
+std::vector<float> ramp(size_t n) {  // the conformance suite's input pattern
+    std::vector<float> v(n);
+    for (size_t i = 0; i < n; ++i) v[i] = (float) ((int) (i % 17) - 8) * 0.25f;
+    return v;
+}
+
+std::vector<float> gauss(size_t n, unsigned seed, float sigma = 1.0f) {
+    std::mt19937 g(seed);
+    std::normal_distribution<float> d(0.0f, sigma);
+    std::vector<float> v(n);
+    for (auto& x : v) x = d(g);
+    return v;
+}
+
+double normwise(const std::vector<float>& got, const std::vector<float>& want) {
+    double num = 0, den = 0;
+    for (size_t i = 0; i < want.size(); ++i) {
+        num = std::max(num, std::fabs((double) got[i] - want[i]));
+        den = std::max(den, std::fabs((double) want[i]));
+    }
+    return den > 0 ? num / den : num;
+}
+
+// the conformance tolerance of the reference (test_backend_conformance.cpp:99) plus the normwise bar
+void compare(const char* name, const std::vector<float>& got, const std::vector<float>& want, double norm_tol = 1e-5) {
+    if (got.size() != want.size()) {
+        fail(std::string(name) + ": size mismatch");
+        return;
+    }
+    int64_t bad = 0;
+    for (size_t i = 0; i < want.size(); ++i)
+        if (std::fabs((double) got[i] - want[i]) > 1e-5 + 2e-4 * std::fabs((double) want[i])) ++bad;
+    const double nw = normwise(got, want);
+    if (bad != 0 || nw > norm_tol) {
+        char buf[256];
+        std::snprintf(buf, sizeof(buf), "%s: %lld elements outside 1e-5+2e-4|ref|, normwise %.3g", name, (long long) bad, nw);
+        fail(buf);
+    } else {
+        std::printf("    [ OK ] %-34s normwise %.2e\n", name, nw);
+    }
+}
+
+struct Built {
+    Tensor* out;
+    std::vector<std::pair<Tensor*, std::vector<float>>> inputs;
+};
+using BuildFn = std::function<Built(Context*)>;
+
+std::vector<float> run_forward(Device* dev, const BuildFn& build) {
+    Context* ctx = context_new(1 << 22);
+    Graph*   g   = graph_new(ctx);
+    Built    b   = build(ctx);
+    Buffer*  buf = buffer_alloc_ctx_tensors(ctx, dev->default_buffer_type());
+    for (auto& in : b.inputs) tensor_set(in.first, in.second.data(), 0, in.second.size() * sizeof(float));
+    graph_build_forward_expand(ctx, g, b.out);
+    if (const Tensor* bad = graph_first_unsupported(g, dev)) {
+        fail(std::string("graph_first_unsupported: ") + op_name(bad->op));
+    }
+    dev->graph_compute(g);
+    std::vector<float> out((size_t) tensor_nelements(b.out));
+    tensor_get(b.out, out.data(), 0, out.size() * sizeof(float));
+    buffer_free(buf);
+    graph_free(g);
+    context_free(ctx);
+    return out;
+}
+
+void conformance_matmul(Device* cpu, Device* cuda) {
+    std::printf("  conformance_matmul (the reference's cases)\n");
+    struct Case {
+        const char* name;
+        BuildFn     fn;
+    };
+    std::vector<Case> cases = {
+        {"mul_mat_basic", [](Context* c) {
+             Tensor* a = new_tensor_2d(c, TYPE_F32, 5, 3);
+             Tensor* b = new_tensor_2d(c, TYPE_F32, 5, 4);
+             return Built{mul_mat(c, a, b), {{a, ramp(15)}, {b, ramp(20)}}};
+         }},
+        {"mul_mat_transposed_a", [](Context* c) {
+             Tensor* base = new_tensor_2d(c, TYPE_F32, 3, 5);
+             Tensor* b    = new_tensor_2d(c, TYPE_F32, 5, 4);
+             return Built{mul_mat(c, transpose(c, base), b), {{base, ramp(15)}, {b, ramp(20)}}};
+         }},
+        {"mul_mat_transposed_b", [](Context* c) {
+             Tensor* a    = new_tensor_2d(c, TYPE_F32, 5, 3);
+             Tensor* base = new_tensor_2d(c, TYPE_F32, 4, 5);
+             return Built{mul_mat(c, a, transpose(c, base)), {{a, ramp(15)}, {base, ramp(20)}}};
+         }},
+        {"mul_mat_tile_boundary", [](Context* c) {
+             Tensor* a = new_tensor_2d(c, TYPE_F32, 33, 70);
+             Tensor* b = new_tensor_2d(c, TYPE_F32, 33, 66);
+             return Built{mul_mat(c, a, b), {{a, ramp(33 * 70)}, {b, ramp(33 * 66)}}};
+         }},
+        {"mul_mat_batch", [](Context* c) {
+             Tensor* a = new_tensor_4d(c, TYPE_F32, 5, 3, 1, 1);
+             Tensor* b = new_tensor_4d(c, TYPE_F32, 5, 4, 2, 3);
+             return Built{mul_mat(c, a, b), {{a, ramp(15)}, {b, ramp(120)}}};
+         }},
+        {"mul_mat_batch_bcast_div", [](Context* c) {
+             Tensor* a = new_tensor_4d(c, TYPE_F32, 5, 3, 2, 1);
+             Tensor* b = new_tensor_4d(c, TYPE_F32, 5, 4, 4, 1);
+             return Built{mul_mat(c, a, b), {{a, ramp(30)}, {b, ramp(80)}}};
+         }},
+        {"mul_mat_batch_transposed", [](Context* c) {
+             Tensor* abase = new_tensor_4d(c, TYPE_F32, 3, 5, 2, 2);
+             Tensor* bbase = new_tensor_4d(c, TYPE_F32, 4, 5, 2, 2);
+             return Built{mul_mat(c, transpose(c, abase), transpose(c, bbase)), {{abase, ramp(60)}, {bbase, ramp(80)}}};
+         }},
+        {"mul_mat_batch_tile_boundary", [](Context* c) {
+             Tensor* a = new_tensor_4d(c, TYPE_F32, 33, 70, 1, 1);
+             Tensor* b = new_tensor_4d(c, TYPE_F32, 33, 66, 2, 2);
+             return Built{mul_mat(c, a, b), {{a, ramp(33 * 70)}, {b, ramp(33 * 66 * 4)}}};
+         }},
+        {"grid_mul_mat_batch_z", [](Context* c) {
+             Tensor* a = new_tensor_4d(c, TYPE_F32, 8, 4, 1, 1);
+             Tensor* b = new_tensor_4d(c, TYPE_F32, 8, 4, 65, 1);
+             return Built{mul_mat(c, a, b), {{a, ramp(32)}, {b, ramp(8 * 4 * 65)}}};
+         }},
+        // tensor-core eligible shapes (16-byte strides), transposed views, broadcast, ragged tiles
+        {"tc_linear_fwd", [](Context* c) {
+             Tensor* w = new_tensor_2d(c, TYPE_F32, 1024, 300);
+             Tensor* x = new_tensor_2d(c, TYPE_F32, 1024, 72);
+             return Built{mul_mat(c, w, x), {{w, gauss(1024 * 300, 1)}, {x, gauss(1024 * 72, 2)}}};
+         }},
+        {"tc_transposed_both", [](Context* c) {
+             Tensor* abase = new_tensor_4d(c, TYPE_F32, 132, 520, 2, 1);
+             Tensor* bbase = new_tensor_4d(c, TYPE_F32, 260, 520, 4, 1);
+             return Built{mul_mat(c, transpose(c, abase), transpose(c, bbase)),
+                          {{abase, gauss(132 * 520 * 2, 3)}, {bbase, gauss(260 * 520 * 4, 4)}}};
+         }},
+    };
+    for (auto& k : cases) compare(k.name, run_forward(cuda, k.fn), run_forward(cpu, k.fn));
+}
+
+struct StepOut {
+    std::vector<float> y, da, db, dbias;
+};
+
+// One training step of y = mul_mat(A, B) [+ bias] with loss = sum(mul(y, G)) through the reference
+// autograd (trc_autograd.cpp:487-503; the injected gradient dL/dy = G).
+StepOut run_step(Device* dev, const int64_t* ane, const int64_t* bne, bool with_bias, unsigned seed) {
+    Context* ctx = context_new(1 << 22);
+    Graph*   g   = graph_new(ctx);
+    Tensor*  A   = new_tensor_4d(ctx, TYPE_F32, ane[0], ane[1], ane[2], ane[3]);
+    Tensor*  B   = new_tensor_4d(ctx, TYPE_F32, bne[0], bne[1], bne[2], bne[3]);
+    tensor_set_param(A);
+    tensor_set_param(B);
+    Tensor* y    = mul_mat(ctx, A, B);
+    Tensor* bias = nullptr;
+    if (with_bias) {
+        bias = new_tensor_1d(ctx, TYPE_F32, y->ne[0]);
+        tensor_set_param(bias);
+        y = add(ctx, y, bias);
+    }
+    Tensor* G    = new_tensor_4d(ctx, TYPE_F32, y->ne[0], y->ne[1], y->ne[2], y->ne[3]);
+    Tensor* loss = sum(ctx, mul(ctx, y, G));
+    tensor_set_loss(loss);
+    graph_build_forward_expand(ctx, g, loss);
+    graph_build_backward_expand(g);
+    if (const Tensor* bad = graph_first_unsupported(g, dev)) fail(std::string("preflight: ") + op_name(bad->op));
+    Buffer* buf = buffer_alloc_ctx_tensors(ctx, dev->default_buffer_type());
+    auto av = gauss((size_t) tensor_nelements(A), seed);
+    auto bv = gauss((size_t) tensor_nelements(B), seed + 1);
+    auto gv = gauss((size_t) tensor_nelements(G), seed + 2, 1e-2f);
+    tensor_set(A, av.data(), 0, av.size() * 4);
+    tensor_set(B, bv.data(), 0, bv.size() * 4);
+    tensor_set(G, gv.data(), 0, gv.size() * 4);
+    if (bias != nullptr) {
+        auto bb = gauss((size_t) tensor_nelements(bias), seed + 3);
+        tensor_set(bias, bb.data(), 0, bb.size() * 4);
+    }
+    graph_reset(g);
+    dev->graph_compute(g);
+    StepOut r;
+    r.y.resize((size_t) tensor_nelements(y));
+    tensor_get(y, r.y.data(), 0, r.y.size() * 4);
+    Tensor* ga = graph_get_grad_acc(g, A);
+    Tensor* gb = graph_get_grad_acc(g, B);
+    r.da.resize((size_t) tensor_nelements(ga));
+    r.db.resize((size_t) tensor_nelements(gb));
+    tensor_get(ga, r.da.data(), 0, r.da.size() * 4);
+    tensor_get(gb, r.db.data(), 0, r.db.size() * 4);
+    if (bias != nullptr) {
+        Tensor* gbias = graph_get_grad_acc(g, bias);
+        r.dbias.resize((size_t) tensor_nelements(gbias));
+        tensor_get(gbias, r.dbias.data(), 0, r.dbias.size() * 4);
+    }
+    buffer_free(buf);
+    graph_free(g);
+    context_free(ctx);
+    return r;
+}
+
+void training_steps(Device* cpu, Device* cuda) {
+    std::printf("  training steps through the reference autograd\n");
+    struct Case {
+        const char* name;
+        int64_t     a[4], b[4];
+        bool        bias;
+    };
+    const Case cases[] = {
+        {"linear_step (W 1024x384, 96 tokens)", {1024, 384, 1, 1}, {1024, 96, 1, 1}, false},
+        {"linear_step_bias", {512, 256, 1, 1}, {512, 80, 1, 1}, true},
+        {"linear_step_ragged", {100, 70, 1, 1}, {100, 33, 1, 1}, false},
+        {"gqa_step (bcast ne2 x4)", {128, 96, 2, 2}, {128, 80, 8, 2}, false},
+    };
+    for (const Case& c : cases) {
+        const StepOut want = run_step(cpu, c.a, c.b, c.bias, 7);
+        const StepOut got  = run_step(cuda, c.a, c.b, c.bias, 7);
+        const std::string n = c.name;
+        compare((n + " y").c_str(), got.y, want.y);
+        compare((n + " dA").c_str(), got.da, want.da);
+        compare((n + " dB").c_str(), got.db, want.db);
+        if (c.bias) compare((n + " dbias").c_str(), got.dbias, want.dbias);
+    }
+}
+
+void gguf_warm_start(Device* cpu, Device* cuda, const char* path) {
+    std::printf("  GGUF warm start: device dequant vs the reference loader (%s)\n", path);
+    GgufFile* f = gguf_open(path, true);
+    if (f == nullptr) {
+        fail("gguf_open failed");
+        return;
+    }
+    for (int64_t i = 0; i < gguf_tensor_count(f); ++i) {
+        const GgufTensorInfo* info = gguf_tensor_info(f, i);
+        Context* ctx = context_new(1 << 20);
+        Tensor* w_dev = gguf_new_tensor(ctx, f, info->name, TYPE_F32);  // device dequant target
+        Tensor* w_ref = gguf_new_tensor(ctx, f, info->name, TYPE_F32);  // reference loader target
+        Buffer* buf   = buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
+        const bool ok1 = cuda_gguf_load_tensor(f, path, info->name, w_dev);
+        const bool ok2 = gguf_load_tensor(f, info->name, w_ref);  // host dequant + tensor_set (H2D)
+        const size_t n = (size_t) tensor_nelements(w_dev);
+        std::vector<float> a(n), b(n);
+        tensor_get(w_dev, a.data(), 0, n * 4);
+        tensor_get(w_ref, b.data(), 0, n * 4);
+        if (!ok1 || !ok2 || std::memcmp(a.data(), b.data(), n * 4) != 0) {
+            fail(std::string("gguf tensor ") + info->name + " not bit-identical");
+        } else {
+            std::printf("    [ OK ] %-34s %zu weights bit-identical (%s)\n", info->name, n, type_name(info->type));
+        }
+        buffer_free(buf);
+        context_free(ctx);
+    }
+    // the warm-started weight feeds nn::Linear (linear_init_weight, src/nn/trc_nn.cpp:209-220)
+    const GgufTensorInfo* info = gguf_tensor_info(f, 0);
+    std::vector<float> outs[2];
+    Device* devs[2] = {cpu, cuda};
+    for (int d = 0; d < 2; ++d) {
+        Context* ctx = context_new(1 << 20);
+        Graph*   g   = graph_new(ctx);
+        Tensor*  w   = gguf_new_tensor(ctx, f, info->name, TYPE_F32);
+        Linear   lin;
+        linear_init_weight(ctx, &lin, w, nullptr);
+        Tensor* x = new_tensor_2d(ctx, TYPE_F32, w->ne[0], 40);
+        Tensor* y = linear_forward(ctx, &lin, x);
+        graph_build_forward_expand(ctx, g, y);
+        Buffer* buf = buffer_alloc_ctx_tensors(ctx, devs[d]->default_buffer_type());
+        if (d == 1) cuda_gguf_load_tensor(f, path, info->name, w);
+        else gguf_load_tensor(f, info->name, w);
+        auto xv = gauss((size_t) tensor_nelements(x), 5);
+        tensor_set(x, xv.data(), 0, xv.size() * 4);
+        devs[d]->graph_compute(g);
+        outs[d].resize((size_t) tensor_nelements(y));
+        tensor_get(y, outs[d].data(), 0, outs[d].size() * 4);
+        buffer_free(buf);
+        graph_free(g);
+        context_free(ctx);
+    }
+    compare("linear_forward on warm-started W", outs[1], outs[0]);
+    gguf_close(f);
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    const std::string mode = argc > 1 ? argv[1] : "all";
+    const int n = cuda_register_devices();
+    Device* cuda = device_by_type(DeviceType::GPU);
+    Device* cpu  = device_cpu();
+    if (n == 0 || cuda == nullptr || cpu == nullptr) {
+        std::printf("no CUDA device registered\n");
+        return 77;
+    }
+    std::printf("devices: %zu registered; CUDA device: %s (%s)\n", device_count(), cuda->props().name.c_str(),
+                cuda->props().description.c_str());
+    if (mode == "alloc_fail") {
+        // TRC_CUDA_FAIL_ALLOC=1 in the environment: the first buffer allocation fails and the core
+        // aborts with its need/available message (src/core/trc_backend_reg.cpp:248-264).
+        Context* ctx = context_new(1 << 16);
+        new_tensor_2d(ctx, TYPE_F32, 1024, 1024);
+        buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
+        std::printf("allocation unexpectedly succeeded\n");
+        return 0;
+    }
+    conformance_matmul(cpu, cuda);
+    training_steps(cpu, cuda);
+    if (argc > 2) gguf_warm_start(cpu, cuda, argv[2]);
+    std::printf("%s: %d failure(s)\n", g_failures == 0 ? "PASS" : "FAIL", g_failures);
+    return g_failures == 0 ? 0 : 1;
+}

@@ -93,12 +93,12 @@ def main(ref_dir: Path) -> None:
     # forward with views: (A base shape, A transposed?, B base shape, B transposed?)
     fwd = {
         "fwd_basic": ((3, 36), False, (5, 36), False),
-        "fwd_ta": ((36, 70), True, (66, 36), False),
-        "fwd_tb": ((70, 36), False, (36, 66), True),
-        "fwd_tab": ((40, 130), True, (40, 258), True),
+        "fwd_ta": ((36, 68), True, (66, 36), False),
+        "fwd_tb": ((70, 36), False, (36, 68), True),
+        "fwd_tab": ((40, 132), True, (40, 260), True),
         "fwd_odd": ((70, 33), False, (66, 33), False),
         "fwd_bcast": ((2, 1, 70, 36), False, (2, 4, 66, 36), False),
-        "fwd_bcast_t": ((2, 1, 36, 70), True, (2, 4, 36, 66), True),
+        "fwd_bcast_t": ((2, 1, 36, 68), True, (2, 4, 36, 72), True),
     }
     for name, (sa, ta, sb, tb) in fwd.items():
         a, b = f32(*sa), f32(*sb)
@@ -107,7 +107,7 @@ def main(ref_dir: Path) -> None:
         m[name + "_d"] = oracle.ref_mul_mat(a, ta, b, tb)
     # training steps: loss = sum(mul(D, G)); A and B are PARAMs (shapes as numpy = reversed ne)
     steps = {
-        "step_linear": ((96, 64), (40, 64)),             # W[k=64, m=96], X[k=64, n=40]
+        "step_linear": ((96, 300), (40, 300)),           # W[k=300, m=96], X[k=300, n=40]: 2 promotion chunks
         "step_gqa": ((2, 2, 48, 16), (2, 8, 40, 16)),    # A[16,48,2,2] . B[16,40,8,2], bcast ne2 x4
         "step_ragged": ((70, 33), (66, 33)),
     }

@@ -1,0 +1,521 @@
+// trc_cuda_backend.cpp -- train.cpp's abstract backend (include/traincpp/trc_backend.h:33-88)
+// implemented for NVIDIA B200 on top of the C ABI of libtrc_cuda.so (include/trc_cuda.h).
+//
+//   CudaBufferType  device() / name() "CUDA<i>" / alignment() 256 / alloc_buffer() -> nullptr on
+//                   failure, so the core prints need/available and aborts as it does for every
+//                   backend (src/core/trc_backend_reg.cpp:248-264)
+//   CudaBuffer      device-local memory: base() is nullptr and tensors are located by
+//                   Tensor::data_offset (src/core/trc_backend_reg.cpp:276-279); set/get_tensor are
+//                   host<->device copies; clear() a device memset
+//   CudaDevice      supports_op() answers for every node without aborting; graph_compute() runs
+//                   each node's kernel on the device's stream and returns when results are ready
+//                   (the synchronous contract of trc_backend.h:78); fill_tensors() is a device fill
+//
+// Fatal errors abort with file:line and a message, like the reference's TRC_ABORT
+// (src/core/trc_impl.h:118-125); a kernel that gave up a bounded wait is reported the same way.
+#include "trc_cuda_backend.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "trc_cuda.h"
+#include "trc_cuda_runtime.h"
+
+namespace traincpp {
+
+namespace {
+
+[[noreturn]] void backend_abort(const char* file, int line, const char* fmt, ...) {
+    std::fprintf(stderr, "[traincpp] 致命错误 %s:%d: ", file, line);
+    va_list ap;
+    va_start(ap, fmt);
+    std::vfprintf(stderr, fmt, ap);
+    va_end(ap);
+    std::fprintf(stderr, "\n");
+    std::fflush(stderr);
+    std::abort();
+}
+
+#define CB_ABORT(...) backend_abort(__FILE__, __LINE__, __VA_ARGS__)
+#define CB_CUDA(call)                                                                                   \
+    do {                                                                                                \
+        const int s_ = (call);                                                                          \
+        if (s_ != TRC_CUDA_OK)                                                                          \
+            CB_ABORT("CUDA: %s -> %s (%s)", #call, trc_cuda_status_string(s_),                          \
+                     trc_cuda_rt_error_string(trc_cuda_last_cuda_error()));                             \
+    } while (0)
+#define CB_TRC(call, what)                                                                          \
+    do {                                                                                            \
+        const int s_ = (call);                                                                      \
+        if (s_ != TRC_CUDA_OK)                                                                      \
+            CB_ABORT("CUDA: %s failed: %s (cudaError %d)", what, trc_cuda_status_string(s_),         \
+                     trc_cuda_last_cuda_error());                                                   \
+    } while (0)
+
+// Host-side failure injection for tests (no GPU fault involved): TRC_CUDA_FAIL_ALLOC=n makes the
+// n-th buffer allocation of the process fail as if the device were out of memory.
+bool fake_alloc_failure() {
+    static std::mutex mu;
+    static long counter = 0;
+    const char* env = std::getenv("TRC_CUDA_FAIL_ALLOC");
+    if (env == nullptr) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    ++counter;
+    return counter == std::atol(env);
+}
+
+class CudaDevice;
+
+class CudaBufferType : public BufferType {
+public:
+    explicit CudaBufferType(CudaDevice* dev, int ordinal) : dev_(dev) {
+        std::snprintf(name_, sizeof(name_), "CUDA%d", ordinal);
+    }
+    Device* device() const override;
+    const char* name() const override { return name_; }
+    size_t alignment() const override { return 256; }
+    Buffer* alloc_buffer(size_t size) override;
+
+private:
+    CudaDevice* dev_;
+    char        name_[16];
+};
+
+class CudaBuffer : public Buffer {
+public:
+    CudaBuffer(CudaBufferType* buft, int ordinal, char* dptr, size_t size)
+        : buft_(buft), ordinal_(ordinal), dptr_(dptr), size_(size) {}
+    ~CudaBuffer() override {
+        int prev = 0;
+        trc_cuda_rt_get_device(&prev);
+        trc_cuda_rt_set_device(ordinal_);
+        trc_cuda_rt_free(dptr_);
+        trc_cuda_rt_set_device(prev);
+    }
+    BufferType* buffer_type() const override { return buft_; }
+    size_t size() const override { return size_; }
+    void* base() override { return nullptr; }  // device-local: not mappable by the host
+    bool is_host() const override { return false; }
+
+    void set_tensor(Tensor* t, size_t offset, const void* data, size_t size) override {
+        check_range(t, offset, size, "set_tensor");
+        CB_CUDA(trc_cuda_rt_set_device(ordinal_));
+        CB_CUDA(trc_cuda_rt_memcpy(dptr_ + t->data_offset + offset, data, size, 0));
+    }
+    void get_tensor(const Tensor* t, size_t offset, void* data, size_t size) const override {
+        check_range(t, offset, size, "get_tensor");
+        CB_CUDA(trc_cuda_rt_set_device(ordinal_));
+        CB_CUDA(trc_cuda_rt_memcpy(data, dptr_ + t->data_offset + offset, size, 1));
+    }
+    void clear() override {
+        CB_CUDA(trc_cuda_rt_set_device(ordinal_));
+        CB_CUDA(trc_cuda_rt_memset(dptr_, 0, size_));
+    }
+
+    char* device_ptr() const { return dptr_; }
+    int   ordinal() const { return ordinal_; }
+
+private:
+    void check_range(const Tensor* t, size_t offset, size_t size, const char* what) const {
+        if (t->data_offset + offset + size > size_)
+            CB_ABORT("CudaBuffer::%s: 越界 (data_offset=%zu offset=%zu size=%zu buffer=%zu)", what, t->data_offset,
+                     offset, size, size_);
+    }
+
+    CudaBufferType* buft_;
+    int             ordinal_;
+    char*           dptr_;
+    size_t          size_;
+};
+
+// Root buffer of a tensor (views resolve through view_src: src/core/trc_backend_reg.cpp:61-67).
+CudaBuffer* cuda_buffer_of(const Tensor* t) {
+    while (t != nullptr && t->buffer == nullptr && t->view_src != nullptr) t = t->view_src;
+    if (t == nullptr || t->buffer == nullptr) return nullptr;
+    return dynamic_cast<CudaBuffer*>(t->buffer);
+}
+
+trc_cuda_view view_of(const Tensor* t) {
+    CudaBuffer* b = cuda_buffer_of(t);
+    if (b == nullptr) CB_ABORT("CUDA: 张量 %s 不在 CUDA buffer 上", t->name);
+    trc_cuda_view v;
+    v.data = b->device_ptr() + t->data_offset;
+    for (int i = 0; i < 4; ++i) {
+        v.ne[i] = t->ne[i];
+        v.nb[i] = static_cast<int64_t>(t->nb[i]);
+    }
+    return v;
+}
+
+bool all_f32(const Tensor* t) {
+    if (t->type != TYPE_F32) return false;
+    for (int i = 0; i < t->nsrc; ++i)
+        if (t->src[i] != nullptr && t->src[i]->type != TYPE_F32) return false;
+    return true;
+}
+
+class CudaDevice : public Device {
+public:
+    explicit CudaDevice(int ordinal) : ordinal_(ordinal), buft_(this, ordinal) {
+        char name[256];
+        int  major = 0, minor = 0;
+        CB_CUDA(trc_cuda_rt_device_info(ordinal, name, sizeof(name), &major, &minor));
+        CB_CUDA(trc_cuda_rt_set_device(ordinal));
+        CB_CUDA(trc_cuda_rt_stream_create(&stream_));
+        props_.name        = std::string("CUDA") + std::to_string(ordinal);
+        props_.description = std::string(name) + " (sm_" + std::to_string(major) + std::to_string(minor) +
+                             "a, tcgen05 3xTF32 mul_mat, device dequant)";
+        props_.type           = DeviceType::GPU;
+        props_.unified_memory = false;
+        refresh_memory();
+    }
+
+    const DeviceProps& props() const override {
+        const_cast<CudaDevice*>(this)->refresh_memory();
+        return props_;
+    }
+    BufferType* default_buffer_type() override { return &buft_; }
+
+    bool supports_op(const Tensor* t) const override {
+        if (t == nullptr) return false;
+        switch (t->op) {
+            case OP_NONE:
+            case OP_RESHAPE:
+            case OP_VIEW:
+            case OP_PERMUTE:
+            case OP_TRANSPOSE:
+                return true;  // leaves and views: nothing to compute
+            case OP_MUL_MAT:
+            case OP_SUM:
+            case OP_REPEAT:
+            case OP_ACC:
+                return all_f32(t);
+            case OP_CONT:
+            case OP_DUP:
+                return all_f32(t);
+            case OP_REPEAT_BACK:
+                return all_f32(t) && tensor_is_contiguous(t);
+            case OP_ADD:
+            case OP_SUB:
+            case OP_MUL:
+            case OP_DIV:
+                return all_f32(t) && t->src[1] != nullptr && tensor_can_repeat(t->src[1], t->src[0]);
+            default:
+                return false;
+        }
+    }
+
+    bool graph_compute(Graph* graph) override {
+        if (graph == nullptr) CB_ABORT("CudaDevice::graph_compute: graph 为空");
+        CB_CUDA(trc_cuda_rt_set_device(ordinal_));
+        plan_fusions(graph);
+        for (Tensor* node : graph->nodes) compute_node(node);
+        CB_CUDA(trc_cuda_rt_stream_sync(stream_));
+        int code = 0;
+        CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
+        if (code != 0) CB_ABORT("CUDA: kernel 等待超时（设备错误码 %d），结果无效", code);
+        return true;
+    }
+
+    bool fill_tensors(const TensorFill* fills, size_t count) override {
+        CB_CUDA(trc_cuda_rt_set_device(ordinal_));
+        for (size_t i = 0; i < count; ++i) {
+            Tensor* t = fills[i].tensor;
+            if (t == nullptr || t->type != TYPE_F32 || !tensor_is_contiguous(t))
+                CB_ABORT("fill_tensors: 仅支持连续 F32 张量");
+            const trc_cuda_view v = view_of(t);
+            CB_TRC(trc_cuda_fill(static_cast<float*>(v.data), tensor_nelements(t), fills[i].value, stream_),
+                   "trc_cuda_fill");
+        }
+        CB_CUDA(trc_cuda_rt_stream_sync(stream_));
+        return true;
+    }
+
+    int          ordinal() const { return ordinal_; }
+    void*        stream() const { return stream_; }
+
+    // Device scratch, grown on demand (sum partials, GGUF staging). Stream-ordered use only.
+    void* scratch(size_t bytes) {
+        if (bytes > scratch_bytes_) {
+            CB_CUDA(trc_cuda_rt_stream_sync(stream_));
+            if (scratch_ != nullptr) CB_CUDA(trc_cuda_rt_free(scratch_));
+            scratch_ = nullptr;
+            scratch_bytes_ = 0;
+            CB_CUDA(trc_cuda_rt_malloc(&scratch_, bytes));
+            scratch_bytes_ = bytes;
+        }
+        return scratch_;
+    }
+
+private:
+    void refresh_memory() {
+        size_t free_b = 0, total_b = 0;
+        int prev = 0;
+        trc_cuda_rt_get_device(&prev);
+        if (trc_cuda_rt_set_device(ordinal_) == TRC_CUDA_OK && trc_cuda_rt_mem_info(&free_b, &total_b) == TRC_CUDA_OK) {
+            props_.memory_free  = free_b;
+            props_.memory_total = total_b;
+        }
+        trc_cuda_rt_set_device(prev);
+    }
+
+    // ---------------------------------------------------------------- graph-level fusion
+    // The composed backward materialises dW as cont(transpose(mul_mat(...))) and adds it into the
+    // parameter's grad_acc with an in-place acc (src/core/trc_autograd.cpp:60-77, 487-503). When the
+    // intermediates have no other reader, the GEMM accumulates straight into grad_acc instead:
+    //   mul_mat M -> permute P -> cont C -> acc(inplace, whole grad_acc)   => one GEMM, D = T(grad_acc) (+=)
+    //   mul_mat M -> acc(inplace, whole grad_acc)                          => one GEMM, D = grad_acc (+=)
+    // Each output element then receives the same single fp32 add as in the unfused graph.
+    // TRC_CUDA_NO_FUSION=1 executes every node as written.
+    struct Fused {
+        const Tensor* acc_node;  // the acc that performs the fused work
+        bool          transposed;
+    };
+    std::unordered_map<const Tensor*, Fused> fused_gemm_;  // mul_mat node -> fusion
+    std::unordered_map<const Tensor*, bool>  skipped_;     // nodes whose work the fused GEMM does
+
+    void plan_fusions(Graph* g) {
+        fused_gemm_.clear();
+        skipped_.clear();
+        const char* off = std::getenv("TRC_CUDA_NO_FUSION");
+        if (off != nullptr && off[0] == '1') return;
+        std::unordered_map<const Tensor*, int> readers;
+        for (Tensor* n : g->nodes)
+            for (int i = 0; i < n->nsrc; ++i)
+                if (n->src[i] != nullptr) readers[n->src[i]]++;
+        auto private_to = [&](const Tensor* t) {
+            return readers[t] == 1 && (t->flags & (TENSOR_FLAG_OUTPUT | TENSOR_FLAG_PARAM | TENSOR_FLAG_LOSS)) == 0;
+        };
+        for (Tensor* n : g->nodes) {
+            if (n->op != OP_ACC || n->nsrc < 2 || n->op_params[4] == 0) continue;  // in-place acc only
+            const Tensor* G = n->src[0];
+            const Tensor* C = n->src[1];
+            if (!tensor_is_contiguous(G) || !tensor_are_same_shape(G, C) || n->op_params[3] != 0) continue;
+            if (static_cast<size_t>(n->op_params[0]) != G->nb[1] || static_cast<size_t>(n->op_params[1]) != G->nb[2] ||
+                static_cast<size_t>(n->op_params[2]) != G->nb[3])
+                continue;
+            if (C->op == OP_MUL_MAT && private_to(C)) {
+                fused_gemm_[C] = {n, false};
+                skipped_[n]    = true;
+            } else if (C->op == OP_CONT && private_to(C) && C->src[0] != nullptr && C->src[0]->op == OP_PERMUTE) {
+                const Tensor* P = C->src[0];
+                const Tensor* M = P->src[0];
+                const int*    ax = P->op_params;
+                if (M == nullptr || M->op != OP_MUL_MAT || !private_to(P) || !private_to(M)) continue;
+                if (!(ax[0] == 1 && ax[1] == 0 && ax[2] == 2 && ax[3] == 3)) continue;
+                fused_gemm_[M] = {n, true};
+                skipped_[C]    = true;
+                skipped_[n]    = true;
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- per-node execution
+    void compute_node(Tensor* t) {
+        if (skipped_.count(t) != 0) return;
+        switch (t->op) {
+            case OP_NONE:
+            case OP_RESHAPE:
+            case OP_VIEW:
+            case OP_PERMUTE:
+            case OP_TRANSPOSE:
+                return;
+            case OP_MUL_MAT: {
+                const trc_cuda_view a = view_of(t->src[0]), b = view_of(t->src[1]);
+                const auto it = fused_gemm_.find(t);
+                if (it == fused_gemm_.end()) {
+                    const trc_cuda_view d = view_of(t);
+                    CB_TRC(trc_cuda_mul_mat(&a, &b, &d, 0, stream_), "trc_cuda_mul_mat");
+                } else {
+                    trc_cuda_view d = view_of(it->second.acc_node->src[0]);  // grad_acc
+                    if (it->second.transposed) {  // D[i, j] lands on grad_acc[j, i]
+                        std::swap(d.ne[0], d.ne[1]);
+                        std::swap(d.nb[0], d.nb[1]);
+                    }
+                    CB_TRC(trc_cuda_mul_mat(&a, &b, &d, TRC_CUDA_MM_ACCUMULATE, stream_), "trc_cuda_mul_mat (fused acc)");
+                }
+                return;
+            }
+            case OP_ADD:
+            case OP_SUB:
+            case OP_MUL:
+            case OP_DIV: {
+                const int op = t->op == OP_ADD ? TRC_CUDA_BIN_ADD
+                             : t->op == OP_SUB ? TRC_CUDA_BIN_SUB
+                             : t->op == OP_MUL ? TRC_CUDA_BIN_MUL
+                                               : TRC_CUDA_BIN_DIV;
+                const trc_cuda_view a = view_of(t->src[0]), b = view_of(t->src[1]), d = view_of(t);
+                CB_TRC(trc_cuda_binary(op, &a, &b, &d, stream_), "trc_cuda_binary");
+                return;
+            }
+            case OP_SUM: {
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                const size_t ws = trc_cuda_sum_workspace_bytes(tensor_nelements(t->src[0]));
+                CB_TRC(trc_cuda_sum(&a, static_cast<float*>(d.data), scratch(ws), ws, stream_), "trc_cuda_sum");
+                return;
+            }
+            case OP_REPEAT: {
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                CB_TRC(trc_cuda_repeat(&a, &d, stream_), "trc_cuda_repeat");
+                return;
+            }
+            case OP_REPEAT_BACK: {
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                CB_TRC(trc_cuda_repeat_back(&a, &d, stream_), "trc_cuda_repeat_back");
+                return;
+            }
+            case OP_CONT:
+            case OP_DUP: {
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                CB_TRC(trc_cuda_cont(&a, &d, stream_), "trc_cuda_cont");
+                return;
+            }
+            case OP_ACC: {
+                // op_params: int32 nb1, nb2, nb3, offset, inplace (src/core/trc_tensor.cpp:353-358)
+                const int32_t* p = t->op_params;
+                const trc_cuda_view b = view_of(t->src[1]);
+                const trc_cuda_view d = view_of(t);
+                if (p[4] == 0) {  // not in place: dst = a, then the region += b
+                    const trc_cuda_view a = view_of(t->src[0]);
+                    CB_TRC(trc_cuda_cont(&a, &d, stream_), "trc_cuda_cont (acc copy)");
+                }
+                CB_TRC(trc_cuda_acc(d.data, static_cast<int64_t>(tensor_nbytes(t)), &b, p[0], p[1], p[2], p[3], stream_),
+                       "trc_cuda_acc");
+                return;
+            }
+            default:
+                CB_ABORT("CUDA: 不支持的算子 %s（张量 %s）；请先用 graph_first_unsupported 预检", op_name(t->op),
+                         t->name);
+        }
+    }
+
+    int            ordinal_;
+    CudaBufferType buft_;
+    DeviceProps    props_;
+    void*          stream_ = nullptr;
+    void*          scratch_ = nullptr;
+    size_t         scratch_bytes_ = 0;
+};
+
+Device* CudaBufferType::device() const { return dev_; }
+
+Buffer* CudaBufferType::alloc_buffer(size_t size) {
+    if (fake_alloc_failure()) return nullptr;
+    const int ordinal = static_cast<CudaDevice*>(dev_)->ordinal();
+    if (trc_cuda_rt_set_device(ordinal) != TRC_CUDA_OK) return nullptr;
+    void* p = nullptr;
+    if (trc_cuda_rt_malloc(&p, size) != TRC_CUDA_OK) return nullptr;
+    return new CudaBuffer(this, ordinal, static_cast<char*>(p), size);
+}
+
+std::mutex& registry_mutex() {
+    static std::mutex mu;
+    return mu;
+}
+
+std::vector<std::unique_ptr<CudaDevice>>& devices() {
+    static std::vector<std::unique_ptr<CudaDevice>> d;
+    return d;
+}
+
+bool is_legacy_quant(Type t) {
+    return t == TYPE_Q4_0 || t == TYPE_Q4_1 || t == TYPE_Q5_0 || t == TYPE_Q5_1 || t == TYPE_Q8_0;
+}
+
+}  // namespace
+
+int cuda_device_count() {
+    int n = 0;
+    if (trc_cuda_rt_device_count(&n) != TRC_CUDA_OK) return 0;
+    return n;
+}
+
+Device* cuda_device(int ordinal) {
+    std::lock_guard<std::mutex> lock(registry_mutex());
+    const int n = cuda_device_count();
+    if (ordinal < 0 || ordinal >= n) return nullptr;
+    auto& d = devices();
+    if (d.size() < static_cast<size_t>(n)) d.resize(static_cast<size_t>(n));
+    if (!d[ordinal]) d[ordinal] = std::make_unique<CudaDevice>(ordinal);
+    return d[ordinal].get();
+}
+
+int cuda_register_devices() {
+    static std::mutex mu;
+    static int        registered = -1;
+    std::lock_guard<std::mutex> lock(mu);
+    if (registered >= 0) return registered;
+    registered = 0;
+    for (int i = 0; i < cuda_device_count(); ++i) {
+        if (Device* d = cuda_device(i)) {
+            backend_register_device(d);
+            ++registered;
+        }
+    }
+    return registered;
+}
+
+bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name, Tensor* dst) {
+    if (f == nullptr || path == nullptr || name == nullptr || dst == nullptr)
+        CB_ABORT("cuda_gguf_load_tensor: 参数为空");
+    const int64_t ti = gguf_find_tensor(f, name);
+    if (ti < 0) {
+        std::fprintf(stderr, "[traincpp] GGUF: 张量不存在 %s\n", name);
+        return false;
+    }
+    const GgufTensorInfo* info = gguf_tensor_info(f, ti);
+    CudaBuffer* buf = cuda_buffer_of(dst);
+    if (!is_legacy_quant(info->type) || dst->type != TYPE_F32 || buf == nullptr)
+        return gguf_load_tensor(f, name, dst);  // the reference path (also reports its errors)
+    // the reference's destination checks (src/io/trc_gguf.cpp:1060-1076)
+    if (!tensor_is_contiguous(dst)) {
+        std::fprintf(stderr, "[traincpp] GGUF: 目标张量 %s 必须连续\n", name);
+        return false;
+    }
+    if (tensor_nelements(dst) != gguf_tensor_nelements(f, ti)) {
+        std::fprintf(stderr, "[traincpp] GGUF: 张量 %s 元素数不匹配\n", name);
+        return false;
+    }
+    const int64_t n_blocks = gguf_tensor_nelements(f, ti) / 32;
+    const size_t  bytes    = info->nbytes;
+    FILE* fp = std::fopen(path, "rb");
+    if (fp == nullptr) {
+        std::fprintf(stderr, "[traincpp] GGUF: 无法打开 %s\n", path);
+        return false;
+    }
+    void* host = nullptr;
+    CB_CUDA(trc_cuda_rt_set_device(buf->ordinal()));
+    CB_CUDA(trc_cuda_rt_malloc_host(&host, bytes));
+    const long pos = static_cast<long>(gguf_data_offset(f) + info->offset);
+    const bool ok = std::fseek(fp, pos, SEEK_SET) == 0 && std::fread(host, 1, bytes, fp) == bytes;
+    std::fclose(fp);
+    if (!ok) {
+        trc_cuda_rt_free_host(host);
+        std::fprintf(stderr, "[traincpp] GGUF: 张量 %s 数据越界\n", name);
+        return false;
+    }
+    CudaDevice* dev = static_cast<CudaDevice*>(buf->buffer_type()->device());
+    void* staging = dev->scratch((bytes + 15) / 16 * 16);
+    float* out = reinterpret_cast<float*>(buf->device_ptr() + dst->data_offset);
+    CB_TRC(trc_cuda_load_quant(static_cast<int>(info->type), host, n_blocks, staging, out, dev->stream()),
+           "trc_cuda_load_quant");
+    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
+    CB_CUDA(trc_cuda_rt_free_host(host));
+    int code = 0;
+    CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
+    if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
+    return true;
+}
+
+}  // namespace traincpp
+
+extern "C" int trc_cuda_backend_register(void) { return traincpp::cuda_register_devices(); }
+
+extern "C" void* trc_cuda_backend_device(int ordinal) { return traincpp::cuda_device(ordinal); }

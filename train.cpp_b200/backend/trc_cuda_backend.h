@@ -1,0 +1,42 @@
+// trc_cuda_backend.h -- CUDA (B200, sm_100a) backend for train.cpp, behind its abstract backend
+// interface (include/traincpp/trc_backend.h:33-88). Drop-in: the GGUF reader, op constructors,
+// autograd, graph_first_unsupported and graph_compute callers stay unchanged; this file only adds
+// a Device / BufferType / Buffer implementation whose kernels live in libtrc_cuda.so
+// (include/trc_cuda.h).
+//
+// Registration mirrors the reference's backend entry points (src/core/trc_backends.h:14-22):
+// cuda_device(i) returns the process-lifetime device of GPU i; cuda_register_devices() appends every
+// visible GPU to the registry with backend_register_device() (src/core/trc_backend_reg.cpp:89-92),
+// after which device_by_type(DeviceType::GPU) and TRC_TEST_DEVICE-style selection find it.
+#pragma once
+
+#include "traincpp/traincpp.h"
+
+#include <cstddef>
+#include <cstdint>
+
+namespace traincpp {
+
+// Number of CUDA devices visible to the process (0 when no driver/GPU is present).
+int cuda_device_count();
+
+// The CUDA device for GPU `ordinal` (created on first use), or nullptr if there is no such GPU.
+Device* cuda_device(int ordinal = 0);
+
+// Registers every visible GPU with the backend registry (idempotent). Returns how many are registered.
+int cuda_register_devices();
+
+// Device-side gguf_load_tensor (src/io/trc_gguf.cpp:1051-1094) for a quantized file tensor and an F32
+// destination allocated on a CUDA buffer: the packed blocks are read from `path` into pinned host
+// staging, copied to the device (4-8x fewer bytes than the F32 result) and dequantized there,
+// bit-exact with the reference. Non-quantized file types and non-CUDA destinations fall back to
+// the reference's own gguf_load_tensor. Returns false (and logs) where the reference would.
+bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name, Tensor* dst);
+
+}  // namespace traincpp
+
+extern "C" {
+// C entry points of the backend library, for hosts that do not link C++ (ctypes, cgo, ...).
+int trc_cuda_backend_register(void);
+void* trc_cuda_backend_device(int ordinal);
+}

@@ -21,7 +21,7 @@ LIB = PKG / "lib"
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["capi.cu", "dequant.cu", "elementwise.cu", "mul_mat_simt.cu", "gemm_tf32x3.cu"]
+CU_SOURCES = ["capi.cu", "runtime.cu", "dequant.cu", "elementwise.cu", "mul_mat_simt.cu", "gemm_tf32x3.cu"]
 
 
 def _run(cmd: list[str], log: Path | None = None) -> None:
@@ -45,7 +45,7 @@ def build_cuda(force: bool = False) -> Path:
     LIB.mkdir(exist_ok=True)
     out = LIB / "libtrc_cuda.so"
     deps = [CSRC / s for s in CU_SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
-    deps.append(ROOT / "include" / "trc_cuda.h")
+    deps += [ROOT / "include" / "trc_cuda.h", ROOT / "include" / "trc_cuda_runtime.h"]
     if not force and not _stale(out, deps):
         return out
     cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-rdc=true", "-shared",
@@ -68,7 +68,8 @@ def build_backend(force: bool = False) -> Path | None:
         return out if out.exists() else None
     cuda_lib = build_cuda()
     src = PKG / "backend" / "trc_cuda_backend.cpp"
-    deps = [src, PKG / "backend" / "trc_cuda_backend.h", ROOT / "include" / "trc_cuda.h", cuda_lib]
+    deps = [src, PKG / "backend" / "trc_cuda_backend.h", ROOT / "include" / "trc_cuda.h",
+            ROOT / "include" / "trc_cuda_runtime.h", cuda_lib]
     if not force and not _stale(out, deps):
         return out
     cuda_inc = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"

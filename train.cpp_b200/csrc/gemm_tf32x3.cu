@@ -9,16 +9,27 @@
 // into a head h = x with the low 13 mantissa bits cleared (what the tensor core reads from the raw
 // fp32 word) and a tail t = x - h (exact in fp32). Per K-step the kernel issues
 //     D += tA * hB,   D += hA * tB,   D += hA * hB
-// into one fp32 TMEM accumulator; only tA*tB (relative size 2^-22) is dropped. Measured against the
-// reference this stays within 1e-5 normwise, where a single TF32 pass is ~3e-4.
+// into an fp32 TMEM accumulator; only tA*tB (relative size 2^-22) is dropped. Measured on B200
+// against a float64 product: 2.3e-6 normwise at every K from 256 to 14336, which keeps the result
+// within 1e-5 normwise of the reference CPU (itself 2.4e-6..4.4e-6 from exact at these K).
+//
+// fp32 promotion. The tensor core's fp32 accumulation does not round to nearest: measured on B200,
+// the error of one long accumulation grows linearly with K (3.6e-5 normwise at K = 4096). So the
+// K loop is cut into chunks of CHUNK_KB k-blocks (256 K); each chunk accumulates from zero in TMEM
+// and the epilogue warps add it to the tile's running total with IEEE round-to-nearest fp32 adds.
+// The two 256-column TMEM buffers swap roles per tile (running total T / chunk X), so the tile
+// double buffering survives: tile i keeps its total in buffer i%2 and its chunks in buffer
+// (i+1)%2, and tile i+1's first chunk can start while tile i's total is being stored.
 //
 // Structure (one persistent CTA per SM, 12 warps):
 //   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (4-stage ring, 64-byte swizzle)
 //   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
 //   warps 2-7   split warpgroup: writes the tails tA, tB of each stage next to the raw tiles
 //   warps 8-11  epilogue: TMEM -> registers (tcgen05.ld) -> strided global stores (ggml nb[])
-// Tile 128 (M, TMEM lanes) x 256 (N) x 16 (K) per stage; two 256-column fp32 accumulators in TMEM
-// (all 512 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+// Tile 128 (M, TMEM lanes) x 256 (N) x 16 (K) per stage; two 256-column fp32 TMEM buffers (all 512
+// columns). Shared-memory operand layouts: K-major tiles use the 64-byte swizzle (64 B rows);
+// MN-major tiles use the 128-byte swizzle with 32-byte atoms, the one layout tcgen05 accepts for
+// MN-major TF32 operands (32-element MN chunks of 16 K-rows x 128 B).
 // Every mbarrier wait is bounded (trc_ptx.cuh); a timeout sets the device error word and the kernel
 // drains its in-flight copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -47,6 +58,7 @@ constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers p
 constexpr int NUM_THREADS  = 384;
 constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 6, EPI_WARP0 = 8;
 constexpr int TMEM_COLS    = 512;
+constexpr int CHUNK_KB     = 16;   // k-blocks per fp32 promotion chunk (256 K)
 constexpr int SMEM_BYTES   = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 struct TcParams {
@@ -102,9 +114,11 @@ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile)
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
     return make_smem_desc(tile + kk * 32, 16, 512, 4);
 }
-// MN-major tile (16-element MN chunks of 16 K-rows x 64 B = 1 KiB): advance 512 B (8 K-rows) per K=8.
+// MN-major tile (32-element MN chunks of 16 K-rows x 128 B = 2 KiB, 128B swizzle with 32B atoms,
+// descriptor layout type 1): LBO = 2 KiB between MN chunks, SBO = 512 B between 4-row K groups,
+// advance 1 KiB (8 K-rows) per K=8.
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
-    return make_smem_desc(tile + kk * 512, 1024, 512, 4);
+    return make_smem_desc(tile + kk * 1024, 2048, 512, 1);
 }
 
 // Tail of one 16-byte chunk of a raw tile (index i < nA: A tile, else B tile).
@@ -172,9 +186,11 @@ __device__ __forceinline__ void decode_a_stage(const TcParams& p, int m0, int k0
 #pragma unroll
             for (int e = 0; e < 16; ++e) w[e] = 0.0f;
         }
-        const int cm = 2 * j + h;  // 16-element MN chunk
+        // 32-element MN chunk j, K-row kr (128 B); the 16 weights fill 32-byte units 2h and 2h+1,
+        // swizzled by (kr & 3).
 #pragma unroll
-        for (int u = 0; u < 4; ++u) off[u] = cm * 1024 + kr * 64 + ((u ^ ((kr >> 1) & 3)) << 4);
+        for (int u = 0; u < 4; ++u)
+            off[u] = j * 2048 + kr * 128 + (((2 * h + (u >> 1)) ^ (kr & 3)) << 5) + ((u & 1) << 4);
     }
     store_head_tail16(st, w, off);
 }
@@ -237,8 +253,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             tma_load_4d(st + OFF_A_RAW, &tmA, &bars->full[s], k0, tc.m0, a2, a3);
                         } else {
 #pragma unroll
-                            for (int c = 0; c < BM / 16; ++c)
-                                tma_load_4d(st + OFF_A_RAW + c * 1024, &tmA, &bars->full[s], tc.m0 + 16 * c, k0, a2,
+                            for (int c = 0; c < BM / 32; ++c)
+                                tma_load_4d(st + OFF_A_RAW + c * 2048, &tmA, &bars->full[s], tc.m0 + 32 * c, k0, a2,
                                             a3);
                         }
                     }
@@ -246,8 +262,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_4d(st + OFF_B_RAW, &tmB, &bars->full[s], k0, tc.n0, b2, b3);
                     } else {
 #pragma unroll
-                        for (int c = 0; c < BN / 16; ++c)
-                            tma_load_4d(st + OFF_B_RAW + c * 1024, &tmB, &bars->full[s], tc.n0 + 16 * c, k0, b2, b3);
+                        for (int c = 0; c < BN / 32; ++c)
+                            tma_load_4d(st + OFF_B_RAW + c * 2048, &tmB, &bars->full[s], tc.n0 + 32 * c, k0, b2, b3);
                     }
                 }
             }
@@ -260,32 +276,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- UMMA issuer
         if (lane == 0) {
             const uint32_t idesc = make_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
-            uint32_t it = 0, tcount = 0;
+            uint32_t it = 0, tcount = 0, uses[2] = {0u, 0u};
             bool ok = true;
             for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
-                const int ab = tcount & 1;
-                if (!mbar_wait(&bars->acc_empty[ab], ((tcount >> 1) & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + ab * BN;
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    if (!mbar_wait(&bars->split[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t st = smem_base + s * STAGE_BYTES;
-#pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + OFF_A_RAW, kk) : desc_kmajor(st + OFF_A_RAW, kk);
-                        const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + OFF_A_TAIL, kk) : desc_kmajor(st + OFF_A_TAIL, kk);
-                        const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + OFF_B_RAW, kk) : desc_kmajor(st + OFF_B_RAW, kk);
-                        const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + OFF_B_TAIL, kk) : desc_kmajor(st + OFF_B_TAIL, kk);
-                        umma_tf32(d_tmem, a_tail, b_raw, idesc, (kb | kk) != 0 ? 1u : 0u);
-                        umma_tf32(d_tmem, a_raw, b_tail, idesc, 1u);
-                        umma_tf32(d_tmem, a_raw, b_raw, idesc, 1u);
+                const int tb = tcount & 1;  // this tile's running-total buffer; chunks >= 1 use tb ^ 1
+                for (int kb0 = 0; kb0 < p.k_blocks && ok; kb0 += CHUNK_KB) {
+                    const int b = kb0 == 0 ? tb : tb ^ 1;
+                    if (!mbar_wait(&bars->acc_empty[b], (uses[b] & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
+                        ok = false;
+                        break;
                     }
-                    umma_commit(&bars->empty[s]);  // frees the stage once these MMAs have read it
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + b * BN;
+                    const int kb1 = min(p.k_blocks, kb0 + CHUNK_KB);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const int s = it % STAGES;
+                        if (!mbar_wait(&bars->split[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t st = smem_base + s * STAGE_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + OFF_A_RAW, kk) : desc_kmajor(st + OFF_A_RAW, kk);
+                            const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + OFF_A_TAIL, kk) : desc_kmajor(st + OFF_A_TAIL, kk);
+                            const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + OFF_B_RAW, kk) : desc_kmajor(st + OFF_B_RAW, kk);
+                            const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + OFF_B_TAIL, kk) : desc_kmajor(st + OFF_B_TAIL, kk);
+                            umma_tf32(d_tmem, a_tail, b_raw, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            umma_tf32(d_tmem, a_raw, b_tail, idesc, 1u);
+                            umma_tf32(d_tmem, a_raw, b_raw, idesc, 1u);
+                        }
+                        umma_commit(&bars->empty[s]);  // frees the stage once these MMAs have read it
+                    }
+                    if (!ok) break;
+                    umma_commit(&bars->acc_full[b]);  // this chunk is complete in TMEM buffer b
+                    ++uses[b];
                 }
-                if (!ok) break;
-                umma_commit(&bars->acc_full[ab]);
             }
             // All MMAs of this thread must be complete before TMEM is released.
             umma_commit(&bars->mma_done);
@@ -336,23 +363,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue
+        // Per tile: chunk 0 lands in buffer tb (the running total T), every further chunk in tb^1 (X)
+        // and is added into T with round-to-nearest fp32 adds; the final sum goes to global memory.
         const int q = warp - EPI_WARP0;  // TMEM lane quarter this warp may access
         const int row = q * 32 + lane;
-        uint32_t tcount = 0;
-        for (int64_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++tcount) {
-            const int ab = tcount & 1;
-            if (!mbar_wait(&bars->acc_full[ab], (tcount >> 1) & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
-            tc_fence_after();
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        uint32_t tcount = 0, uses[2] = {0u, 0u};
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+            const int tb = tcount & 1, xb = tb ^ 1;
             const TileCoord tc = tile_coord(p, tile);
             const int m = tc.m0 + row;
             char* drow = p.d + static_cast<int64_t>(tc.p2) * p.d_s2 + static_cast<int64_t>(tc.p3) * p.d_s3 +
                          static_cast<int64_t>(m) * p.d_sm;
             const int n_valid = min(BN, p.N - tc.n0);
+            const int n_groups = (n_valid + 31) / 32;  // uniform across the warp
+            const uint32_t t_addr = tmem_base + lane_off + tb * BN;
+            const uint32_t x_addr = tmem_base + lane_off + xb * BN;
+            if (!mbar_wait(&bars->acc_full[tb], uses[tb] & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
+            ++uses[tb];
+            tc_fence_after();
+            for (int kb0 = CHUNK_KB; kb0 < p.k_blocks; kb0 += CHUNK_KB) {
+                if (!mbar_wait(&bars->acc_full[xb], uses[xb] & 1u, TRC_DEVERR_WAIT_ACCUM)) { ok = false; break; }
+                ++uses[xb];
+                tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                if (c * 32 >= n_valid) break;  // uniform across the warp
+                for (int c = 0; c < n_groups; ++c) {
+                    uint32_t x[32], t[32];
+                    tmem_ld_32x32b_x32(x_addr + c * 32, x);
+                    tmem_ld_32x32b_x32(t_addr + c * 32, t);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__fadd_rn(__uint_as_float(t[e]), __uint_as_float(x[e])));
+                    tmem_st_32x32b_x32(t_addr + c * 32, t);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->acc_empty[xb]);  // chunk buffer free for the next chunk
+            }
+            if (!ok) break;
+#pragma unroll 1
+            for (int c = 0; c < n_groups; ++c) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * BN + c * 32, r);
+                tmem_ld_32x32b_x32(t_addr + c * 32, r);
                 tmem_ld_wait();
                 if (m < p.M) {
 #pragma unroll
@@ -368,7 +422,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty[ab]);
+            if (lane == 0) mbar_arrive(&bars->acc_empty[tb]);
         }
     }
 
@@ -414,7 +468,7 @@ bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtens
         mn_major = true;
         dims[0] = R; dims[1] = K;
         strides[0] = K == 1 ? static_cast<cuuint64_t>((R * 4 + 15) / 16 * 16) : v.nb[0];
-        box[0] = 16; box[1] = BK;
+        box[0] = 32; box[1] = BK;
     } else {
         return false;
     }
@@ -440,7 +494,8 @@ bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtens
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return false;
     const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.data, dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
