@@ -88,20 +88,11 @@ def llama7b_tensors() -> list[tuple[str, int, tuple[int, int]]]:
     return t
 
 
-def lpt_shards(sizes: Iterable[int], n_shards: int) -> list[list[int]]:
-    """Greedy longest-processing-time partition of item indices into n_shards by size (bytes):
-    each item, largest first, goes to the currently lightest shard. Deterministic (ties by index)."""
-    sizes = list(sizes)
-    order = sorted(range(len(sizes)), key=lambda i: (-sizes[i], i))
-    loads = [0] * n_shards
-    shards: list[list[int]] = [[] for _ in range(n_shards)]
-    for i in order:
-        s = min(range(n_shards), key=lambda k: (loads[k], k))
-        shards[s].append(i)
-        loads[s] += sizes[i]
-    for s in shards:
-        s.sort()
-    return shards
+def lpt_shards(sizes, n_shards: int):
+    """Byte-balanced tensor partition (see sharding.lpt_shards)."""
+    from sharding import lpt_shards as _lpt
+
+    return _lpt(list(sizes), n_shards)
 
 
 # ------------------------------------------------------------------ GGUF v3 writer
