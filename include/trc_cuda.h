@@ -38,7 +38,8 @@ enum {
     TRC_CUDA_EUNSUPPORTED = -2, /* element type or layout this library does not compute */
     TRC_CUDA_EDEVICE      = -3, /* a kernel hit its wait limit; see trc_cuda_device_error() */
     TRC_CUDA_ECUDA        = -4, /* a CUDA runtime call failed; see trc_cuda_last_cuda_error() */
-    TRC_CUDA_ENOMEM       = -5  /* a device allocation failed */
+    TRC_CUDA_ENOMEM       = -5, /* a device allocation failed */
+    TRC_CUDA_ETOOBIG      = -6  /* larger than the fixed static buffer of an allocation-free entry point */
 };
 
 /* ggml / GGUF type ids of the legacy quantized blocks (include/traincpp/trc_types.h:11-49). */
@@ -115,6 +116,24 @@ int trc_cuda_dequant_many(const trc_cuda_dequant_job* jobs, int n_jobs, void* st
  * F32 result). Pinned host memory makes the copy asynchronous; pageable memory is also accepted. */
 int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
                         void* stream);
+
+/* Allocation-free variant of trc_cuda_load_quant, for callers that cannot call cudaMalloc: code
+ * that must not grow device memory (a process whose device memory is owned by another allocator or
+ * has a fixed budget, or a loader running while other work owns the allocator). It needs no
+ * caller staging buffer: the packed blocks are staged in a fixed array inside the library, a
+ * file-scope static __device__ array of TRC_CUDA_STATIC_STAGING_BYTES (64 MiB) that every GPU
+ * which loads the library holds until the process exits. The call itself allocates nothing and
+ * calls no allocating routine.
+ *   - Tensors whose packed bytes exceed TRC_CUDA_STATIC_STAGING_BYTES are rejected with
+ *     TRC_CUDA_ETOOBIG before any device work.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) for
+ *     that device; make that first call before any stream capture begins.
+ *   - All calls share the one array per device and it keeps the last call's bytes; each call
+ *     overwrites the bytes it uses before reading them, so nothing needs clearing. Calls whose
+ *     copies or kernels overlap on the GPU (different streams without ordering) race on the array.
+ * This entry point has no counterpart in the reference, which dequantizes on the host. */
+#define TRC_CUDA_STATIC_STAGING_BYTES ((size_t) 64 << 20)
+int trc_cuda_load_quant_static(int type, const void* host_blocks, int64_t n_blocks, float* out, void* stream);
 
 /* ------------------------------------------------------------------ mul_mat */
 

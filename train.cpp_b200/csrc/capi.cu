@@ -57,6 +57,7 @@ const char* trc_cuda_status_string(int status) {
         case TRC_CUDA_EDEVICE: return "a kernel hit its wait limit (device error word set)";
         case TRC_CUDA_ECUDA: return "CUDA runtime error";
         case TRC_CUDA_ENOMEM: return "device allocation failed";
+        case TRC_CUDA_ETOOBIG: return "tensor larger than the fixed 64 MiB static staging buffer";
         default: return "unknown status";
     }
 }

@@ -77,6 +77,7 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_dequant": (I, [I, P, I64, P, P]),
         "trc_cuda_dequant_many": (I, [ctypes.POINTER(DequantJob), I, P]),
         "trc_cuda_load_quant": (I, [I, P, I64, P, P, P]),
+        "trc_cuda_load_quant_static": (I, [I, P, I64, P, P]),
         "trc_cuda_mul_mat": (I, [VP, VP, VP, U32, P]),
         "trc_cuda_mul_mat_q": (I, [I, P, I64, I64, I, VP, VP, U32, P]),
         "trc_cuda_mul_mat_kernel": (I, [VP, VP, VP, U32]),
@@ -206,6 +207,25 @@ def gguf_load_tensor(qtype: int, host_blocks, dst: torch.Tensor, staging: torch.
         raise TrcCudaError("host or staging buffer smaller than the tensor")
     _check(lib().trc_cuda_load_quant(qtype, ctypes.c_void_p(ptr), n_blocks, staging.data_ptr(), dst.data_ptr(),
                                      _stream(stream)), "trc_cuda_load_quant")
+
+
+STATIC_STAGING_BYTES = 64 << 20
+ETOOBIG = -6
+
+
+def gguf_load_tensor_static(qtype: int, host_blocks, dst: torch.Tensor, stream=None) -> None:
+    """gguf_load_tensor without a staging buffer and without any allocation: the packed bytes are
+    staged in the library's fixed 64 MiB device array (for callers that cannot allocate device
+    memory). Tensors larger than that are rejected; calls overlapping on the GPU race on the array."""
+    if isinstance(host_blocks, torch.Tensor):
+        ptr, nbytes = host_blocks.data_ptr(), host_blocks.numel() * host_blocks.element_size()
+    else:
+        ptr, nbytes = host_blocks.ctypes.data, host_blocks.nbytes
+    n_blocks = dst.numel() // QK
+    if nbytes < n_blocks * block_bytes(qtype):
+        raise TrcCudaError("host buffer smaller than the tensor")
+    _check(lib().trc_cuda_load_quant_static(qtype, ctypes.c_void_p(ptr), n_blocks, dst.data_ptr(), _stream(stream)),
+           "trc_cuda_load_quant_static")
 
 
 # ------------------------------------------------------------------ mul_mat
