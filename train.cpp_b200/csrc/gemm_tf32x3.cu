@@ -59,7 +59,10 @@ constexpr int NUM_THREADS  = 384;
 constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 6, EPI_WARP0 = 8;
 constexpr int TMEM_COLS    = 512;
 constexpr int CHUNK_KB     = 16;   // k-blocks per fp32 promotion chunk (256 K)
-constexpr int SMEM_BYTES   = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128-row x 32-column fp32 group of D, staged for a TMA store
+constexpr int EPI_BUFS      = 2;
+constexpr int EPI_OFF       = STAGES * STAGE_BYTES;
+constexpr int SMEM_BYTES    = STAGES * STAGE_BYTES + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 struct TcParams {
     int     M, N, K;           // M: TMEM lanes (rows of D tiles), N: columns, K: reduction
@@ -71,6 +74,7 @@ struct TcParams {
     int64_t total_tiles;
     char*   d;
     int64_t d_sm, d_sn, d_s2, d_s3;  // byte strides of D along M, N, plane2, plane3
+    int     tma_store;               // 1: D is written (or reduce-added) by TMA from shared memory
     // quantized A (fused variant): packed blocks of the weight W, rows of q_row_bytes bytes
     const uint8_t* qa;
     int64_t        q_row_bytes;
@@ -154,45 +158,41 @@ __device__ __forceinline__ void store_head_tail16(uint8_t* st, const float (&w)[
     }
 }
 
-// A-stage decode for the fused dequant GEMM (thread t of 128). The stage covers A rows m0..m0+127
-// and K columns k0..k0+15, i.e. one half (16 weights) of a 32-weight block per W row (QTRANS = 0)
-// or 16 W rows x 4 blocks (QTRANS = 1). Out-of-range weights are written as zeros.
+// A-stage decode for the fused dequant GEMM (thread t of 128). A stage covers A rows m0..m0+127
+// and K columns k0..k0+15: one half (16 weights) of a 32-weight block per W row (QTRANS = 0,
+// K-major) or 16 W rows x 4 blocks (QTRANS = 1, MN-major). a_stage_block() says where thread t's
+// 16 weights come from (nullptr: out of range, written as zeros); a_stage_offsets() where they go.
 template <int QTYPE, int QTRANS>
-__device__ __forceinline__ void decode_a_stage(const TcParams& p, int m0, int k0, int t, uint8_t* st) {
+__device__ __forceinline__ const uint8_t* a_stage_block(const TcParams& p, int m0, int k0, int t, int& half) {
     constexpr int BB = QuantTraits<QTYPE>::kBytes;
-    float w[16];
-    int   off[4];
     if constexpr (QTRANS == 0) {
-        // K-major: row r = t (W row m0 + r), weights k0..k0+15 = half (k0/16)&1 of block k0/32.
-        const int r = t, m = m0 + r;
-        const int half = (k0 >> 4) & 1;
-        if (m < p.M && k0 < p.K) {
-            const uint8_t* blk = p.qa + static_cast<int64_t>(m) * p.q_row_bytes + static_cast<int64_t>(k0 >> 5) * BB;
-            decode_half<QTYPE>(blk, half, w);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) w[e] = 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) off[u] = r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+        const int m = m0 + t;
+        half = (k0 >> 4) & 1;
+        if (m < p.M && k0 < p.K) return p.qa + static_cast<int64_t>(m) * p.q_row_bytes + static_cast<int64_t>(k0 >> 5) * BB;
     } else {
-        // MN-major: K-row kr = t/8 (W row k0 + kr), block j = (t/2)%4 (weights m0 + 32j ..), half h.
-        const int kr = t >> 3, j = (t >> 1) & 3, h = t & 1;
+        const int kr = t >> 3, j = (t >> 1) & 3;
+        half = t & 1;
         const int wrow = k0 + kr, m = m0 + 32 * j;
-        if (wrow < p.K && m < p.M) {
-            const uint8_t* blk = p.qa + static_cast<int64_t>(wrow) * p.q_row_bytes + static_cast<int64_t>(m >> 5) * BB;
-            decode_half<QTYPE>(blk, h, w);
-        } else {
+        if (wrow < p.K && m < p.M) return p.qa + static_cast<int64_t>(wrow) * p.q_row_bytes + static_cast<int64_t>(m >> 5) * BB;
+    }
+    return nullptr;
+}
+
+// Swizzled byte offsets of thread t's four 16-byte chunks (4 weights each) in the stage's A tiles.
+template <int QTRANS>
+__device__ __forceinline__ void a_stage_offsets(int t, int (&off)[4]) {
+    if constexpr (QTRANS == 0) {
+        // K-major, 64-byte rows: row t, chunk u at unit u ^ ((t >> 1) & 3)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) w[e] = 0.0f;
-        }
-        // 32-element MN chunk j, K-row kr (128 B); the 16 weights fill 32-byte units 2h and 2h+1,
-        // swizzled by (kr & 3).
+        for (int u = 0; u < 4; ++u) off[u] = t * 64 + ((u ^ ((t >> 1) & 3)) << 4);
+    } else {
+        // MN-major, 32-element chunks of 16 K-rows x 128 B: chunk j, K-row kr; the 16 weights fill
+        // 32-byte units 2h and 2h+1, swizzled by (kr & 3)
+        const int kr = t >> 3, j = (t >> 1) & 3, h = t & 1;
 #pragma unroll
         for (int u = 0; u < 4; ++u)
             off[u] = j * 2048 + kr * 128 + (((2 * h + (u >> 1)) ^ (kr & 3)) << 5) + ((u & 1) << 4);
     }
-    store_head_tail16(st, w, off);
 }
 
 // QTYPE = 0: A is an F32 view loaded by TMA. QTYPE = ggml Q-type: A is decoded from packed blocks by
@@ -200,10 +200,10 @@ __device__ __forceinline__ void decode_a_stage(const TcParams& p, int m0, int k0
 template <int QTYPE, int QTRANS>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ TcParams p) {
+                       const __grid_constant__ CUtensorMap tmD, const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + EPI_OFF + EPI_BUFS * EPI_BUF_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         fence_barrier_init();
         if (QTYPE == 0) prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (p.tma_store) prefetch_tmap(&tmD);
     }
     if (warp == 1) {
         tmem_alloc(&bars->tmem_slot, TMEM_COLS);
@@ -276,13 +277,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- UMMA issuer
         if (lane == 0) {
             const uint32_t idesc = make_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
-            uint32_t it = 0, tcount = 0, uses[2] = {0u, 0u};
+            // uses0/uses1: chunks committed so far into TMEM buffer 0/1 (scalars, kept in registers)
+            uint32_t it = 0, tcount = 0, uses0 = 0, uses1 = 0;
             bool ok = true;
             for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
                 const int tb = tcount & 1;  // this tile's running-total buffer; chunks >= 1 use tb ^ 1
                 for (int kb0 = 0; kb0 < p.k_blocks && ok; kb0 += CHUNK_KB) {
                     const int b = kb0 == 0 ? tb : tb ^ 1;
-                    if (!mbar_wait(&bars->acc_empty[b], (uses[b] & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
+                    const uint32_t ub = b ? uses1 : uses0;
+                    if (!mbar_wait(&bars->acc_empty[b], (ub & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
                         ok = false;
                         break;
                     }
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     if (!ok) break;
                     umma_commit(&bars->acc_full[b]);  // this chunk is complete in TMEM buffer b
-                    ++uses[b];
+                    if (b) ++uses1; else ++uses0;
                 }
             }
             // All MMAs of this thread must be complete before TMEM is released.
@@ -321,44 +324,73 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp < EPI_WARP0) {
         // ---------------------------------------------------------------- split warpgroup
         const int t = threadIdx.x - SPLIT_WARP0 * 32;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-            const TileCoord tc = tile_coord(p, tile);
-            for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-                const int s = it % STAGES;
-                uint8_t* st = smem + s * STAGE_BYTES;
-                constexpr int nA = A_BYTES / 16, nAll = (A_BYTES + B_BYTES) / 16;
-                if constexpr (QTYPE != 0) {
-                    if (t < 128) {
-                        // Warps 2-5 decode this stage's A tile straight from the packed blocks into
-                        // explicit head + tail tiles. They need no TMA data, only the stage released
-                        // by the MMAs of its previous round.
-                        if (it >= STAGES &&
-                            !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) {
-                            ok = false;
-                        } else {
-                            decode_a_stage<QTYPE, QTRANS>(p, tc.m0, kb * BK, t, st);
-                        }
-                    } else {
-                        // Warps 6-7 split the TMA-loaded B tile.
-                        if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
-                            ok = false;
-                        } else {
-                            for (int i = nA + (t - 128); i < nAll; i += SPLIT_WARPS * 32 - 128) split_one(st, i, nA);
-                        }
-                    }
-                } else {
-                    if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
-                        ok = false;
-                    } else {
-                        for (int i = t; i < nAll; i += SPLIT_WARPS * 32) split_one(st, i, nA);
-                    }
+        constexpr int nA = A_BYTES / 16, nAll = (A_BYTES + B_BYTES) / 16;
+        if (QTYPE != 0 && t < 128) {
+            // Warps 2-5 of the fused kernel: decode each stage's A tile from the packed blocks into
+            // explicit head + tail tiles. They need no TMA data, only the stage released by the MMAs
+            // of its previous round. The packed words of the next stage are loaded before the
+            // current stage is decoded, so their L2 latency overlaps the decode and the wait.
+            int off[4];
+            a_stage_offsets<QTRANS>(t, off);
+            int64_t tile = blockIdx.x;
+            int kb = 0, m0 = tile < p.total_tiles ? tile_coord(p, tile).m0 : 0;
+            uint32_t it = 0;
+            int half = 0;
+            const uint8_t* blk = tile < p.total_tiles ? a_stage_block<QTYPE, QTRANS>(p, m0, 0, t, half) : nullptr;
+            HalfBlockWords cur;
+            if (blk != nullptr) load_half_words<QTYPE>(blk, half, cur);
+            while (tile < p.total_tiles) {
+                int64_t ntile = tile;
+                int nkb = kb + 1, nm0 = m0;
+                if (nkb == p.k_blocks) {
+                    nkb = 0;
+                    ntile += gridDim.x;
+                    if (ntile < p.total_tiles) nm0 = tile_coord(p, ntile).m0;
                 }
-                if (!ok) break;
+                int nhalf = 0;
+                const uint8_t* nblk = ntile < p.total_tiles ? a_stage_block<QTYPE, QTRANS>(p, nm0, nkb * BK, t, nhalf) : nullptr;
+                HalfBlockWords nxt;
+                if (nblk != nullptr) load_half_words<QTYPE>(nblk, nhalf, nxt);
+                const int s = it % STAGES;
+                if (it >= STAGES && !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) break;
+                float w[16];
+                if (blk != nullptr) {
+                    decode_half_words<QTYPE>(cur, half, w);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+                }
+                store_head_tail16(smem + s * STAGE_BYTES, w, off);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->split[s]);
+                cur = nxt;
+                blk = nblk;
+                half = nhalf;
+                tile = ntile;
+                kb = nkb;
+                m0 = nm0;
+                ++it;
+            }
+        } else {
+            // F32 kernel: all six warps split the A and B tiles; fused kernel: warps 6-7 split B.
+            const int i_begin = QTYPE == 0 ? t : nA + (t - 128);
+            const int i_step  = QTYPE == 0 ? SPLIT_WARPS * 32 : SPLIT_WARPS * 32 - 128;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * STAGE_BYTES;
+                    for (int i = i_begin; i < nAll; i += i_step) split_one(st, i, nA);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->split[s]);
+                }
             }
         }
     } else {
@@ -368,7 +400,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int q = warp - EPI_WARP0;  // TMEM lane quarter this warp may access
         const int row = q * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-        uint32_t tcount = 0, uses[2] = {0u, 0u};
+        uint32_t tcount = 0, uses_t = 0, uses_x = 0;  // chunks consumed from this tile's T / X buffer roles
+        uint32_t uses0 = 0, uses1 = 0;                // ... per physical buffer (scalars, in registers)
+        uint32_t gcount = 0;                          // column groups staged for TMA stores so far
+        const bool epi_leader = (threadIdx.x == EPI_WARP0 * 32);
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
             const int tb = tcount & 1, xb = tb ^ 1;
@@ -380,12 +415,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int n_groups = (n_valid + 31) / 32;  // uniform across the warp
             const uint32_t t_addr = tmem_base + lane_off + tb * BN;
             const uint32_t x_addr = tmem_base + lane_off + xb * BN;
-            if (!mbar_wait(&bars->acc_full[tb], uses[tb] & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
-            ++uses[tb];
+            uses_t = tb ? uses1 : uses0;
+            if (!mbar_wait(&bars->acc_full[tb], uses_t & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
+            if (tb) ++uses1; else ++uses0;
             tc_fence_after();
             for (int kb0 = CHUNK_KB; kb0 < p.k_blocks; kb0 += CHUNK_KB) {
-                if (!mbar_wait(&bars->acc_full[xb], uses[xb] & 1u, TRC_DEVERR_WAIT_ACCUM)) { ok = false; break; }
-                ++uses[xb];
+                uses_x = xb ? uses1 : uses0;
+                if (!mbar_wait(&bars->acc_full[xb], uses_x & 1u, TRC_DEVERR_WAIT_ACCUM)) { ok = false; break; }
+                if (xb) ++uses1; else ++uses0;
                 tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < n_groups; ++c) {
@@ -408,7 +445,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_addr + c * 32, r);
                 tmem_ld_wait();
-                if (m < p.M) {
+                if (p.tma_store) {
+                    // Stage the 128 x 32 group column-major (each column's 128 rows contiguous, the
+                    // layout of the TMA box) and let one thread store or reduce-add it.
+                    const int buf = gcount & 1;
+                    if (gcount >= EPI_BUFS) {
+                        if (epi_leader) bulk_wait_group_read<EPI_BUFS - 1>();  // this buffer's last store has read it
+                        named_barrier_sync(1, 128);
+                    }
+                    float* sb = reinterpret_cast<float*>(smem + EPI_OFF + buf * EPI_BUF_BYTES);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) sb[e * BM + row] = __uint_as_float(r[e]);
+                    fence_proxy_async_smem();
+                    named_barrier_sync(1, 128);
+                    if (epi_leader) {
+                        const uint32_t src = smem_base + EPI_OFF + buf * EPI_BUF_BYTES;
+                        if (p.accumulate) tma_reduce_add_4d(&tmD, src, tc.m0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        else tma_store_4d(&tmD, src, tc.m0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        bulk_commit_group();
+                    }
+                    ++gcount;
+                } else if (m < p.M) {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int n = tc.n0 + c * 32 + e;
@@ -424,6 +481,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[tb]);
         }
+        if (epi_leader) bulk_wait_group_all();  // every TMA store has completed before the CTA exits
     }
 
     tc_fence_before();
@@ -500,9 +558,49 @@ bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtens
     return r == CUDA_SUCCESS;
 }
 
+// Tensor map of D for the TMA-store epilogue, in the kernel's orientation: rows (TMEM lanes) M with
+// byte stride sm, columns N with stride sn, then the two plane dimensions. Box: 128 rows x 32
+// columns, no swizzle (the epilogue stages each group column-major). False when TMA cannot write
+// D (rows not contiguous, unaligned base or strides); the epilogue then stores element by element.
+bool encode_output(void* data, int64_t M, int64_t N, int64_t P2, int64_t P3, int64_t sm, int64_t sn, int64_t s2,
+                   int64_t s3, CUtensorMap& map) {
+    if (sm != 4 || (reinterpret_cast<uint64_t>(data) & 15u) != 0) return false;
+    if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31)) return false;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(P2),
+                          static_cast<cuuint64_t>(P3)};
+    cuuint64_t strides[3];
+    if (N > 1) {
+        if (!stride_ok(sn)) return false;
+        strides[0] = sn;
+    } else {
+        strides[0] = static_cast<cuuint64_t>((M * 4 + 15) / 16 * 16);
+    }
+    if (P2 > 1) {
+        if (!stride_ok(s2)) return false;
+        strides[1] = s2;
+    } else {
+        strides[1] = (strides[0] * dims[1] + 15) / 16 * 16;
+    }
+    if (P3 > 1) {
+        if (!stride_ok(s3)) return false;
+        strides[2] = s3;
+    } else {
+        strides[2] = (strides[1] * dims[2] + 15) / 16 * 16;
+    }
+    if (strides[1] >= (cuuint64_t(1) << 40) || strides[2] >= (cuuint64_t(1) << 40)) return false;
+    const cuuint32_t box[4]  = {BM, 32, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    return enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 // Launches one instantiation; the >48 KiB dynamic shared memory opt-in is set once per device.
 template <int QTYPE, int QTRANS>
-int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& p, cudaStream_t stream) {
+int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmD, const TcParams& p,
+              cudaStream_t stream) {
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
     int dev = 0;
@@ -521,7 +619,7 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const TcParams& p,
     const int sms = sm_count_current();
     if (sms <= 0) return TRC_CUDA_ECUDA;
     const int64_t grid = std::min<int64_t>(p.total_tiles, sms);
-    tf32x3_gemm_kernel<QTYPE, QTRANS><<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
+    tf32x3_gemm_kernel<QTYPE, QTRANS><<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tmD, p);
     note_launch();
     return check_launch();
 }
@@ -581,7 +679,10 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     p.d_s2 = d.nb[2];
     p.d_s3 = d.nb[3];
 
-    return launch_tc<0, 0>(tmA, tmB, p, stream);
+    CUtensorMap tmD;
+    std::memset(&tmD, 0, sizeof(tmD));
+    p.tma_store = encode_output(d.data, M, N, planes2, planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
+    return launch_tc<0, 0>(tmA, tmB, tmD, p, stream);
 }
 
 int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
@@ -624,10 +725,13 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
     p.q_blocks_per_row = static_cast<int>(w_ne0 / 32);
     p.q_row_bytes = static_cast<int64_t>(w_ne0 / 32) * static_cast<int64_t>(bb);
     p.q_rows = static_cast<int>(w_ne1);
+    CUtensorMap tmD;
+    std::memset(&tmD, 0, sizeof(tmD));
+    p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
 
 #define TRC_Q_CASE(T)                                                                   \
     case T:                                                                             \
-        return a_transposed ? launch_tc<T, 1>(tmA, tmB, p, stream) : launch_tc<T, 0>(tmA, tmB, p, stream);
+        return a_transposed ? launch_tc<T, 1>(tmA, tmB, tmD, p, stream) : launch_tc<T, 0>(tmA, tmB, tmD, p, stream);
     switch (type) {
         TRC_Q_CASE(2)
         TRC_Q_CASE(3)

@@ -50,6 +50,7 @@ __host__ __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
 template <int TYPE>
 struct QuantTraits;
 
+template <> struct QuantTraits<0> { static constexpr int kBytes = 0;  static constexpr int kQs = 0; };  // F32: no blocks
 template <> struct QuantTraits<2> { static constexpr int kBytes = 18; static constexpr int kQs = 2; };  // Q4_0
 template <> struct QuantTraits<3> { static constexpr int kBytes = 20; static constexpr int kQs = 4; };  // Q4_1
 template <> struct QuantTraits<6> { static constexpr int kBytes = 22; static constexpr int kQs = 6; };  // Q5_0
@@ -92,35 +93,47 @@ __device__ __forceinline__ void decode_quad(const uint8_t* blk, int c, float (&w
     }
 }
 
-// Decode weights 16h .. 16h+15 (h = 0 or 1) of the block at `blk` (2-byte aligned, any memory):
-// the packed fields are read once as 16-bit words.
+// Raw 16-bit words of one half-block (the fields weights 16h..16h+15 need), so that the global
+// loads of a later stage can be issued before the current stage is decoded.
+struct HalfBlockWords {
+    uint32_t w[12];
+};
+
 template <int TYPE>
-__device__ __forceinline__ void decode_half(const uint8_t* blk, int h, float (&w)[16]) {
+__device__ __forceinline__ void load_half_words(const uint8_t* blk, int h, HalfBlockWords& r) {
     const uint16_t* p16 = reinterpret_cast<const uint16_t*>(blk);
-    const float     d   = half_bits_to_float(p16[0]);
     if constexpr (TYPE == 8) {
-        uint32_t q[8];
+        r.w[0] = p16[0];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] = p16[1 + 8 * h + i];
+        for (int i = 0; i < 8; ++i) r.w[1 + i] = p16[1 + 8 * h + i];
+    } else {
+        constexpr int n16 = QuantTraits<TYPE>::kQs / 2 + 8;  // header words + 16 qs bytes
+#pragma unroll
+        for (int i = 0; i < n16; ++i) r.w[i] = p16[i];
+    }
+}
+
+// Decode weights 16h .. 16h+15 from words loaded by load_half_words.
+template <int TYPE>
+__device__ __forceinline__ void decode_half_words(const HalfBlockWords& r, int h, float (&w)[16]) {
+    const float d = half_bits_to_float(r.w[0]);
+    if constexpr (TYPE == 8) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-            const int v = static_cast<int>(static_cast<int8_t>((q[e >> 1] >> (8 * (e & 1))) & 0xFFu));
+            const int v = static_cast<int>(static_cast<int8_t>((r.w[1 + (e >> 1)] >> (8 * (e & 1))) & 0xFFu));
             w[e] = static_cast<float>(v) * d;
         }
     } else {
-        constexpr int kQs16 = QuantTraits<TYPE>::kQs / 2;  // first qs word
-        uint32_t      qs[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qs[i] = p16[kQs16 + i];
+        constexpr int kQs16 = QuantTraits<TYPE>::kQs / 2;
         uint32_t qh = 0;
-        if constexpr (TYPE == 6) qh = static_cast<uint32_t>(p16[1]) | (static_cast<uint32_t>(p16[2]) << 16);
-        if constexpr (TYPE == 7) qh = static_cast<uint32_t>(p16[2]) | (static_cast<uint32_t>(p16[3]) << 16);
+        if constexpr (TYPE == 6) qh = r.w[1] | (r.w[2] << 16);
+        if constexpr (TYPE == 7) qh = r.w[2] | (r.w[3] << 16);
         float m = 0.0f;
-        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(p16[1]);
+        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(r.w[1]);
         const int shift = 4 * h;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-            const uint32_t byte = (qs[e >> 1] >> (8 * (e & 1))) & 0xFFu;
+            const uint32_t byte = (r.w[kQs16 + (e >> 1)] >> (8 * (e & 1))) & 0xFFu;
             int q = static_cast<int>((byte >> shift) & 0xFu);
             if constexpr (TYPE == 6 || TYPE == 7) q |= static_cast<int>(((qh >> (16 * h + e)) & 1u) << 4);
             if constexpr (TYPE == 2) w[e] = static_cast<float>(q - 8) * d;
