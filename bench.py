@@ -472,13 +472,12 @@ def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> 
     B = torch.randn((p3, 32, 2048, 128), generator=gen, device="cuda")
     G = torch.randn((p3, 32, 2048, 2048), generator=gen, device="cuda")
     D = torch.empty((p3, 32, 2048, 2048), device="cuda")
-    dA_pre = torch.empty((p3, 32, 128, 2048), device="cuda")
     dA = torch.empty((p3, 8, 2048, 128), device="cuda")
     dB = torch.empty((p3, 32, 2048, 128), device="cuda")
     gflop = 2.0 * 128 * 2048 * 2048 * 32 * p3
     t_f = timed(lambda: tc.mul_mat(A, B, out=D))
-    t_a = timed(lambda: (tc.mul_mat(G.transpose(-1, -2), B.transpose(-1, -2), out=dA_pre),
-                         tc.repeat_back(dA_pre.transpose(-1, -2), [128, 2048, 8, p3], out=dA)))
+    # dA = repeat_back(T(mul_mat(T(G), T(B)))): one plane-reducing GEMM writing T(dA)
+    t_a = timed(lambda: tc.mul_mat_repeat_back(G.transpose(-1, -2), B.transpose(-1, -2), dA.transpose(-1, -2)))
     t_b = timed(lambda: tc.mul_mat(A.transpose(-1, -2), G, out=dB))
     out["gqa_bcast"] = {
         "fwd_tflops": round(world * gflop / t_f / 1e9, 2), "da_tflops": round(world * gflop / t_a / 1e9, 2),

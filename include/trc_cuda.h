@@ -156,6 +156,18 @@ enum {
 int trc_cuda_mul_mat(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags,
                      void* stream);
 
+/* d = repeat_back(mul_mat(a, b)) in one kernel: d may have fewer planes than b (b.ne2 % d.ne2 == 0,
+ * b.ne3 % d.ne3 == 0) and output plane (q2, q3) receives the sum of the products of every source
+ * plane (p2, p3) with p2 % d.ne2 == q2 and p3 % d.ne3 == q3. This is the dA of a broadcast mul_mat in
+ * the composed backward (src/core/trc_autograd.cpp:490-496: mul_mat, transpose, repeat_back) without
+ * the intermediate; with d a transposed view and TRC_CUDA_MM_ACCUMULATE it also performs the
+ * following acc into the parameter's grad_acc. Replaces compute_mul_mat + compute_repeat_back
+ * (src/backends/cpu/trc_cpu_ops.cpp:182-216, 932-951). The SIMT kernel keeps the reference's order
+ * and rounding (each plane's product rounded, then added in plane order) bit for bit; the tcgen05
+ * kernel accumulates the planes in its K loop, within the same 1e-5 normwise bar. */
+int trc_cuda_mul_mat_repeat_back(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d,
+                                 uint32_t flags, void* stream);
+
 enum { TRC_CUDA_KERNEL_TCGEN05 = 1, TRC_CUDA_KERNEL_SIMT = 2 };
 
 /* Which kernel trc_cuda_mul_mat would run for these views and flags: TRC_CUDA_KERNEL_TCGEN05 (the

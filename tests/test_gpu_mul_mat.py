@@ -146,3 +146,34 @@ def test_full_size_linear_forward_vs_fp64(tc):
     ref64 = (X.double() @ W.double().t())
     err = ((Y.double() - ref64).abs().max() / ref64.abs().max()).item()
     assert err <= 5e-6, err
+
+
+@pytest.mark.parametrize("simt", [True, False], ids=["simt", "tcgen05"])
+@pytest.mark.parametrize("transposed_out,accumulate", [(False, False), (True, False), (True, True)])
+def test_mul_mat_repeat_back(tc, simt, transposed_out, accumulate):
+    """d = repeat_back(mul_mat(a, b)) in one kernel: the broadcast-operand dA of the composed
+    backward. SIMT is bit-exact with the reference's mul_mat + repeat_back; tcgen05 within 1e-5."""
+    rng = np.random.default_rng(21)
+    G = rng.standard_normal((2, 8, 40, 48)).astype(np.float32)      # ggml [48, 40, 8, 2]: dL/dD
+    B = rng.standard_normal((2, 8, 40, 128)).astype(np.float32)     # ggml [128, 40, 8, 2]
+    a_t, b_t = np.swapaxes(G, -1, -2), np.swapaxes(B, -1, -2)       # T(G) [40, 48, ..], T(B) [40, 128, ..]
+    prod = oracle.mul_mat(a_t, b_t)                                  # [48, 128, 8, 2] -> numpy (2, 8, 128, 48)
+    want = oracle.repeat_back(prod, [48, 128, 2, 2])                 # planes i2 % 2
+    base = rng.standard_normal((2, 2, 48, 128)).astype(np.float32) if transposed_out else None
+    if transposed_out:
+        # write through the transposed view of a [128, 48, 2, 2] tensor (grad_acc of A)
+        out_t = dev(base)
+        out = out_t.transpose(-1, -2)
+        if accumulate:
+            want = want + np.swapaxes(base, -1, -2)
+        else:
+            out_t.zero_()
+    else:
+        out = torch.zeros((2, 2, 128, 48), device="cuda")
+    tc.mul_mat_repeat_back(dev(G).transpose(-1, -2), dev(B).transpose(-1, -2), out, accumulate=accumulate, simt=simt)
+    got = out.cpu().numpy()
+    if simt and not accumulate:
+        assert np.array_equal(np.ascontiguousarray(got).view(np.uint32), np.ascontiguousarray(want).view(np.uint32))
+    else:
+        assert normwise(np.ascontiguousarray(got), np.ascontiguousarray(want)) <= 1e-5
+    assert tc.device_error() == 0

@@ -267,16 +267,21 @@ private:
     }
 
     // ---------------------------------------------------------------- graph-level fusion
-    // The composed backward materialises dW as cont(transpose(mul_mat(...))) and adds it into the
-    // parameter's grad_acc with an in-place acc (src/core/trc_autograd.cpp:60-77, 487-503). When the
-    // intermediates have no other reader, the GEMM accumulates straight into grad_acc instead:
-    //   mul_mat M -> permute P -> cont C -> acc(inplace, whole grad_acc)   => one GEMM, D = T(grad_acc) (+=)
-    //   mul_mat M -> acc(inplace, whole grad_acc)                          => one GEMM, D = grad_acc (+=)
-    // Each output element then receives the same single fp32 add as in the unfused graph.
+    // The composed backward (src/core/trc_autograd.cpp:60-77, 487-503) materialises intermediates
+    // that the GEMM can write or accumulate directly when nothing else reads them:
+    //   dW:  mul_mat M -> permute P -> cont C -> acc(inplace, whole grad_acc)   => GEMM into T(grad_acc), +=
+    //   dB:  mul_mat M -> acc(inplace, whole grad_acc)                          => GEMM into grad_acc, +=
+    //   dA of a broadcast operand:
+    //        mul_mat M -> permute P -> repeat_back R -> acc(inplace, grad_acc)  => plane-reducing GEMM into
+    //                                                                              T(grad_acc), +=
+    //        mul_mat M -> permute P -> repeat_back R (other readers)           => plane-reducing GEMM into T(R)
+    // Every output element still receives one fp32 add from the fused acc, as in the unfused graph.
     // TRC_CUDA_NO_FUSION=1 executes every node as written.
     struct Fused {
-        const Tensor* acc_node;  // the acc that performs the fused work
-        bool          transposed;
+        const Tensor* target;      // tensor the GEMM writes (grad_acc, or the repeat_back output)
+        bool          transposed;  // write through the transposed view of target
+        bool          reduce;      // sum broadcast planes (repeat_back) in the GEMM
+        bool          accumulate;  // target += product
     };
     std::unordered_map<const Tensor*, Fused> fused_gemm_;  // mul_mat node -> fusion
     std::unordered_map<const Tensor*, bool>  skipped_;     // nodes whose work the fused GEMM does
@@ -293,26 +298,38 @@ private:
         auto private_to = [&](const Tensor* t) {
             return readers[t] == 1 && (t->flags & (TENSOR_FLAG_OUTPUT | TENSOR_FLAG_PARAM | TENSOR_FLAG_LOSS)) == 0;
         };
+        auto is_transpose_of_private_mul_mat = [&](const Tensor* P) {
+            if (P == nullptr || P->op != OP_PERMUTE || !private_to(P)) return false;
+            const int* ax = P->op_params;
+            const Tensor* M = P->src[0];
+            return ax[0] == 1 && ax[1] == 0 && ax[2] == 2 && ax[3] == 3 && M != nullptr && M->op == OP_MUL_MAT &&
+                   private_to(M) && fused_gemm_.count(M) == 0;
+        };
         for (Tensor* n : g->nodes) {
-            if (n->op != OP_ACC || n->nsrc < 2 || n->op_params[4] == 0) continue;  // in-place acc only
-            const Tensor* G = n->src[0];
-            const Tensor* C = n->src[1];
-            if (!tensor_is_contiguous(G) || !tensor_are_same_shape(G, C) || n->op_params[3] != 0) continue;
-            if (static_cast<size_t>(n->op_params[0]) != G->nb[1] || static_cast<size_t>(n->op_params[1]) != G->nb[2] ||
-                static_cast<size_t>(n->op_params[2]) != G->nb[3])
-                continue;
-            if (C->op == OP_MUL_MAT && private_to(C)) {
-                fused_gemm_[C] = {n, false};
-                skipped_[n]    = true;
-            } else if (C->op == OP_CONT && private_to(C) && C->src[0] != nullptr && C->src[0]->op == OP_PERMUTE) {
-                const Tensor* P = C->src[0];
-                const Tensor* M = P->src[0];
-                const int*    ax = P->op_params;
-                if (M == nullptr || M->op != OP_MUL_MAT || !private_to(P) || !private_to(M)) continue;
-                if (!(ax[0] == 1 && ax[1] == 0 && ax[2] == 2 && ax[3] == 3)) continue;
-                fused_gemm_[M] = {n, true};
-                skipped_[C]    = true;
-                skipped_[n]    = true;
+            if (n->op == OP_ACC && n->nsrc >= 2 && n->op_params[4] != 0) {  // in-place acc into a whole tensor
+                const Tensor* G = n->src[0];
+                const Tensor* C = n->src[1];
+                if (!tensor_is_contiguous(G) || !tensor_are_same_shape(G, C) || n->op_params[3] != 0) continue;
+                if (static_cast<size_t>(n->op_params[0]) != G->nb[1] || static_cast<size_t>(n->op_params[1]) != G->nb[2] ||
+                    static_cast<size_t>(n->op_params[2]) != G->nb[3])
+                    continue;
+                if (C->op == OP_MUL_MAT && private_to(C) && fused_gemm_.count(C) == 0) {
+                    fused_gemm_[C] = {G, false, false, true};
+                    skipped_[n]    = true;
+                } else if ((C->op == OP_CONT || C->op == OP_REPEAT_BACK) && private_to(C) &&
+                           is_transpose_of_private_mul_mat(C->src[0])) {
+                    fused_gemm_[C->src[0]->src[0]] = {G, true, C->op == OP_REPEAT_BACK, true};
+                    skipped_[C] = true;
+                    skipped_[n] = true;
+                }
+            }
+        }
+        // second pass: a repeat_back whose consumer is not a fusable acc is written by the GEMM directly
+        for (Tensor* n : g->nodes) {
+            if (n->op == OP_REPEAT_BACK && skipped_.count(n) == 0 && tensor_is_contiguous(n) &&
+                is_transpose_of_private_mul_mat(n->src[0])) {
+                fused_gemm_[n->src[0]->src[0]] = {n, true, true, false};
+                skipped_[n] = true;
             }
         }
     }
@@ -334,12 +351,17 @@ private:
                     const trc_cuda_view d = view_of(t);
                     CB_TRC(trc_cuda_mul_mat(&a, &b, &d, 0, stream_), "trc_cuda_mul_mat");
                 } else {
-                    trc_cuda_view d = view_of(it->second.acc_node->src[0]);  // grad_acc
-                    if (it->second.transposed) {  // D[i, j] lands on grad_acc[j, i]
+                    const Fused& f = it->second;
+                    trc_cuda_view d = view_of(f.target);
+                    if (f.transposed) {  // D[i, j] lands on target[j, i]
                         std::swap(d.ne[0], d.ne[1]);
                         std::swap(d.nb[0], d.nb[1]);
                     }
-                    CB_TRC(trc_cuda_mul_mat(&a, &b, &d, TRC_CUDA_MM_ACCUMULATE, stream_), "trc_cuda_mul_mat (fused acc)");
+                    const uint32_t flags = f.accumulate ? TRC_CUDA_MM_ACCUMULATE : 0u;
+                    if (f.reduce)
+                        CB_TRC(trc_cuda_mul_mat_repeat_back(&a, &b, &d, flags, stream_), "trc_cuda_mul_mat_repeat_back (fused)");
+                    else
+                        CB_TRC(trc_cuda_mul_mat(&a, &b, &d, flags, stream_), "trc_cuda_mul_mat (fused)");
                 }
                 return;
             }

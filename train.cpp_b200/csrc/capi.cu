@@ -151,6 +151,28 @@ int trc_cuda_mul_mat(const trc_cuda_view* a, const trc_cuda_view* b, const trc_c
     return mul_mat_simt(*a, *b, *d, acc, s);
 }
 
+int trc_cuda_mul_mat_repeat_back(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d,
+                                 uint32_t flags, void* stream) {
+    if (!view_ok(a) || !view_ok(b) || !view_ok(d)) return TRC_CUDA_EINVAL;
+    if (a->ne[0] != b->ne[0]) return TRC_CUDA_EINVAL;
+    if (a->ne[2] <= 0 || a->ne[3] <= 0 || b->ne[2] % a->ne[2] != 0 || b->ne[3] % a->ne[3] != 0) return TRC_CUDA_EINVAL;
+    if (d->ne[0] != a->ne[1] || d->ne[1] != b->ne[1] || d->ne[2] <= 0 || d->ne[3] <= 0 ||
+        b->ne[2] % d->ne[2] != 0 || b->ne[3] % d->ne[3] != 0)
+        return TRC_CUDA_EINVAL;
+    if (nelements(*d) == 0) return TRC_CUDA_OK;
+    const bool acc = (flags & TRC_CUDA_MM_ACCUMULATE) != 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->ne[0] == 0) {
+        if (acc) return TRC_CUDA_OK;
+        return mul_mat_simt(*a, *b, *d, false, s);
+    }
+    if ((flags & TRC_CUDA_MM_SIMT) == 0) {
+        const int st = mul_mat_tc(*a, *b, *d, acc, s);
+        if (st != TRC_CUDA_EUNSUPPORTED) return st;
+    }
+    return mul_mat_simt(*a, *b, *d, acc, s);
+}
+
 int trc_cuda_mul_mat_kernel(const trc_cuda_view* a, const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags) {
     const int st = check_mul_mat_shapes(a, b, d);
     if (st != TRC_CUDA_OK) return st;

@@ -21,11 +21,13 @@
 // double buffering survives: tile i keeps its total in buffer i%2 and its chunks in buffer
 // (i+1)%2, and tile i+1's first chunk can start while tile i's total is being stored.
 //
-// Structure (one persistent CTA per SM, 12 warps):
+// Structure (one persistent CTA per SM, 14 warps):
 //   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (4-stage ring, 64-byte swizzle)
 //   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
-//   warps 2-7   split warpgroup: writes the tails tA, tB of each stage next to the raw tiles
-//   warps 8-11  epilogue: TMEM -> registers (tcgen05.ld) -> strided global stores (ggml nb[])
+//   warps 2-9   split warps: write the tails tA, tB of each stage next to the raw tiles (fused
+//               variant: also decode the packed weight tile into head + tail)
+//   warps 10-13 epilogue: TMEM -> registers (tcgen05.ld) -> shared memory -> TMA store (or strided
+//               stores when TMA cannot address D)
 // Tile 128 (M, TMEM lanes) x 256 (N) x 16 (K) per stage; two 256-column fp32 TMEM buffers (all 512
 // columns). Shared-memory operand layouts: K-major tiles use the 64-byte swizzle (64 B rows);
 // MN-major tiles use the 128-byte swizzle with 32-byte atoms, the one layout tcgen05 accepts for
@@ -45,6 +47,8 @@
 #include "trc_ptx.cuh"
 #include "trc_quant.cuh"
 
+#include <cuda_fp16.h>
+
 namespace trc {
 
 namespace {
@@ -55,8 +59,8 @@ constexpr int B_BYTES     = BN * BK * 4;                 // 16 KiB
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);     // raw + tail = 48 KiB
 constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES, OFF_B_TAIL = 2 * A_BYTES + B_BYTES;
 constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
-constexpr int NUM_THREADS  = 384;
-constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 6, EPI_WARP0 = 8;
+constexpr int NUM_THREADS  = 448;
+constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 8, EPI_WARP0 = 10;  // epilogue warps 10-13 cover TMEM quarters 2,3,0,1
 constexpr int TMEM_COLS    = 512;
 constexpr int CHUNK_KB     = 16;   // k-blocks per fp32 promotion chunk (256 K)
 constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128-row x 32-column fp32 group of D, staged for a TMA store
@@ -68,8 +72,11 @@ struct TcParams {
     int     M, N, K;           // M: TMEM lanes (rows of D tiles), N: columns, K: reduction
     int     m_tiles, n_tiles, k_blocks;
     int     planes2, planes3;  // output planes
+    int     red2, red3;        // source planes summed into each output plane (repeat_back fused)
+    int     kv_blocks;         // k-blocks per tile: k_blocks x red2 x red3
     int     a_ne2, a_ne3, b_ne2, b_ne3;
     int     a_mn, b_mn;        // 1 = operand contiguous along M (resp. N)
+    int     a_tma5, b_tma5;    // MN-major operand loaded by one 5-D TMA per stage (else one per 32-row chunk)
     int     accumulate;
     int64_t total_tiles;
     char*   d;
@@ -139,60 +146,91 @@ __device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
     *dst = v;
 }
 
-// Writes 16 consecutive weights w[0..15] as head (TF32-truncated) and tail into the A tiles of a
-// stage: `chunk_off[u]` is the byte offset (already swizzled) of the u-th group of four weights.
-__device__ __forceinline__ void store_head_tail16(uint8_t* st, const float (&w)[16], const int (&chunk_off)[4]) {
+// decode_quad_words with the fp16 fields converted by the hardware (cvt.f32.f16): the same value
+// for every finite scale and minimum, in one instruction instead of the portable bit decode.
+template <int TYPE>
+__device__ __forceinline__ void decode_quad_words_cvt(const QuadWords& r, int j0, float (&w)[4]) {
+    const float    d = __half2float(__ushort_as_half(static_cast<unsigned short>(r.d)));
+    const uint32_t q = r.q0 | (r.q1 << 16);
+    if constexpr (TYPE == 8) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        uint4 h, l;
-        uint32_t* hp = &h.x;
-        uint32_t* lp = &l.x;
+        for (int e = 0; e < 4; ++e) w[e] = static_cast<float>(static_cast<int>(static_cast<int8_t>((q >> (8 * e)) & 0xFFu))) * d;
+    } else {
+        const int shift = j0 >= 16 ? 4 : 0;
+        float m = 0.0f;
+        if constexpr (TYPE == 3 || TYPE == 7) m = __half2float(__ushort_as_half(static_cast<unsigned short>(r.m)));
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const uint32_t bits = __float_as_uint(w[4 * u + e]);
-            hp[e] = bits & 0xFFFFE000u;
-            lp[e] = tf32_tail_bits(bits);
+            int v = static_cast<int>((q >> (8 * e + shift)) & 0xFu);
+            if constexpr (TYPE == 6 || TYPE == 7) v |= static_cast<int>(((r.qh >> ((j0 & 15) + e)) & 1u) << 4);
+            if constexpr (TYPE == 2) w[e] = static_cast<float>(v - 8) * d;
+            if constexpr (TYPE == 6) w[e] = static_cast<float>(v - 16) * d;
+            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(v), d, m);
         }
-        *reinterpret_cast<uint4*>(st + OFF_A_RAW + chunk_off[u])  = h;
-        *reinterpret_cast<uint4*>(st + OFF_A_TAIL + chunk_off[u]) = l;
     }
 }
 
-// A-stage decode for the fused dequant GEMM (thread t of 128). A stage covers A rows m0..m0+127
-// and K columns k0..k0+15: one half (16 weights) of a 32-weight block per W row (QTRANS = 0,
-// K-major) or 16 W rows x 4 blocks (QTRANS = 1, MN-major). a_stage_block() says where thread t's
-// 16 weights come from (nullptr: out of range, written as zeros); a_stage_offsets() where they go.
+// Fused dequant: a stage's A tile (128 rows x 16 K) is 512 quads of 4 consecutive weights. Quad q
+// of the stage comes from quad_block() (nullptr: out of range, written as zeros) and goes, as head
+// (TF32-truncated) and tail, to the swizzled byte offset quad_offset(q) of the A tiles. Consecutive
+// quads read adjacent bytes of the packed rows, so a warp's loads touch few cache lines.
+constexpr int A_QUADS = BM * BK / 4;
+
+// Per tile: the packed-row pointer of quad q (K-major: its W row; MN-major: its K-row offset and
+// block column), nullptr when the quad's rows lie outside the matrix.
 template <int QTYPE, int QTRANS>
-__device__ __forceinline__ const uint8_t* a_stage_block(const TcParams& p, int m0, int k0, int t, int& half) {
+__device__ __forceinline__ const uint8_t* quad_tile_base(const TcParams& p, int m0, int q) {
     constexpr int BB = QuantTraits<QTYPE>::kBytes;
     if constexpr (QTRANS == 0) {
-        const int m = m0 + t;
-        half = (k0 >> 4) & 1;
-        if (m < p.M && k0 < p.K) return p.qa + static_cast<int64_t>(m) * p.q_row_bytes + static_cast<int64_t>(k0 >> 5) * BB;
+        const int m = m0 + (q >> 2);
+        return m < p.M ? p.qa + static_cast<int64_t>(m) * p.q_row_bytes : nullptr;
     } else {
-        const int kr = t >> 3, j = (t >> 1) & 3;
-        half = t & 1;
-        const int wrow = k0 + kr, m = m0 + 32 * j;
-        if (wrow < p.K && m < p.M) return p.qa + static_cast<int64_t>(wrow) * p.q_row_bytes + static_cast<int64_t>(m >> 5) * BB;
+        const int kr = q >> 5, m = m0 + 32 * ((q & 31) >> 3);
+        return m < p.M ? p.qa + static_cast<int64_t>(kr) * p.q_row_bytes + static_cast<int64_t>(m >> 5) * BB : nullptr;
     }
-    return nullptr;
 }
 
-// Swizzled byte offsets of thread t's four 16-byte chunks (4 weights each) in the stage's A tiles.
-template <int QTRANS>
-__device__ __forceinline__ void a_stage_offsets(int t, int (&off)[4]) {
+// Per stage: the block holding quad q's four weights and the index j0 of the first of them
+// (nullptr: out of range). K-major: block k0/32 of the row, weights (k0 mod 32) + 4 (q mod 4);
+// MN-major: W row k0 + q/32, weights 4 ((q mod 32) mod 8).
+template <int QTYPE, int QTRANS>
+__device__ __forceinline__ const uint8_t* quad_block(const TcParams& p, const uint8_t* base, int k0, int q, int& j0) {
+    constexpr int BB = QuantTraits<QTYPE>::kBytes;
+    if (base == nullptr) return nullptr;
     if constexpr (QTRANS == 0) {
-        // K-major, 64-byte rows: row t, chunk u at unit u ^ ((t >> 1) & 3)
-#pragma unroll
-        for (int u = 0; u < 4; ++u) off[u] = t * 64 + ((u ^ ((t >> 1) & 3)) << 4);
+        j0 = (k0 & 16) + 4 * (q & 3);
+        return base + (k0 >> 5) * BB;
     } else {
-        // MN-major, 32-element chunks of 16 K-rows x 128 B: chunk j, K-row kr; the 16 weights fill
-        // 32-byte units 2h and 2h+1, swizzled by (kr & 3)
-        const int kr = t >> 3, j = (t >> 1) & 3, h = t & 1;
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-            off[u] = j * 2048 + kr * 128 + (((2 * h + (u >> 1)) ^ (kr & 3)) << 5) + ((u & 1) << 4);
+        j0 = (q & 7) * 4;
+        return k0 + (q >> 5) < p.K ? base + static_cast<int64_t>(k0) * p.q_row_bytes : nullptr;
     }
+}
+
+template <int QTRANS>
+__device__ __forceinline__ int quad_offset(int q) {
+    if constexpr (QTRANS == 0) {
+        const int r = q >> 2, u = q & 3;  // K-major: 64-byte rows, unit u ^ ((r >> 1) & 3)
+        return r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+    } else {
+        const int kr = q >> 5, mq = q & 31;  // MN-major: 32-element chunk mq/8, K-row kr, 32-byte units ^ (kr & 3)
+        return (mq >> 3) * 2048 + kr * 128 + ((((mq & 7) >> 1) ^ (kr & 3)) << 5) + ((mq & 1) << 4);
+    }
+}
+
+// Decoded weights are finite for finite scales, so the tail needs no special-value handling
+// (a non-finite scale makes the product NaN either way).
+__device__ __forceinline__ void store_quad_head_tail(uint8_t* st, int off, const float (&w)[4]) {
+    uint4 h, l;
+    uint32_t* hp = &h.x;
+    uint32_t* lp = &l.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint32_t bits = __float_as_uint(w[e]);
+        hp[e] = bits & 0xFFFFE000u;
+        lp[e] = __float_as_uint(__fsub_rn(w[e], __uint_as_float(hp[e])));
+    }
+    *reinterpret_cast<uint4*>(st + OFF_A_RAW + off)  = h;
+    *reinterpret_cast<uint4*>(st + OFF_A_TAIL + off) = l;
 }
 
 // QTYPE = 0: A is an F32 view loaded by TMA. QTYPE = ggml Q-type: A is decoded from packed blocks by
@@ -240,9 +278,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool ok = true;
             for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
                 const TileCoord tc = tile_coord(p, tile);
-                const int a2 = tc.p2 % p.a_ne2, a3 = tc.p3 % p.a_ne3;
-                const int b2 = tc.p2 % p.b_ne2, b3 = tc.p3 % p.b_ne3;
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                int r = 0, kb = 0;  // source-plane round and k-block of the virtual k-block vkb
+                for (int vkb = 0; vkb < p.kv_blocks; ++vkb, ++it) {
+                    const int sp2 = tc.p2 + p.planes2 * (r % p.red2), sp3 = tc.p3 + p.planes3 * (r / p.red2);
+                    const int a2 = sp2 % p.a_ne2, a3 = sp3 % p.a_ne3;
+                    const int b2 = sp2 % p.b_ne2, b3 = sp3 % p.b_ne3;
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
                     if (!mbar_wait(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
@@ -252,6 +292,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if constexpr (QTYPE == 0) {
                         if (!p.a_mn) {
                             tma_load_4d(st + OFF_A_RAW, &tmA, &bars->full[s], k0, tc.m0, a2, a3);
+                        } else if (p.a_tma5) {
+                            tma_load_5d(st + OFF_A_RAW, &tmA, &bars->full[s], 0, k0, tc.m0 / 32, a2, a3);
                         } else {
 #pragma unroll
                             for (int c = 0; c < BM / 32; ++c)
@@ -261,10 +303,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     if (!p.b_mn) {
                         tma_load_4d(st + OFF_B_RAW, &tmB, &bars->full[s], k0, tc.n0, b2, b3);
+                    } else if (p.b_tma5) {
+                        tma_load_5d(st + OFF_B_RAW, &tmB, &bars->full[s], 0, k0, tc.n0 / 32, b2, b3);
                     } else {
 #pragma unroll
                         for (int c = 0; c < BN / 32; ++c)
                             tma_load_4d(st + OFF_B_RAW + c * 2048, &tmB, &bars->full[s], tc.n0 + 32 * c, k0, b2, b3);
+                    }
+                    if (++kb == p.k_blocks) {
+                        kb = 0;
+                        ++r;
                     }
                 }
             }
@@ -282,7 +330,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool ok = true;
             for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
                 const int tb = tcount & 1;  // this tile's running-total buffer; chunks >= 1 use tb ^ 1
-                for (int kb0 = 0; kb0 < p.k_blocks && ok; kb0 += CHUNK_KB) {
+                for (int kb0 = 0; kb0 < p.kv_blocks && ok; kb0 += CHUNK_KB) {
                     const int b = kb0 == 0 ? tb : tb ^ 1;
                     const uint32_t ub = b ? uses1 : uses0;
                     if (!mbar_wait(&bars->acc_empty[b], (ub & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
@@ -291,7 +339,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * BN;
-                    const int kb1 = min(p.k_blocks, kb0 + CHUNK_KB);
+                    const int kb1 = min(p.kv_blocks, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = it % STAGES;
                         if (!mbar_wait(&bars->split[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
@@ -325,61 +373,85 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- split warpgroup
         const int t = threadIdx.x - SPLIT_WARP0 * 32;
         constexpr int nA = A_BYTES / 16, nAll = (A_BYTES + B_BYTES) / 16;
-        if (QTYPE != 0 && t < 128) {
-            // Warps 2-5 of the fused kernel: decode each stage's A tile from the packed blocks into
-            // explicit head + tail tiles. They need no TMA data, only the stage released by the MMAs
-            // of its previous round. The packed words of the next stage are loaded before the
-            // current stage is decoded, so their L2 latency overlaps the decode and the wait.
-            int off[4];
-            a_stage_offsets<QTRANS>(t, off);
+        if constexpr (QTYPE != 0) {
+            // Fused kernel: the six warps decode the stage's A quads (up to 3 per thread) from the
+            // packed blocks into head + tail tiles, then split the TMA-loaded B tile. The packed
+            // words of the next stage are loaded before the current stage is decoded, so their L2
+            // latency overlaps the decode and the waits.
+            constexpr int NT = SPLIT_WARPS * 32;
+            constexpr int QPT = (A_QUADS + NT - 1) / NT;
+            int qoff[QPT];
+#pragma unroll
+            for (int i = 0; i < QPT; ++i) qoff[i] = (t + NT * i) < A_QUADS ? quad_offset<QTRANS>(t + NT * i) : 0;
             int64_t tile = blockIdx.x;
-            int kb = 0, m0 = tile < p.total_tiles ? tile_coord(p, tile).m0 : 0;
+            int kb = 0;
+            const uint8_t* base[QPT];  // this tile's packed-row pointers
+#pragma unroll
+            for (int i = 0; i < QPT; ++i)
+                base[i] = (tile < p.total_tiles && t + NT * i < A_QUADS)
+                              ? quad_tile_base<QTYPE, QTRANS>(p, tile_coord(p, tile).m0, t + NT * i) : nullptr;
+            QuadWords cur[QPT];
+            const uint8_t* cblk[QPT];
+            int cj0[QPT];
+#pragma unroll
+            for (int i = 0; i < QPT; ++i) {
+                cblk[i] = quad_block<QTYPE, QTRANS>(p, base[i], 0, t + NT * i, cj0[i]);
+                if (cblk[i] != nullptr) load_quad_words<QTYPE>(cblk[i], cj0[i], cur[i]);
+            }
             uint32_t it = 0;
-            int half = 0;
-            const uint8_t* blk = tile < p.total_tiles ? a_stage_block<QTYPE, QTRANS>(p, m0, 0, t, half) : nullptr;
-            HalfBlockWords cur;
-            if (blk != nullptr) load_half_words<QTYPE>(blk, half, cur);
             while (tile < p.total_tiles) {
                 int64_t ntile = tile;
-                int nkb = kb + 1, nm0 = m0;
+                int nkb = kb + 1;
                 if (nkb == p.k_blocks) {
                     nkb = 0;
                     ntile += gridDim.x;
-                    if (ntile < p.total_tiles) nm0 = tile_coord(p, ntile).m0;
-                }
-                int nhalf = 0;
-                const uint8_t* nblk = ntile < p.total_tiles ? a_stage_block<QTYPE, QTRANS>(p, nm0, nkb * BK, t, nhalf) : nullptr;
-                HalfBlockWords nxt;
-                if (nblk != nullptr) load_half_words<QTYPE>(nblk, nhalf, nxt);
-                const int s = it % STAGES;
-                if (it >= STAGES && !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) break;
-                float w[16];
-                if (blk != nullptr) {
-                    decode_half_words<QTYPE>(cur, half, w);
-                } else {
+                    const int nm0 = ntile < p.total_tiles ? tile_coord(p, ntile).m0 : 0;
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) w[e] = 0.0f;
+                    for (int i = 0; i < QPT; ++i)
+                        base[i] = (ntile < p.total_tiles && t + NT * i < A_QUADS)
+                                      ? quad_tile_base<QTYPE, QTRANS>(p, nm0, t + NT * i) : nullptr;
                 }
-                store_head_tail16(smem + s * STAGE_BYTES, w, off);
+                QuadWords nxt[QPT];
+                const uint8_t* nblk[QPT];
+                int nj0[QPT];
+#pragma unroll
+                for (int i = 0; i < QPT; ++i) {
+                    nblk[i] = quad_block<QTYPE, QTRANS>(p, base[i], nkb * BK, t + NT * i, nj0[i]);
+                    if (nblk[i] != nullptr) load_quad_words<QTYPE>(nblk[i], nj0[i], nxt[i]);
+                }
+                const int s = it % STAGES;
+                uint8_t* st = smem + s * STAGE_BYTES;
+                if (it >= STAGES && !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) break;
+#pragma unroll
+                for (int i = 0; i < QPT; ++i) {
+                    if (t + NT * i >= A_QUADS) continue;
+                    float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (cblk[i] != nullptr) decode_quad_words_cvt<QTYPE>(cur[i], cj0[i], w);
+                    store_quad_head_tail(st, qoff[i], w);
+                }
+                if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
+                for (int i = nA + t; i < nAll; i += NT) split_one(st, i, nA);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->split[s]);
-                cur = nxt;
-                blk = nblk;
-                half = nhalf;
+#pragma unroll
+                for (int i = 0; i < QPT; ++i) {
+                    cur[i] = nxt[i];
+                    cblk[i] = nblk[i];
+                    cj0[i] = nj0[i];
+                }
                 tile = ntile;
                 kb = nkb;
-                m0 = nm0;
                 ++it;
             }
         } else {
-            // F32 kernel: all six warps split the A and B tiles; fused kernel: warps 6-7 split B.
-            const int i_begin = QTYPE == 0 ? t : nA + (t - 128);
-            const int i_step  = QTYPE == 0 ? SPLIT_WARPS * 32 : SPLIT_WARPS * 32 - 128;
+            // F32 kernel: all split warps split the A and B tiles.
+            const int i_begin = t;
+            const int i_step  = SPLIT_WARPS * 32;
             uint32_t it = 0;
             bool ok = true;
             for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-                for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+                for (int kb = 0; kb < p.kv_blocks; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
                         ok = false;
@@ -397,7 +469,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- epilogue
         // Per tile: chunk 0 lands in buffer tb (the running total T), every further chunk in tb^1 (X)
         // and is added into T with round-to-nearest fp32 adds; the final sum goes to global memory.
-        const int q = warp - EPI_WARP0;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;  // TMEM lane quarter this warp may access (warp id mod 4)
         const int row = q * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
         uint32_t tcount = 0, uses_t = 0, uses_x = 0;  // chunks consumed from this tile's T / X buffer roles
@@ -419,7 +491,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!mbar_wait(&bars->acc_full[tb], uses_t & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
             if (tb) ++uses1; else ++uses0;
             tc_fence_after();
-            for (int kb0 = CHUNK_KB; kb0 < p.k_blocks; kb0 += CHUNK_KB) {
+            for (int kb0 = CHUNK_KB; kb0 < p.kv_blocks; kb0 += CHUNK_KB) {
                 uses_x = xb ? uses1 : uses0;
                 if (!mbar_wait(&bars->acc_full[xb], uses_x & 1u, TRC_DEVERR_WAIT_ACCUM)) { ok = false; break; }
                 if (xb) ++uses1; else ++uses0;
@@ -509,7 +581,8 @@ bool stride_ok(int64_t s) { return s > 0 && (s % 16) == 0 && s < (int64_t(1) << 
 
 // Builds the tensor map of one operand: a ggml view with ne0 = K, ne1 = rows (M or N).
 // Returns false when TMA cannot address the view (the caller then uses the SIMT kernel).
-bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtensorMap& map) {
+bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtensorMap& map, bool* tma5 = nullptr) {
+    if (tma5 != nullptr) *tma5 = false;
     if ((reinterpret_cast<uint64_t>(v.data) & 15u) != 0) return false;
     const int64_t K = v.ne[0], R = v.ne[1];
     if (K >= (int64_t(1) << 31) || R >= (int64_t(1) << 31)) return false;
@@ -551,6 +624,20 @@ bool encode_operand(const trc_cuda_view& v, int box_rows, bool& mn_major, CUtens
     box[3] = 1;
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return false;
+    if (mn_major && tma5 != nullptr && R % 32 == 0 && R / 32 < (int64_t(1) << 31)) {
+        // One box per stage: dims (32 MN elements, K, R/32 chunks of 32, planes), so the box
+        // {32, 16, box_rows/32} lands chunk-major -- chunk c at c x 2 KiB -- the descriptor layout.
+        const cuuint64_t dims5[5]    = {32, dims[1], static_cast<cuuint64_t>(R / 32), dims[2], dims[3]};
+        const cuuint64_t strides5[4] = {strides[0], 128, strides[1], strides[2]};
+        const cuuint32_t box5[5]     = {32, static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows / 32), 1, 1};
+        const cuuint32_t estr5[5]    = {1, 1, 1, 1, 1};
+        if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, v.data, dims5, strides5, box5, estr5,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            *tma5 = true;
+            return true;
+        }
+    }
     const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.data, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE,
                            mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B,
@@ -633,6 +720,7 @@ bool mul_mat_tc_eligible(const trc_cuda_view& a_in, const trc_cuda_view& b_in, c
     const int64_t M = A.ne[1], N = B.ne[1], K = a_in.ne[0];
     if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return false;
     if (b_in.ne[2] >= (1 << 30) || b_in.ne[3] >= (1 << 30)) return false;
+    if (d.ne[2] <= 0 || d.ne[3] <= 0 || b_in.ne[2] % d.ne[2] != 0 || b_in.ne[3] % d.ne[3] != 0) return false;
     CUtensorMap tm;
     bool mn = false;
     return encode_operand(A, BM, mn, tm) && encode_operand(B, BN, mn, tm);
@@ -646,14 +734,19 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     const trc_cuda_view& A = swap ? b_in : a_in;  // MMA-A: rows = M
     const trc_cuda_view& B = swap ? a_in : b_in;  // MMA-B: rows = N
     const int64_t M = A.ne[1], N = B.ne[1], K = a_in.ne[0];
-    const int64_t planes2 = b_in.ne[2], planes3 = b_in.ne[3];
+    // Output planes; when d has fewer planes than b, the source planes p with p % d.ne == q are
+    // summed into output plane q (repeat_back fused into the K loop).
+    const int64_t planes2 = d.ne[2], planes3 = d.ne[3];
+    if (planes2 <= 0 || planes3 <= 0 || b_in.ne[2] % planes2 != 0 || b_in.ne[3] % planes3 != 0) return TRC_CUDA_EINVAL;
+    const int64_t red2 = b_in.ne[2] / planes2, red3 = b_in.ne[3] / planes3;
     if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
     if (planes2 >= (1 << 30) || planes3 >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
+    if ((K + BK - 1) / BK * red2 * red3 >= (int64_t(1) << 30)) return TRC_CUDA_EUNSUPPORTED;
 
     CUtensorMap tmA, tmB;
-    bool a_mn = false, b_mn = false;
-    if (!encode_operand(A, BM, a_mn, tmA)) return TRC_CUDA_EUNSUPPORTED;
-    if (!encode_operand(B, BN, b_mn, tmB)) return TRC_CUDA_EUNSUPPORTED;
+    bool a_mn = false, b_mn = false, a5 = false, b5 = false;
+    if (!encode_operand(A, BM, a_mn, tmA, &a5)) return TRC_CUDA_EUNSUPPORTED;
+    if (!encode_operand(B, BN, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
 
     TcParams p;
     std::memset(&p, 0, sizeof(p));
@@ -665,12 +758,17 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
     p.planes2 = static_cast<int>(planes2);
     p.planes3 = static_cast<int>(planes3);
+    p.red2 = static_cast<int>(red2);
+    p.red3 = static_cast<int>(red3);
+    p.kv_blocks = p.k_blocks * p.red2 * p.red3;
     p.a_ne2 = static_cast<int>(A.ne[2]);
     p.a_ne3 = static_cast<int>(A.ne[3]);
     p.b_ne2 = static_cast<int>(B.ne[2]);
     p.b_ne3 = static_cast<int>(B.ne[3]);
     p.a_mn = a_mn ? 1 : 0;
     p.b_mn = b_mn ? 1 : 0;
+    p.a_tma5 = a5 ? 1 : 0;
+    p.b_tma5 = b5 ? 1 : 0;
     p.accumulate = accumulate ? 1 : 0;
     p.total_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * planes2 * planes3;
     p.d    = static_cast<char*>(d.data);
@@ -694,8 +792,8 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
     if ((reinterpret_cast<uint64_t>(w_blocks) & 1u) != 0) return TRC_CUDA_EINVAL;
     CUtensorMap tmA, tmB;
     std::memset(&tmA, 0, sizeof(tmA));
-    bool b_mn = false;
-    if (!encode_operand(b, BN, b_mn, tmB)) return TRC_CUDA_EUNSUPPORTED;
+    bool b_mn = false, b5 = false;
+    if (!encode_operand(b, BN, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
     const size_t bb = trc_cuda_block_bytes(type);
 
     TcParams p;
@@ -708,12 +806,16 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
     p.planes2 = static_cast<int>(b.ne[2]);
     p.planes3 = static_cast<int>(b.ne[3]);
+    p.red2 = 1;
+    p.red3 = 1;
+    p.kv_blocks = p.k_blocks;
     p.a_ne2 = 1;
     p.a_ne3 = 1;
     p.b_ne2 = static_cast<int>(b.ne[2]);
     p.b_ne3 = static_cast<int>(b.ne[3]);
     p.a_mn = a_transposed ? 1 : 0;
     p.b_mn = b_mn ? 1 : 0;
+    p.b_tma5 = b5 ? 1 : 0;
     p.accumulate = accumulate ? 1 : 0;
     p.total_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * b.ne[2] * b.ne[3];
     p.d    = static_cast<char*>(d.data);

@@ -93,52 +93,49 @@ __device__ __forceinline__ void decode_quad(const uint8_t* blk, int c, float (&w
     }
 }
 
-// Raw 16-bit words of one half-block (the fields weights 16h..16h+15 need), so that the global
-// loads of a later stage can be issued before the current stage is decoded.
-struct HalfBlockWords {
-    uint32_t w[12];
+// Raw 16-bit words a quad (weights j0..j0+3, j0 a multiple of 4) needs: the scale d, the minimum m
+// (_1 formats), the 16-bit word of qh holding bits j0..j0+3 (Q5 formats) and the two words holding
+// the four quant bytes. Loading them into registers first lets a later stage's loads overlap the
+// decode of the current one.
+struct QuadWords {
+    uint32_t d, m, qh, q0, q1;
 };
 
 template <int TYPE>
-__device__ __forceinline__ void load_half_words(const uint8_t* blk, int h, HalfBlockWords& r) {
+__device__ __forceinline__ void load_quad_words(const uint8_t* blk, int j0, QuadWords& r) {
     const uint16_t* p16 = reinterpret_cast<const uint16_t*>(blk);
+    r.d = p16[0];
     if constexpr (TYPE == 8) {
-        r.w[0] = p16[0];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r.w[1 + i] = p16[1 + 8 * h + i];
+        r.q0 = p16[1 + (j0 >> 1)];
+        r.q1 = p16[2 + (j0 >> 1)];
     } else {
-        constexpr int n16 = QuantTraits<TYPE>::kQs / 2 + 8;  // header words + 16 qs bytes
-#pragma unroll
-        for (int i = 0; i < n16; ++i) r.w[i] = p16[i];
+        constexpr int qs16 = QuantTraits<TYPE>::kQs / 2;
+        r.q0 = p16[qs16 + ((j0 & 15) >> 1)];
+        r.q1 = p16[qs16 + ((j0 & 15) >> 1) + 1];
+        if constexpr (TYPE == 3 || TYPE == 7) r.m = p16[1];
+        if constexpr (TYPE == 6) r.qh = p16[1 + (j0 >> 4)];
+        if constexpr (TYPE == 7) r.qh = p16[2 + (j0 >> 4)];
     }
 }
 
-// Decode weights 16h .. 16h+15 from words loaded by load_half_words.
 template <int TYPE>
-__device__ __forceinline__ void decode_half_words(const HalfBlockWords& r, int h, float (&w)[16]) {
-    const float d = half_bits_to_float(r.w[0]);
+__device__ __forceinline__ void decode_quad_words(const QuadWords& r, int j0, float (&w)[4]) {
+    const float    d = half_bits_to_float(r.d);
+    const uint32_t q = r.q0 | (r.q1 << 16);
     if constexpr (TYPE == 8) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int v = static_cast<int>(static_cast<int8_t>((r.w[1 + (e >> 1)] >> (8 * (e & 1))) & 0xFFu));
-            w[e] = static_cast<float>(v) * d;
-        }
+        for (int e = 0; e < 4; ++e) w[e] = static_cast<float>(static_cast<int>(static_cast<int8_t>((q >> (8 * e)) & 0xFFu))) * d;
     } else {
-        constexpr int kQs16 = QuantTraits<TYPE>::kQs / 2;
-        uint32_t qh = 0;
-        if constexpr (TYPE == 6) qh = r.w[1] | (r.w[2] << 16);
-        if constexpr (TYPE == 7) qh = r.w[2] | (r.w[3] << 16);
+        const int shift = j0 >= 16 ? 4 : 0;
         float m = 0.0f;
-        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(r.w[1]);
-        const int shift = 4 * h;
+        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(r.m);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const uint32_t byte = (r.w[kQs16 + (e >> 1)] >> (8 * (e & 1))) & 0xFFu;
-            int q = static_cast<int>((byte >> shift) & 0xFu);
-            if constexpr (TYPE == 6 || TYPE == 7) q |= static_cast<int>(((qh >> (16 * h + e)) & 1u) << 4);
-            if constexpr (TYPE == 2) w[e] = static_cast<float>(q - 8) * d;
-            if constexpr (TYPE == 6) w[e] = static_cast<float>(q - 16) * d;
-            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(q), d, m);
+        for (int e = 0; e < 4; ++e) {
+            int v = static_cast<int>((q >> (8 * e + shift)) & 0xFu);
+            if constexpr (TYPE == 6 || TYPE == 7) v |= static_cast<int>(((r.qh >> ((j0 & 15) + e)) & 1u) << 4);
+            if constexpr (TYPE == 2) w[e] = static_cast<float>(v - 8) * d;
+            if constexpr (TYPE == 6) w[e] = static_cast<float>(v - 16) * d;
+            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(v), d, m);
         }
     }
 }

@@ -81,6 +81,7 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_mul_mat": (I, [VP, VP, VP, U32, P]),
         "trc_cuda_mul_mat_q": (I, [I, P, I64, I64, I, VP, VP, U32, P]),
         "trc_cuda_mul_mat_kernel": (I, [VP, VP, VP, U32]),
+        "trc_cuda_mul_mat_repeat_back": (I, [VP, VP, VP, U32, P]),
         "trc_cuda_cont": (I, [VP, VP, P]),
         "trc_cuda_acc": (I, [P, I64, VP, I64, I64, I64, I64, P]),
         "trc_cuda_repeat_back": (I, [VP, VP, P]),
@@ -249,6 +250,17 @@ def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, a
     va, vb, vd = view_of(a), view_of(b), view_of(out)
     _check(lib().trc_cuda_mul_mat(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), flags, _stream(stream)),
            "trc_cuda_mul_mat")
+    return out
+
+
+def mul_mat_repeat_back(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, accumulate: bool = False,
+                        simt: bool = False, stream=None) -> torch.Tensor:
+    """out (+)= repeat_back(mul_mat(a, b), shape of out): the broadcast-plane reduction of the
+    composed backward's dA fused into the GEMM (out may have fewer planes than b)."""
+    flags = (MM_ACCUMULATE if accumulate else 0) | (MM_SIMT if simt else 0)
+    va, vb, vd = view_of(a), view_of(b), view_of(out)
+    _check(lib().trc_cuda_mul_mat_repeat_back(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), flags,
+                                              _stream(stream)), "trc_cuda_mul_mat_repeat_back")
     return out
 
 
