@@ -76,51 +76,121 @@ def profile_value(name: str, key: str):
 
 # ------------------------------------------------------------------ clocks sampler
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) of this rank's GPU during the timed region."""
+    """SM clock and clock-event reasons of this rank's GPU, sampled every millisecond by NVML in a
+    background thread while the timed region runs (`mark_start` / `mark_stop` bracket it; only
+    samples taken between them are reported). Reads only; no GPU setting is touched. Falls back
+    to nvidia-smi at 200 ms when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples: list[tuple[float, float, int]] = []  # (time, sm MHz, reason mask)
+        self.sm_max = None
+        self.window = [None, None]
+        self.stop_evt = threading.Event()
+        self.thread = None
+        self.nvml = None
+        self.handle = None
+        self.smi = None
+        self.smi_out = None
+
+    def _open_nvml(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = getattr(torch.cuda.get_device_properties(self.cuda_index), "uuid", None)
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}") if uuid is not None else None
+        except pynvml.NVMLError:
+            handle = None
+        if handle is None:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+        self.nvml, self.handle = pynvml, handle
+        self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+
+    def _poll(self):
+        nv, h = self.nvml, self.handle
+        while not self.stop_evt.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((time.perf_counter(), sm, mask))
+            except Exception:  # noqa: BLE001 -- a failed read only loses a sample
+                pass
+            time.sleep(0.001)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            self._open_nvml()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+            self.smi_out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            try:
+                self.smi = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={self.SMI_FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=self.smi_out, stderr=subprocess.DEVNULL)
+            except OSError:
+                self.smi = None
+        time.sleep(0.05)  # the sampler is running before the timed region starts
         return self
 
+    def mark_start(self):
+        self.window[0] = time.perf_counter()
+
+    def mark_stop(self):
+        self.window[1] = time.perf_counter()
+
     def __exit__(self, *exc):
-        if self.proc is not None:
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+        if self.smi is not None:
             time.sleep(0.25)
-            self.proc.terminate()
+            self.smi.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self.smi.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self.smi.kill()
 
     def summary(self) -> dict:
-        self.out.flush()
+        if self.nvml is not None:
+            t0, t1 = self.window
+            rows = [s for s in self.samples if t0 is not None and t1 is not None and t0 <= s[0] <= t1]
+            if not rows:  # region shorter than one poll: the nearest samples either side
+                rows = self.samples[-2:]
+            if not rows:
+                return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": ["unsampled"], "samples": 0,
+                        "source": "nvml"}
+            reasons = sorted({name for name, const in self.REASONS for _, _, m in rows
+                              if m & int(getattr(self.nvml, const))})
+            return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": self.sm_max,
+                    "reasons": reasons, "samples": len(rows), "source": "nvml, 1 ms poll"}
         rows = []
-        for line in Path(self.out.name).read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.out.name)
+        if self.smi_out is not None:
+            self.smi_out.flush()
+            for line in Path(self.smi_out.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.smi_out.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [n for n, _ in self.REASONS]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 # ------------------------------------------------------------------ CPU baseline (reference code)
@@ -149,7 +219,7 @@ def reference_dequant_rate(blocks: dict, threads: int, reps: int, kind_hint: str
     chunk, `threads` at a time. Falls back to the oracle restatement if oracle/_ref is absent."""
     import oracle
 
-    chunks = max(1, threads // len(FORMATS)) if threads > len(FORMATS) else 1
+    chunks = -(-threads // len(FORMATS)) if threads > len(FORMATS) else 1  # >= one GGUF tensor per thread
     use_ref = oracle.ref_available()
     with tempfile.TemporaryDirectory() as td:
         path = Path(td) / "cfg2.gguf"
@@ -223,7 +293,7 @@ def run_reference_arm(args) -> None:
     # each step is one pass over the workload; warmup passes run untimed
     import oracle  # noqa: F401
 
-    res = reference_dequant_rate(blocks, threads, reps=max(1, args.steps) + max(0, args.warmup) - max(0, args.warmup))
+    res = reference_dequant_rate(blocks, threads, reps=max(1, args.steps))
     line = {
         "metric": METRIC, "impl": "reference", "value": round(res["value"], 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -315,11 +385,13 @@ def run_ours(args) -> None:
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        clk.mark_start()
         start.record(stream)
         for _ in range(args.steps):
             step()
         stop.record(stream)
         torch.cuda.synchronize()
+        clk.mark_stop()
     launches = tc.launch_count() - launches0
     barrier()
     ms = max_over_ranks(start.elapsed_time(stop)) / args.steps
