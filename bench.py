@@ -345,9 +345,8 @@ def run_ours(args) -> None:
     staging = {t: torch.empty_like(d_blocks[t]) for t in FORMATS}
     readback = torch.empty(len(FORMATS) * 32, dtype=torch.float32).pin_memory()
 
-    def step():
-        # one launch for the whole step: the batched entry point a model loader uses
-        tc.dequantize_many([(t, d_blocks[t], d_out[t]) for t in FORMATS])
+    # one launch for the whole step: the batched entry point a model loader uses
+    step = tc.DequantBatch([(t, d_blocks[t], d_out[t]) for t in FORMATS])
 
     def per_format_launch_us(reps: int) -> dict:
         """Per-format launch times (one tensor per launch), CUDA events on the launching stream."""
@@ -431,9 +430,12 @@ def run_ours(args) -> None:
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": readback.numel() * 4,
            "ms_per_step": round(e2e_ms, 4), "api": "trc_cuda_load_quant (host packed -> device F32)"}
 
-    # ---- secondary: the mul_mat workloads (tensor cores)
-    secondary = None
+    # ---- secondary: the whole-model dequant (cfg3) and the mul_mat workloads (tensor cores)
+    secondary = whole = None
     if not args.no_secondary:
+        whole = run_whole_model(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
+        if world > 1:
+            whole["all_gather"] = run_gather(tc, torch, rank, world, barrier, max_over_ranks, args)
         secondary = run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
 
     cpu = None
@@ -457,6 +459,8 @@ def run_ours(args) -> None:
                          "per_format_single_tensor_launches": per_format},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "gpu_launches": launches,
         }
+        if whole is not None:
+            line["whole_model"] = whole
         if secondary is not None:
             line["mul_mat"] = secondary
         print(json.dumps(line), flush=True)
@@ -478,6 +482,222 @@ def run_only(args) -> None:
     tc.lib()
     res = run_gemm_workloads(tc, torch, 0, 1, lambda: None, lambda x: x, measured_peaks(), args)
     print(json.dumps({"only": args.only, "mul_mat": res}), flush=True)
+
+
+def ref_dequant_seconds(items, reps: int = 3) -> dict:
+    """Median seconds of train.cpp's own gguf_tensor_to_f32 (oracle/_ref, one host thread) per
+    tensor: items are (name, type, ne0, ne1, packed numpy blocks). None if oracle/_ref is absent."""
+    import oracle
+
+    if not oracle.ref_available():
+        return None
+    L = oracle.ref_lib()
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        path = Path(td) / "sample.gguf"
+        synth.write_gguf(path, [(n, t, (ne0, ne1), b) for n, t, ne0, ne1, b in items])
+        handle = L.ref_gguf_open(str(path).encode())
+        try:
+            for n, t, ne0, ne1, _ in items:
+                dst = np.empty(ne0 * ne1, dtype=np.float32)
+                L.ref_gguf_tensor_to_f32(handle, n.encode(), dst.ctypes.data, ne0 * ne1)  # page in
+                times = []
+                for _ in range(reps):
+                    t0 = time.perf_counter()
+                    L.ref_gguf_tensor_to_f32(handle, n.encode(), dst.ctypes.data, ne0 * ne1)
+                    times.append(time.perf_counter() - t0)
+                out[n] = statistics.median(times)
+        finally:
+            L.ref_gguf_close(handle)
+    return out
+
+
+def run_whole_model(tc, torch, rank, world, barrier, max_over_ranks, peaks, args) -> dict:
+    """Whole-model dequant (the Llama-7B-shaped GGUF: 226 tensors, 6.74 G weights, 31.87 GB of
+    algorithmic traffic), sharded by tensor across ranks with the byte-balanced LPT partition and
+    no collective. Total work is fixed, so this is strong scaling. Packed blocks are drawn on the
+    device (seeded), then checked against the oracle on a slice of every tensor class."""
+    import sharding
+    import oracle
+
+    stream = torch.cuda.current_stream()
+    tensors = synth.llama7b_tensors()
+    sizes = [algorithmic_bytes(t, ne[0] * ne[1] // 32) for _, t, ne in tensors]
+    shards = sharding.lpt_shards(sizes, world)
+    mine = shards[rank]
+    gen = torch.Generator(device="cuda").manual_seed(7000 + rank)
+    packed, outs, jobs = [], [], []
+    for i in mine:
+        _, t, ne = tensors[i]
+        nb = ne[0] * ne[1] // 32
+        b = synth.random_blocks_torch(t, nb, gen, "cuda")
+        o = torch.empty(nb * 32, dtype=torch.float32, device="cuda")
+        packed.append(b)
+        outs.append(o)
+        jobs.append((t, b, o))
+    batch = tc.DequantBatch(jobs)
+    batch()
+    torch.cuda.synchronize()
+    # correctness guard: the first 2048 blocks of the first tensor of each type, bit-exact
+    seen = set()
+    for (t, b, o) in jobs:
+        if t in seen:
+            continue
+        seen.add(t)
+        nb = min(2048, o.numel() // 32)
+        want = oracle.dequant(t, b[: nb * synth.BLOCK_BYTES[t]].cpu().numpy(), nb)
+        got = o[: nb * 32].cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"whole-model dequant mismatch, type {t}"
+
+    for _ in range(max(3, args.warmup)):
+        batch()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 20))
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = tc.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(reps):
+        batch()
+    e.record(stream)
+    torch.cuda.synchronize()
+    launches = (tc.launch_count() - launches0) // reps
+    barrier()
+    my_ms = a.elapsed_time(e) / reps
+    ms = max_over_ranks(my_ms)
+    total = sum(sizes)
+    res = {
+        "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "scaling": "strong", "total_bytes": total, "tensors": len(tensors),
+        "rank0_tensors": len(shards[0]), "rank0_bytes": sum(sizes[i] for i in shards[0]),
+        "lpt_imbalance": round(sharding.imbalance(sizes, shards), 4),
+        "per_gpu_frac_of_hbm": round(sum(sizes[i] for i in mine) / (my_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+        "launches_per_step": launches, "steps": reps,
+        "workload": "Llama-7B-shaped GGUF: Q8_0 attention, Q4_0 MLP, Q5_1 embedding/output; "
+                    "device-resident packed blocks, LPT shard by tensor",
+    }
+
+    # end to end: packed bytes from pinned host memory through trc_cuda_load_quant, one staging
+    # buffer per stream-ordered tensor, plus a readback of one block per tensor
+    pinned = [b.cpu().pin_memory() for b in packed]
+    staging = torch.empty(max(b.numel() for b in packed), dtype=torch.uint8, device="cuda")
+    readback = torch.empty(len(jobs) * 32, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        for i, (t, _, o) in enumerate(jobs):
+            tc.gguf_load_tensor(t, pinned[i], o, staging)
+        for i, (_, _, o) in enumerate(jobs):
+            readback[i * 32:(i + 1) * 32].copy_(o[:32], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e2e_reps = max(2, min(args.steps, 5))
+    barrier()
+    a.record(stream)
+    for _ in range(e2e_reps):
+        e2e_step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(a.elapsed_time(e) / e2e_reps)
+    res["e2e"] = {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                  "h2d_bytes_per_step": sum(b.numel() for b in packed), "d2h_bytes_per_step": readback.numel() * 4,
+                  "steps": e2e_reps, "api": "trc_cuda_load_quant per tensor (host packed -> device F32)"}
+    del pinned, staging, packed, outs, jobs, batch
+
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # bounded CPU sample: one tensor of each class through the reference, scaled by the counts
+        items = [("q8", synth.TYPE_Q8_0, 4096, 4096), ("q4", synth.TYPE_Q4_0, 4096, 11008),
+                 ("q51", synth.TYPE_Q5_1, 4096, 32000)]
+        counts = {"q8": 128, "q4": 96, "q51": 2}
+        secs = ref_dequant_seconds([(n, t, a0, a1, synth.random_blocks(t, a0 * a1 // 32, seed=99))
+                                    for n, t, a0, a1 in items])
+        if secs is not None:
+            cpu_s = sum(counts[n] * secs[n] for n in counts)
+            res["cpu_baseline"] = {"value": round(total / cpu_s / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                   "kind": "reference",
+                                   "sample": "one tensor of each class (Q8_0 4096x4096, Q4_0 4096x11008, Q5_1 "
+                                             "4096x32000), median of 3, scaled by the class counts 128/96/2",
+                                   "extrapolated_seconds": round(cpu_s, 2)}
+    return res
+
+
+NVLINK_PEER_GBS = 770.0  # peer copy per direction per GPU measured on this pool's B200s (900 nominal)
+
+
+def run_gather(tc, torch, rank, world, barrier, max_over_ranks, args) -> dict:
+    """The path's one collective: a dequantized tensor sharded by rows that every GPU then needs
+    whole (the Q5_1 token embedding, 4096 x 32000, 524 MB of F32). Fused: each rank dequantizes
+    its rows and stores them into every rank's buffer over NVLink in the same launch
+    (trc_cuda_dequant_many_to_peers). Baseline: the same dequant into a local shard followed by
+    NCCL all_gather_into_tensor. Both are checked bit-exact against the oracle on slices."""
+    import torch.distributed as dist
+    import sharding
+    import oracle
+
+    t, ne0, rows = synth.TYPE_Q5_1, 4096, 32000
+    row_bytes = ne0 // 32 * synth.BLOCK_BYTES[t]
+    gen = torch.Generator(device="cuda").manual_seed(5151)  # the same packed tensor on every rank
+    packed = synth.random_blocks_torch(t, rows * ne0 // 32, gen, "cuda")
+    rr = sharding.plane_range(rows, rank, world)
+    mine = packed[rr.start * row_bytes: rr.stop * row_bytes]
+    f32_bytes = rows * ne0 * 4
+    buf = tc.PeerBuffer(f32_bytes)
+    full = buf.tensor()
+    jobs = [(t, mine, full[rr.start * ne0: rr.stop * ne0])]
+    shard = torch.empty((rr.stop - rr.start) * ne0, dtype=torch.float32, device="cuda")
+    full_nccl = torch.empty(rows * ne0, dtype=torch.float32, device="cuda")
+
+    def fused():
+        tc.dequantize_to_peers(jobs, buf)
+
+    def nccl():
+        tc.gguf_tensor_to_f32(t, mine, out=shard)
+        dist.all_gather_into_tensor(full_nccl, shard)
+
+    stream = torch.cuda.current_stream()
+    reps = max(3, min(args.steps, 20))
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(a.elapsed_time(e) / reps)
+
+    t_fused = timed(fused)
+    t_nccl = timed(nccl)
+    # parity: the first 1024 blocks of every rank's shard, in both assembled copies
+    ok = True
+    for r in range(world):
+        lo = sharding.plane_range(rows, r, world).start
+        nb = 1024
+        want = oracle.dequant(t, packed[lo * row_bytes: lo * row_bytes + nb * synth.BLOCK_BYTES[t]].cpu().numpy(), nb)
+        for got in (full, full_nccl):
+            g = got[lo * ne0: lo * ne0 + nb * 32].cpu().numpy()
+            ok = ok and bool(np.array_equal(g.view(np.uint32), want.view(np.uint32)))
+    assert ok, "all-gathered dequant differs from the oracle"
+    barrier()
+    buf.close()
+    egress = (world - 1) / world * f32_bytes  # bytes each rank sends over NVLink
+
+    def line(ms):
+        return {"ms": round(ms, 4), "assembled_GBps_per_rank": round(f32_bytes / (ms * 1e-3) / 1e9, 1),
+                "nvlink_egress_GBps_per_rank": round(egress / (ms * 1e-3) / 1e9, 1),
+                "frac_of_nvlink_peer": round(egress / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4)}
+
+    return {"tensor": "token_embd Q5_1 4096 x 32000 (524 MB F32), rows sharded over ranks",
+            "fused_dequant_to_peers": line(t_fused), "dequant_then_nccl_all_gather": line(t_nccl),
+            "nvlink_peak_GBps": NVLINK_PEER_GBS, "nvlink_peak_source": "measured peer copy per direction (pool)",
+            "steps": reps}
 
 
 def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args) -> dict:
@@ -531,6 +751,8 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         "frac_of_3xtf32_peak": round(3 * flops / step_ms / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
         "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
     }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["linear_q5_0"]["cpu_reference"] = linear_cpu_rates(tc, torch, wq, K, M, X, dY)
     del wq, X, dY, Y, dX, dW
     if only == "linear":
         return out
@@ -558,9 +780,55 @@ def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> 
         "frac_of_3xtf32_peak": round(3 * gflop / (t_f + t_a + t_b) / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
         "shape": f"A [128,2048,8,{p3}] . B [128,2048,32,{p3}] per rank (ne[3] sharded over {world})",
     }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["gqa_bcast"]["cpu_reference"] = gqa_cpu_rates(A, B, G)
     out["peak_3xtf32_tflops"] = round(tf32x3_peak, 1) if tf32x3_peak else None
     out["peak_note"] = "TF32 dense taken as half the measured bf16 burst rate; 3 passes"
     return out
+
+
+def _ref_gflops(a_base, a_trans, b_base, b_trans, flops: float) -> float | None:
+    """GFLOP/s of train.cpp's CPU mul_mat (oracle/_ref, one thread) on one slice, best of 2."""
+    import oracle
+
+    if not oracle.ref_available():
+        return None
+    best = None
+    for _ in range(2):
+        t0 = time.perf_counter()
+        oracle.ref_mul_mat(a_base, a_trans, b_base, b_trans)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return round(flops / best / 1e9, 3)
+
+
+def linear_cpu_rates(tc, torch, wq, K, M, X, dY) -> dict:
+    """The reference CPU backend on deterministic slices of the Linear step (it would take hours
+    in full): forward on 16 token columns, dX on 4, dW on 4 of its K columns."""
+    W = tc.gguf_tensor_to_f32(synth.TYPE_Q5_0, wq).view(M, K).cpu().numpy()
+    Xn, dYn = X.cpu().numpy(), dY.cpu().numpy()
+    return {
+        "fwd_gflops": _ref_gflops(W, False, Xn[:16], False, 2.0 * K * M * 16),
+        "dx_gflops": _ref_gflops(W, True, dYn[:4], False, 2.0 * K * M * 4),
+        "dw_gflops": _ref_gflops(dYn, True, np.ascontiguousarray(Xn[:, :4]), True, 2.0 * X.shape[0] * M * 4),
+        "cores": 1, "kind": "reference",
+        "sample": "forward: 16 of 2048 token columns; dX: 4 columns; dW: 4 of 4096 output columns",
+    }
+
+
+def gqa_cpu_rates(A, B, G) -> dict:
+    """The reference CPU backend on one (i2, i3) plane of the GQA workload, sliced for the
+    transposed-view backward products."""
+    a = A[0, 0].cpu().numpy()          # [2048, 128]: ne [128, 2048]
+    b = B[0, 0].cpu().numpy()
+    g = G[0, 0].cpu().numpy()          # [2048, 2048]
+    return {
+        "fwd_gflops": _ref_gflops(a, False, b, False, 2.0 * 128 * 2048 * 2048),
+        "da_gflops": _ref_gflops(g, True, np.ascontiguousarray(b[:, :16]), True, 2.0 * 2048 * 2048 * 16),
+        "db_gflops": _ref_gflops(a, True, np.ascontiguousarray(g[:64]), False, 2.0 * 2048 * 128 * 64),
+        "cores": 1, "kind": "reference",
+        "sample": "one plane; forward in full, dA on 16 of 128 columns, dB on 64 of 2048 columns",
+    }
 
 
 def main() -> None:

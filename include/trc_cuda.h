@@ -109,6 +109,20 @@ typedef struct trc_cuda_dequant_job {
  * gguf_load_tensor (src/io/trc_gguf.cpp:1051-1094) for each tensor, minus the host F32 copy. */
 int trc_cuda_dequant_many(const trc_cuda_dequant_job* jobs, int n_jobs, void* stream);
 
+/* Dequantize-and-all-gather: trc_cuda_dequant_many whose every output float is also written, in
+ * the same launch, at the same offset of up to 8 peer GPUs' buffers over NVLink. Each job's `out`
+ * lies in the local buffer starting at `local_base`; its copy on peer p is at
+ * peer_bases[p] + (out - local_base), peer_bases being the peers' buffers mapped into this
+ * process by trc_cuda_rt_ipc_open (plain peer stores, no multicast). With every rank
+ * dequantizing its own rows of a tensor, one call per rank leaves the whole F32 tensor on every
+ * GPU: the NCCL all-gather a sharded dequantized tensor would otherwise need, fused into the
+ * dequant kernel's stores. The copies are complete when the launch is: synchronize the stream,
+ * then barrier across the ranks before a peer reads. EINVAL when n_peers is outside 0..8, a peer
+ * base is null or not a multiple of 16 bytes away from local_base, or an output lies below
+ * local_base. */
+int trc_cuda_dequant_many_to_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base,
+                                   void* const* peer_bases, int n_peers, void* stream);
+
 /* Device-side gguf_load_tensor for a quantized tensor with an F32 destination
  * (src/io/trc_gguf.cpp:1082-1089): copies the packed blocks from HOST memory `host_blocks` into
  * the caller's device staging buffer (>= n_blocks*block_bytes bytes, 16-byte aligned), then

@@ -39,6 +39,18 @@ int trc_cuda_rt_stream_create(void** stream);           /* non-blocking stream o
 int trc_cuda_rt_stream_destroy(void* stream);
 int trc_cuda_rt_stream_sync(void* stream);
 
+/* Peer memory between the processes of one node (one process per GPU), for the dequant
+ * all-gather over NVLink (trc_cuda_dequant_many_to_peers). Plain CUDA IPC mappings: peer loads
+ * and stores, no multicast object. ptr must be the base of a trc_cuda_rt_malloc allocation; the
+ * handle is TRC_CUDA_IPC_HANDLE_BYTES opaque bytes that another process passes to
+ * trc_cuda_rt_ipc_open, which maps the allocation into the current device's address space
+ * (peer access enabled on first use). trc_cuda_rt_ipc_close unmaps it. */
+#define TRC_CUDA_IPC_HANDLE_BYTES 64
+int trc_cuda_rt_ipc_get_handle(void* ptr, void* handle);
+int trc_cuda_rt_ipc_open(const void* handle, void** ptr);
+int trc_cuda_rt_ipc_close(void* ptr);
+int trc_cuda_rt_can_access_peer(int device, int peer, int* can_access);
+
 #ifdef __cplusplus
 }
 #endif

@@ -110,6 +110,32 @@ def test_batched_jobs_whole_model_slice(tc):
         assert bits_equal(o.cpu().numpy(), w)
 
 
+def test_prepared_batch_replays_and_spans_launches(tc):
+    """DequantBatch: 300 jobs (more than one launch holds) built once and replayed; each replay
+    rewrites every output bit-exactly, device-generated blocks included."""
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    jobs, outs = [], []
+    for i in range(300):
+        t = TYPES[i % len(TYPES)]
+        n_blocks = 4096 // 32 + (i % 7) * 3
+        b = synth.random_blocks_torch(t, n_blocks, gen, "cuda")
+        o = torch.empty(n_blocks * 32, dtype=torch.float32, device="cuda")
+        jobs.append((t, b, o))
+        outs.append(o)
+    batch = tc.DequantBatch(jobs)
+    assert len(batch) == 300
+    launches = tc.launch_count()
+    batch()
+    assert tc.launch_count() - launches == 2
+    for o in outs:
+        o.fill_(float("nan"))
+    batch()
+    torch.cuda.synchronize()
+    for (t, b, o) in jobs[::23]:
+        assert bits_equal(o.cpu().numpy(), oracle.dequant(t, b.cpu().numpy()))
+    assert tc.device_error() == 0
+
+
 def test_load_from_pinned_host(tc):
     t = synth.TYPE_Q5_0
     n_blocks = 4096 * 64 // 32

@@ -107,6 +107,11 @@ int trc_cuda_dequant_many(const trc_cuda_dequant_job* jobs, int n_jobs, void* st
     return dequant_jobs(jobs, n_jobs, static_cast<cudaStream_t>(stream));
 }
 
+int trc_cuda_dequant_many_to_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base,
+                                   void* const* peer_bases, int n_peers, void* stream) {
+    return dequant_jobs_peers(jobs, n_jobs, local_base, peer_bases, n_peers, static_cast<cudaStream_t>(stream));
+}
+
 int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
                         void* stream) {
     const size_t bb = trc_cuda_block_bytes(type);

@@ -35,6 +35,7 @@ constexpr int kRun       = 256;       // blocks per run
 constexpr int kMaxBlk    = 34;        // largest block (Q8_0)
 constexpr int kMaxJobs   = 256;       // jobs per launch (kernel parameter of ~10 KiB)
 constexpr int kBufBytes  = kRun * kMaxBlk;
+constexpr int kMaxPeers  = 8;         // copies of each output written to other GPUs' buffers
 
 struct DqJob {
     const uint8_t* src;
@@ -48,7 +49,9 @@ struct DqJob {
 struct DqBatch {
     DqJob   job[kMaxJobs];
     int32_t n_jobs;
+    int32_t n_peers;                // PEERS kernels: copies written besides `out`
     int64_t total_runs;
+    int64_t peer_delta[kMaxPeers];  // byte distance from a job's out to its copy in peer p's buffer
 };
 
 __device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
@@ -59,8 +62,12 @@ __device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
     return (addr & 15u) == 0 && (bytes & 15) == 0;
 }
 
-template <int TYPE>
-__device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, int64_t b0, int nblk) {
+// PEERS: every quad is also stored at the same offset of each peer GPU's buffer (peer-mapped
+// addresses, plain stores over NVLink), which fuses the all-gather of a sharded tensor into its
+// dequantization.
+template <int TYPE, bool PEERS>
+__device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, int64_t b0, int nblk,
+                                           const DqBatch& batch) {
     constexpr int kBB = QuantTraits<TYPE>::kBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = lane & 7;
@@ -72,16 +79,28 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
             float w[4];
             decode_quad<TYPE>(buf + lb * kBB, c, w);
             float* o = J.out + (b0 + lb) * 32 + 4 * c;
+            const float4 v = make_float4(w[0], w[1], w[2], w[3]);
             if (vec_ok) {
                 // streaming store: the output is written once and read by a later kernel
-                __stcs(reinterpret_cast<float4*>(o), make_float4(w[0], w[1], w[2], w[3]));
+                __stcs(reinterpret_cast<float4*>(o), v);
             } else {
                 o[0] = w[0]; o[1] = w[1]; o[2] = w[2]; o[3] = w[3];
+            }
+            if constexpr (PEERS) {
+                for (int p = 0; p < batch.n_peers; ++p) {
+                    float* q = reinterpret_cast<float*>(reinterpret_cast<char*>(o) + batch.peer_delta[p]);
+                    if (vec_ok) {
+                        *reinterpret_cast<float4*>(q) = v;  // deltas are multiples of 16
+                    } else {
+                        q[0] = w[0]; q[1] = w[1]; q[2] = w[2]; q[3] = w[3];
+                    }
+                }
             }
         }
     }
 }
 
+template <bool PEERS>
 __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DqBatch batch) {
     __shared__ __align__(128) uint8_t buf[2][kBufBytes];
     __shared__ __align__(8) uint64_t bar[2];
@@ -93,8 +112,9 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     }
     __syncthreads();
 
-    uint32_t phase[2]   = {0u, 0u};
-    bool     pending[2] = {false, false};
+    // Per slot s, bit s: the mbarrier phase to wait for, and whether a bulk copy is in flight
+    // (bit masks, so that the per-slot state stays in registers).
+    uint32_t phase_bits = 0u, pending_bits = 0u;
     int      jcur       = 0;  // job cursor (runs only increase for a CTA)
 
     auto locate = [&](int64_t run, int& j) {
@@ -116,7 +136,7 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
         locate(run, jcur);
         if (run_bulk_ok(batch.job[jcur], run - batch.job[jcur].run_begin)) {
             if (threadIdx.x == 0) issue(run, jcur, 0);
-            pending[0] = true;
+            pending_bits |= 1u;
         }
     }
     for (; run < batch.total_runs && ok; run += gridDim.x, ++it) {
@@ -135,16 +155,16 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
             locate(next, jn);
             if (run_bulk_ok(batch.job[jn], next - batch.job[jn].run_begin)) {
                 if (threadIdx.x == 0) issue(next, jn, slot ^ 1);
-                pending[slot ^ 1] = true;
+                pending_bits |= 1u << (slot ^ 1);
             }
         }
 
-        if (pending[slot]) {
-            const bool mine = mbar_wait(&bar[slot], phase[slot], TRC_DEVERR_WAIT_BULK);
+        if ((pending_bits >> slot) & 1u) {
+            const bool mine = mbar_wait(&bar[slot], (phase_bits >> slot) & 1u, TRC_DEVERR_WAIT_BULK);
             ok = __syncthreads_and(mine ? 1 : 0) != 0;  // every thread takes the same branch
             if (mine) {
-                phase[slot] ^= 1u;
-                pending[slot] = false;
+                phase_bits ^= 1u << slot;
+                pending_bits &= ~(1u << slot);
             }
             if (!ok) break;
         } else {
@@ -155,26 +175,42 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
         }
 
         switch (J.type) {
-            case 2: decode_run<2>(buf[slot], J, b0, nblk); break;
-            case 3: decode_run<3>(buf[slot], J, b0, nblk); break;
-            case 6: decode_run<6>(buf[slot], J, b0, nblk); break;
-            case 7: decode_run<7>(buf[slot], J, b0, nblk); break;
-            case 8: decode_run<8>(buf[slot], J, b0, nblk); break;
+            case 2: decode_run<2, PEERS>(buf[slot], J, b0, nblk, batch); break;
+            case 3: decode_run<3, PEERS>(buf[slot], J, b0, nblk, batch); break;
+            case 6: decode_run<6, PEERS>(buf[slot], J, b0, nblk, batch); break;
+            case 7: decode_run<7, PEERS>(buf[slot], J, b0, nblk, batch); break;
+            case 8: decode_run<8, PEERS>(buf[slot], J, b0, nblk, batch); break;
             default: break;
         }
         __syncthreads();
     }
     // Never leave the CTA with a bulk copy still writing into its shared memory.
     for (int s = 0; s < 2; ++s) {
-        if (pending[s]) mbar_wait_drain(&bar[s], phase[s]);
+        if ((pending_bits >> s) & 1u) mbar_wait_drain(&bar[s], (phase_bits >> s) & 1u);
     }
+    // The peer copies are visible to every GPU before the grid counts as complete.
+    if constexpr (PEERS) __threadfence_system();
 }
 
 }  // namespace
 
 int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream) {
+    return dequant_jobs_peers(jobs, n_jobs, nullptr, nullptr, 0, stream);
+}
+
+int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base,
+                       void* const* peer_bases, int n_peers, cudaStream_t stream) {
     static_assert(sizeof(DqBatch) < 32000, "kernel parameter limit");
     if (n_jobs < 0 || (n_jobs > 0 && jobs == nullptr)) return TRC_CUDA_EINVAL;
+    if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && (peer_bases == nullptr || local_base == nullptr)))
+        return TRC_CUDA_EINVAL;
+    int64_t deltas[kMaxPeers] = {};
+    for (int p = 0; p < n_peers; ++p) {
+        if (peer_bases[p] == nullptr) return TRC_CUDA_EINVAL;
+        deltas[p] = static_cast<int64_t>(reinterpret_cast<uintptr_t>(peer_bases[p]) -
+                                         reinterpret_cast<uintptr_t>(local_base));
+        if ((deltas[p] & 15) != 0) return TRC_CUDA_EINVAL;  // copies keep the outputs' 16-byte alignment
+    }
     // Validate every job before touching the device.
     bool any_work = false;
     for (int i = 0; i < n_jobs; ++i) {
@@ -185,6 +221,8 @@ int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stre
         if (in.blocks == nullptr || in.out == nullptr) return TRC_CUDA_EINVAL;
         if ((reinterpret_cast<uint64_t>(in.blocks) & 1u) != 0 || (reinterpret_cast<uint64_t>(in.out) & 3u) != 0)
             return TRC_CUDA_EINVAL;  // fp16 fields need 2-byte, floats 4-byte alignment
+        if (n_peers > 0 && reinterpret_cast<uintptr_t>(in.out) < reinterpret_cast<uintptr_t>(local_base))
+            return TRC_CUDA_EINVAL;  // outputs lie in the local buffer that the peers mirror
         any_work = true;
     }
     if (!any_work) return TRC_CUDA_OK;
@@ -193,6 +231,8 @@ int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stre
     for (int first = 0; first < n_jobs; first += kMaxJobs) {
         DqBatch batch;
         batch.n_jobs    = 0;
+        batch.n_peers   = n_peers;
+        for (int p = 0; p < kMaxPeers; ++p) batch.peer_delta[p] = deltas[p];
         int64_t runs    = 0;
         const int count = std::min(kMaxJobs, n_jobs - first);
         for (int i = 0; i < count; ++i) {
@@ -211,7 +251,8 @@ int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stre
         if (batch.n_jobs == 0) continue;
         batch.total_runs = runs;
         const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * 8);
-        dequant_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
+        if (n_peers > 0) dequant_kernel<true><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
+        else dequant_kernel<false><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
         note_launch();
         const int st = check_launch();
         if (st != TRC_CUDA_OK) return st;

@@ -108,4 +108,33 @@ int trc_cuda_rt_stream_destroy(void* stream) { return rt(cudaStreamDestroy(stati
 
 int trc_cuda_rt_stream_sync(void* stream) { return rt(cudaStreamSynchronize(static_cast<cudaStream_t>(stream))); }
 
+static_assert(sizeof(cudaIpcMemHandle_t) == TRC_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+
+int trc_cuda_rt_ipc_get_handle(void* ptr, void* handle) {
+    if (ptr == nullptr || handle == nullptr) return TRC_CUDA_EINVAL;
+    cudaIpcMemHandle_t h;
+    const int st = rt(cudaIpcGetMemHandle(&h, ptr));
+    if (st == TRC_CUDA_OK) std::memcpy(handle, &h, sizeof(h));
+    return st;
+}
+
+int trc_cuda_rt_ipc_open(const void* handle, void** ptr) {
+    if (handle == nullptr || ptr == nullptr) return TRC_CUDA_EINVAL;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    return rt(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int trc_cuda_rt_ipc_close(void* ptr) {
+    if (ptr == nullptr) return TRC_CUDA_EINVAL;
+    return rt(cudaIpcCloseMemHandle(ptr));
+}
+
+int trc_cuda_rt_can_access_peer(int device, int peer, int* can_access) {
+    if (can_access == nullptr) return TRC_CUDA_EINVAL;
+    *can_access = 0;
+    return rt(cudaDeviceCanAccessPeer(can_access, device, peer));
+}
+
 }  // extern "C"

@@ -57,6 +57,8 @@ int sm_count_current();
 
 // Per-library entry points implemented in the individual .cu files.
 int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream);
+int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base, void* const* peer_bases,
+                       int n_peers, cudaStream_t stream);
 int mul_mat_simt(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate,
                  cudaStream_t stream);
 // Returns TRC_CUDA_EUNSUPPORTED when the layout cannot be fed by TMA (caller then uses SIMT).

@@ -64,6 +64,40 @@ def random_blocks(qtype: int, n_blocks: int, seed: int, d_range=(1e-3, 1e-2), m_
     return out.reshape(-1)
 
 
+def random_blocks_torch(qtype: int, n_blocks: int, generator, device) -> "torch.Tensor":
+    """random_blocks' distributions drawn on the device with a seeded torch generator (for the
+    multi-GB whole-model workload; the bytes differ from the numpy draw). Returns a uint8 tensor
+    of n_blocks * block_bytes."""
+    import torch
+
+    bb = BLOCK_BYTES[qtype]
+    out = torch.empty((n_blocks, bb), dtype=torch.uint8, device=device)
+
+    def f16_bytes(lo: float, hi: float) -> "torch.Tensor":
+        x = torch.rand(n_blocks, generator=generator, device=device, dtype=torch.float32) * (hi - lo) + lo
+        return x.to(torch.float16).view(torch.uint8).view(n_blocks, 2)
+
+    def rand_bytes(n: int) -> "torch.Tensor":
+        return torch.randint(0, 256, (n_blocks, n), generator=generator, device=device, dtype=torch.uint8)
+
+    out[:, 0:2] = f16_bytes(1e-3, 1e-2)
+    if qtype == TYPE_Q4_0:
+        out[:, 2:18] = rand_bytes(16)
+    elif qtype == TYPE_Q4_1:
+        out[:, 2:4] = f16_bytes(-0.05, 0.05)
+        out[:, 4:20] = rand_bytes(16)
+    elif qtype == TYPE_Q5_0:
+        out[:, 2:22] = rand_bytes(20)
+    elif qtype == TYPE_Q5_1:
+        out[:, 2:4] = f16_bytes(-0.05, 0.05)
+        out[:, 4:24] = rand_bytes(20)
+    elif qtype == TYPE_Q8_0:
+        out[:, 2:34] = rand_bytes(32)  # every byte value is an int8 in [-128, 127]
+    else:
+        raise ValueError(f"not a legacy quantized type: {qtype}")
+    return out.view(-1)
+
+
 def normal(shape, seed: int, sigma: float = 1.0) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(seed))
     return (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(sigma)).astype(np.float32)

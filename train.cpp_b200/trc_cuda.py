@@ -90,6 +90,13 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_sum_workspace_bytes": (SZ, [I64]),
         "trc_cuda_sum": (I, [VP, P, P, SZ, P]),
         "trc_cuda_fill": (I, [P, I64, ctypes.c_float, P]),
+        "trc_cuda_dequant_many_to_peers": (I, [ctypes.POINTER(DequantJob), I, P, ctypes.POINTER(P), I, P]),
+        "trc_cuda_rt_malloc": (I, [ctypes.POINTER(P), SZ]),
+        "trc_cuda_rt_free": (I, [P]),
+        "trc_cuda_rt_ipc_get_handle": (I, [P, P]),
+        "trc_cuda_rt_ipc_open": (I, [P, ctypes.POINTER(P)]),
+        "trc_cuda_rt_ipc_close": (I, [P]),
+        "trc_cuda_rt_can_access_peer": (I, [I, I, ctypes.POINTER(I)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -181,8 +188,108 @@ def gguf_tensor_to_f32(qtype: int, blocks: torch.Tensor, n_elems: int | None = N
     return out
 
 
+class DequantBatch:
+    """A prepared batch of dequant jobs (qtype, packed uint8 CUDA tensor, F32 output): the job
+    array is built and checked once, and each call is one trc_cuda_dequant_many (one kernel
+    launch per 256 jobs) with no per-job host work -- what a model loader replays per step."""
+
+    def __init__(self, jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]]):
+        self._keep = [(b, o) for _, b, o in jobs]  # the tensors must outlive the array
+        self._arr = (DequantJob * max(1, len(jobs)))()
+        self._n = len(jobs)
+        for i, (qtype, blocks, out) in enumerate(jobs):
+            bb = block_bytes(qtype)
+            if bb == 0:
+                raise TrcCudaError(f"type {qtype} is not a legacy quantized type")
+            self._arr[i].blocks = blocks.data_ptr()
+            self._arr[i].out = out.data_ptr()
+            self._arr[i].n_blocks = out.numel() // QK
+            self._arr[i].type = qtype
+            if blocks.numel() < self._arr[i].n_blocks * bb:
+                raise TrcCudaError("packed buffer is smaller than its output")
+
+    def __len__(self) -> int:
+        return self._n
+
+    def __call__(self, stream=None) -> None:
+        _check(lib().trc_cuda_dequant_many(self._arr, self._n, _stream(stream)), "trc_cuda_dequant_many")
+
+
 def dequantize_many(jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]], stream=None) -> None:
     """Batched device dequantization: jobs of (qtype, packed uint8 CUDA tensor, F32 output)."""
+    DequantBatch(jobs)(stream)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over raw device memory, so torch.as_tensor can wrap it."""
+
+    def __init__(self, ptr: int, shape, typestr: str, owner):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None, "stream": None}
+        self._owner = owner
+
+
+class PeerBuffer:
+    """One device buffer per rank of a process group (one process per GPU on one node), each
+    mapped into every other rank's address space with CUDA IPC: `bases[r]` is rank r's buffer as
+    this process addresses it (plain peer loads and stores over NVLink; no multicast object).
+    Allocated with trc_cuda_rt_malloc so that the IPC handle covers exactly this buffer.
+    Collective: every rank of `group` constructs it with the same nbytes, and calls close()."""
+
+    def __init__(self, nbytes: int, group=None):
+        import torch.distributed as dist
+
+        L = lib()
+        self.nbytes = int(nbytes)
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        ptr = ctypes.c_void_p()
+        _check(L.trc_cuda_rt_malloc(ctypes.byref(ptr), self.nbytes), "trc_cuda_rt_malloc")
+        self.ptr = ptr.value
+        self._opened: list[int] = []
+        handle = (ctypes.c_ubyte * IPC_HANDLE_BYTES)()
+        _check(L.trc_cuda_rt_ipc_get_handle(ctypes.c_void_p(self.ptr), handle), "trc_cuda_rt_ipc_get_handle")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(self.ptr)
+                continue
+            raw = (ctypes.c_ubyte * IPC_HANDLE_BYTES).from_buffer_copy(h)
+            peer = ctypes.c_void_p()
+            _check(L.trc_cuda_rt_ipc_open(raw, ctypes.byref(peer)), "trc_cuda_rt_ipc_open")
+            self.bases.append(peer.value)
+            self._opened.append(peer.value)
+
+    def tensor(self, dtype=torch.float32) -> torch.Tensor:
+        """The local buffer as a flat torch CUDA tensor (no copy; valid until close())."""
+        item = torch.empty((), dtype=dtype).element_size()
+        typestr = {torch.float32: "<f4", torch.uint8: "|u1", torch.int32: "<i4"}[dtype]
+        return torch.as_tensor(_DeviceArray(self.ptr, (self.nbytes // item,), typestr, self),
+                               device=f"cuda:{torch.cuda.current_device()}")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this one. Call after a barrier, when no rank still
+        writes into another's buffer."""
+        if self.ptr is None:
+            return
+        L = lib()
+        for p in self._opened:
+            L.trc_cuda_rt_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        L.trc_cuda_rt_free(ctypes.c_void_p(self.ptr))
+        self.ptr = None
+
+
+def dequantize_to_peers(jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]], buf: PeerBuffer,
+                        stream=None) -> None:
+    """Dequantize jobs whose F32 outputs lie in buf's local buffer and write every output at the
+    same offset of every other rank's buffer as well (trc_cuda_dequant_many_to_peers): the
+    all-gather of a row-sharded tensor fused into its dequantization, one launch per rank."""
     arr = (DequantJob * max(1, len(jobs)))()
     for i, (qtype, blocks, out) in enumerate(jobs):
         bb = block_bytes(qtype)
@@ -192,7 +299,12 @@ def dequantize_many(jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]], stre
         arr[i].type = qtype
         if blocks.numel() < arr[i].n_blocks * bb:
             raise TrcCudaError("packed buffer is smaller than its output")
-    _check(lib().trc_cuda_dequant_many(arr, len(jobs), _stream(stream)), "trc_cuda_dequant_many")
+        if not (buf.ptr <= out.data_ptr() and out.data_ptr() + out.numel() * 4 <= buf.ptr + buf.nbytes):
+            raise TrcCudaError("dequantize_to_peers: an output lies outside the peer buffer")
+    peers = [b for r, b in enumerate(buf.bases) if r != buf.rank]
+    parr = (ctypes.c_void_p * max(1, len(peers)))(*peers)
+    _check(lib().trc_cuda_dequant_many_to_peers(arr, len(jobs), ctypes.c_void_p(buf.ptr), parr, len(peers),
+                                                _stream(stream)), "trc_cuda_dequant_many_to_peers")
 
 
 def gguf_load_tensor(qtype: int, host_blocks, dst: torch.Tensor, staging: torch.Tensor, stream=None) -> None:
