@@ -153,8 +153,11 @@ int trc_cuda_load_quant_static(int type, const void* host_blocks, int64_t n_bloc
 
 enum {
     TRC_CUDA_MM_ACCUMULATE = 1u, /* d += a*b instead of d = a*b */
-    TRC_CUDA_MM_SIMT       = 2u  /* force the fp32 SIMT kernel (exact reference summation order);
+    TRC_CUDA_MM_SIMT       = 2u, /* force the fp32 SIMT kernel (exact reference summation order);
                                     the default picks the tcgen05 3xTF32 kernel when the layout allows */
+    TRC_CUDA_MM_ONE_CTA    = 4u  /* tcgen05 kernel with one CTA per 128 x 256 tile (cta_group::1); the
+                                    default runs 256 x 256 tiles on CTA pairs (cta_group::2, a cluster
+                                    of two SMs sharing the B tile) when M spans more than 128 rows */
 };
 
 /* ggml mul_mat: for every plane (i2, i3) of b,

@@ -29,20 +29,22 @@ def dev(x):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
 
+@pytest.mark.parametrize("one_cta", [False, True], ids=["pair", "one_cta"])
 @pytest.mark.parametrize("transposed", [False, True], ids=["W", "WT"])
 @pytest.mark.parametrize("qtype", TYPES, ids=lambda t: NAMES[t])
-def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed):
+def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed, one_cta):
     w_ne0, w_ne1, n = 512, 400, 136  # W [k=512, m=400]; ragged M/N tiles
     blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=40 + qtype)
     Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)  # numpy (ne1, ne0)
     K = w_ne1 if transposed else w_ne0
     x = np.random.default_rng(qtype).standard_normal((n, K)).astype(np.float32)
     want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, x)
-    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed).cpu().numpy()
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed,
+                       one_cta=one_cta).cpu().numpy()
     assert got.shape == want.shape
     assert normwise(got, want) <= 1e-5
     Wd = tc.gguf_tensor_to_f32(qtype, dev(blocks)).reshape(w_ne1, w_ne0)
-    two_step = tc.mul_mat(Wd.t() if transposed else Wd, dev(x)).cpu().numpy()
+    two_step = tc.mul_mat(Wd.t() if transposed else Wd, dev(x), one_cta=one_cta).cpu().numpy()
     assert normwise(got, two_step) <= 2e-6
     assert tc.device_error() == 0
 

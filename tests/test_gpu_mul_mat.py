@@ -177,3 +177,57 @@ def test_mul_mat_repeat_back(tc, simt, transposed_out, accumulate):
     else:
         assert normwise(np.ascontiguousarray(got), np.ascontiguousarray(want)) <= 1e-5
     assert tc.device_error() == 0
+
+
+# ---- CTA pairs (tcgen05 cta_group::2) against one CTA per tile and the reference
+
+PAIR_SHAPES = [
+    # (K, M, N, a_transposed, b_transposed, planes): M > 128 takes the CTA-pair kernel by default
+    (332, 300, 520, False, False, (1, 1)),    # ragged in every dimension, second CTA's rows partly out
+    (256, 129, 257, False, False, (1, 1)),    # the pair's second CTA holds one row
+    (300, 260, 72, True, True, (1, 1)),       # both operands MN-major (the dW layout)
+    (520, 384, 300, True, False, (2, 3)),     # MN-major A, planes
+    (4096, 512, 512, False, False, (1, 1)),   # several promotion chunks
+]
+
+
+@pytest.mark.parametrize("k,m,n,ta,tb,planes", PAIR_SHAPES)
+def test_cta_pair_matches_single_cta_and_reference(tc, k, m, n, ta, tb, planes):
+    rng = np.random.default_rng(k + m + n)
+    p2, p3 = planes
+    a = rng.standard_normal((p3, p2, m, k) if not ta else (p3, p2, k, m)).astype(np.float32)
+    b = rng.standard_normal((p3, p2, n, k) if not tb else (p3, p2, k, n)).astype(np.float32)
+    want = oracle.mul_mat(npop(a, ta), npop(b, tb))
+    A, B = op(dev(a), ta), op(dev(b), tb)
+    assert tc.mul_mat_kernel(A, B, tc.ggml_empty(tc.mul_mat_out_ne(A, B))) == tc.KERNEL_TCGEN05
+    pair = tc.mul_mat(A, B).cpu().numpy()
+    single = tc.mul_mat(A, B, one_cta=True).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(pair, want) <= TOL, normwise(pair, want)
+    assert normwise(single, want) <= TOL, normwise(single, want)
+    # same tiles' K order and promotion chunks: the two kernels agree to the last bits or close to it
+    assert normwise(pair, single) <= 1e-6
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_cta_pair_transposed_output_accumulate_and_plane_reduction(tc, accumulate):
+    """dA of a broadcast product through a transposed output view with ACCUMULATE (the GQA
+    backward shape, reduced), pair vs single CTA."""
+    rng = np.random.default_rng(7)
+    G = rng.standard_normal((2, 4, 300, 272)).astype(np.float32)      # ne [272, 300, 4, 2]
+    Bm = rng.standard_normal((2, 4, 300, 136)).astype(np.float32)     # ne [136, 300, 4, 2]
+    base = rng.standard_normal((2, 2, 272, 136)).astype(np.float32)   # dA, ne [136, 272, 2, 2]
+    outs = []
+    for one in (False, True):
+        dA = dev(base.copy())
+        # T(dA) (ne [272, 136, 2, 2]) (+)= repeat_back(mul_mat(T(G), T(B)))
+        tc.mul_mat_repeat_back(dev(G).transpose(-1, -2), dev(Bm).transpose(-1, -2), dA.transpose(-1, -2),
+                               accumulate=accumulate, one_cta=one)
+        outs.append(dA.cpu().numpy())
+    prod = oracle.mul_mat(np.swapaxes(G, -1, -2), np.swapaxes(Bm, -1, -2))   # numpy [2, 4, 136, 272]
+    red = oracle.repeat_back(prod, [272, 136, 2, 2])                         # numpy [2, 2, 136, 272]
+    want = np.swapaxes(red, -1, -2) + (base if accumulate else np.float32(0))
+    for got in outs:
+        assert normwise(got, want) <= TOL, normwise(got, want)
+    assert normwise(outs[0], outs[1]) <= 1e-6
+    assert tc.device_error() == 0

@@ -53,24 +53,42 @@ namespace trc {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
-constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
-constexpr int B_BYTES     = BN * BK * 4;                 // 16 KiB
-constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);     // raw + tail = 48 KiB
-constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES, OFF_B_TAIL = 2 * A_BYTES + B_BYTES;
-constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
-constexpr int NUM_THREADS  = 448;
-constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 8, EPI_WARP0 = 10;  // epilogue warps 10-13 cover TMEM quarters 2,3,0,1
+constexpr int BM = 128, BN = 256, BK = 16;   // D tile of one CTA: BM rows (TMEM lanes) x BN columns
+constexpr int NUM_THREADS  = 576;
+// warps 10-17: two epilogue teams of four warps (TMEM lane quarters 2,3,0,1 each); team h owns
+// columns 128h .. 128h+127 of every tile
+constexpr int SPLIT_WARP0 = 2, SPLIT_WARPS = 8, EPI_WARP0 = 10, EPI_WARPS = 8;
 constexpr int TMEM_COLS    = 512;
 constexpr int CHUNK_KB     = 16;   // k-blocks per fp32 promotion chunk (256 K)
 constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128-row x 32-column fp32 group of D, staged for a TMA store
-constexpr int EPI_BUFS      = 2;
-constexpr int EPI_OFF       = STAGES * STAGE_BYTES;
-constexpr int SMEM_BYTES    = STAGES * STAGE_BYTES + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_BUFS      = 2;            // one staging buffer per epilogue team
+constexpr int EPI_BAR_TEAM0 = 1, EPI_BAR_ALL = 3;  // named barriers: per team (1, 2), all epilogue warps (3)
+constexpr int MAX_STAGES    = 6;
+
+// Shared-memory geometry per CTA group. CG = 1: one CTA computes a 128 x 256 tile from a 128-row
+// A tile and a 256-row B tile. CG = 2 (tcgen05 cta_group::2): a cluster of two CTAs computes a
+// 256 x 256 tile; each CTA stages its own 128 rows of A and 128 of the 256 rows of B, and the
+// leader's MMA reads both CTAs' shared memory, so each SM stages and splits half the B bytes.
+template <int CG>
+struct Geo {
+    static constexpr int BN_CTA      = BN / CG;                     // B rows staged by one CTA
+    static constexpr int STAGES      = CG == 2 ? 6 : 4;
+    static constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
+    static constexpr int B_BYTES     = BN_CTA * BK * 4;             // 16 KiB (CG 1) / 8 KiB (CG 2)
+    static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);     // raw + tail
+    static constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES;
+    static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;
+    static constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
+    static constexpr int EPI_OFF     = STAGES * STAGE_BYTES;
+    static constexpr int SMEM_BYTES  = EPI_OFF + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int TILE_M      = CG * BM;                     // D rows per tile
+    static_assert(STAGES <= MAX_STAGES, "barrier arrays");
+    static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
 
 struct TcParams {
     int     M, N, K;           // M: TMEM lanes (rows of D tiles), N: columns, K: reduction
-    int     m_tiles, n_tiles, k_blocks;
+    int     m_tiles, n_tiles, k_blocks;  // m_tiles counts tiles of CG*128 rows
     int     planes2, planes3;  // output planes
     int     red2, red3;        // source planes summed into each output plane (repeat_back fused)
     int     kv_blocks;         // k-blocks per tile: k_blocks x red2 x red3
@@ -90,11 +108,11 @@ struct TcParams {
 };
 
 struct Barriers {
-    uint64_t full[STAGES];
-    uint64_t split[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[MAX_STAGES];   // this CTA's TMA tiles of the stage have landed
+    uint64_t split[MAX_STAGES];  // (leader) every split warp of the group has written its tails
+    uint64_t empty[MAX_STAGES];  // the MMAs reading the stage have completed
     uint64_t acc_full[2];
-    uint64_t acc_empty[2];
+    uint64_t acc_empty[2];       // (leader) every epilogue warp of the group has drained the buffer
     uint64_t mma_done;
     uint32_t tmem_slot;
 };
@@ -106,15 +124,16 @@ __device__ __forceinline__ uint32_t tf32_tail_bits(uint32_t u) {
 }
 
 struct TileCoord {
-    int m0, n0, p2, p3;
+    int m0, n0, p2, p3;  // m0: first row of the (CG*128-row) tile
 };
 
+template <int CG>
 __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile) {
     const int64_t per_plane = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
     const int64_t plane     = tile / per_plane;
     const int64_t r         = tile - plane * per_plane;
     TileCoord c;
-    c.m0 = static_cast<int>(r / p.n_tiles) * BM;
+    c.m0 = static_cast<int>(r / p.n_tiles) * Geo<CG>::TILE_M;
     c.n0 = static_cast<int>(r % p.n_tiles) * BN;
     c.p2 = static_cast<int>(plane % p.planes2);
     c.p3 = static_cast<int>(plane / p.planes2);
@@ -133,11 +152,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
 }
 
 // Tail of one 16-byte chunk of a raw tile (index i < nA: A tile, else B tile).
+template <class G>
 __device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
-    const uint4* src = i < nA ? reinterpret_cast<const uint4*>(st + OFF_A_RAW) + i
-                              : reinterpret_cast<const uint4*>(st + OFF_B_RAW) + (i - nA);
-    uint4* dst = i < nA ? reinterpret_cast<uint4*>(st + OFF_A_TAIL) + i
-                        : reinterpret_cast<uint4*>(st + OFF_B_TAIL) + (i - nA);
+    const uint4* src = i < nA ? reinterpret_cast<const uint4*>(st + G::OFF_A_RAW) + i
+                              : reinterpret_cast<const uint4*>(st + G::OFF_B_RAW) + (i - nA);
+    uint4* dst = i < nA ? reinterpret_cast<uint4*>(st + G::OFF_A_TAIL) + i
+                        : reinterpret_cast<uint4*>(st + G::OFF_B_TAIL) + (i - nA);
     uint4 v = *src;
     v.x = tf32_tail_bits(v.x);
     v.y = tf32_tail_bits(v.y);
@@ -145,6 +165,9 @@ __device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
     v.w = tf32_tail_bits(v.w);
     *dst = v;
 }
+
+// A-tile offsets (the same in both geometries), used by the fused decode.
+constexpr int OFF_A_RAW = 0, OFF_A_TAIL = BM * BK * 4;
 
 // decode_quad_words with the fp16 fields converted by the hardware (cvt.f32.f16): the same value
 // for every finite scale and minimum, in one instruction instead of the portable bit decode.
@@ -234,26 +257,35 @@ __device__ __forceinline__ void store_quad_head_tail(uint8_t* st, int off, const
 }
 
 // QTYPE = 0: A is an F32 view loaded by TMA. QTYPE = ggml Q-type: A is decoded from packed blocks by
-// the split warpgroup (QTRANS = 0: A = W, K-major; QTRANS = 1: A = transpose(W), MN-major).
-template <int QTYPE, int QTRANS>
+// the split warps (QTRANS = 0: A = W, K-major; QTRANS = 1: A = transpose(W), MN-major).
+// CG = 1: one CTA per tile. CG = 2: a cluster of two CTAs per tile (tcgen05 cta_group::2); CTA rank
+// r of the pair owns rows m0 + 128 r of D and B rows n0 + 128 r of the tile. Each CTA's TMA lands on
+// its own `full` barrier; its split warps then arrive on the leader's `split` barrier, the leader's
+// single thread issues the pair's MMAs and commits them to both CTAs' `empty` / `acc_full`
+// barriers, and both CTAs' epilogue warps arrive on the leader's `acc_empty`.
+template <int QTYPE, int QTRANS, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmD, const __grid_constant__ TcParams p) {
+    using G = Geo<CG>;
+    constexpr bool PAIR = CG == 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + EPI_OFF + EPI_BUFS * EPI_BUF_BYTES);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + G::EPI_OFF + EPI_BUFS * EPI_BUF_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 = leader
+    const int64_t tile0 = blockIdx.x / CG, tile_step = gridDim.x / CG;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < G::STAGES; ++s) {
             mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->split[s], SPLIT_WARPS);
+            mbar_init(&bars->split[s], SPLIT_WARPS * CG);
             mbar_init(&bars->empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&bars->acc_full[a], 1);
-            mbar_init(&bars->acc_empty[a], 4);
+            mbar_init(&bars->acc_empty[a], EPI_WARPS * CG);
         }
         mbar_init(&bars->mma_done, 1);
         fence_barrier_init();
@@ -262,11 +294,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (p.tma_store) prefetch_tmap(&tmD);
     }
     if (warp == 1) {
-        tmem_alloc(&bars->tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc<CG>(&bars->tmem_slot, TMEM_COLS);
+        tmem_relinquish<CG>();
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = bars->tmem_slot;
     const uint32_t smem_base = smem_u32(smem);
@@ -276,39 +309,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-                const TileCoord tc = tile_coord(p, tile);
+            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step) {
+                const TileCoord tc = tile_coord<CG>(p, tile);
+                const int am0 = tc.m0 + BM * static_cast<int>(rank);              // this CTA's A rows
+                const int bn0 = tc.n0 + G::BN_CTA * static_cast<int>(rank);       // this CTA's B rows
                 int r = 0, kb = 0;  // source-plane round and k-block of the virtual k-block vkb
                 for (int vkb = 0; vkb < p.kv_blocks; ++vkb, ++it) {
                     const int sp2 = tc.p2 + p.planes2 * (r % p.red2), sp3 = tc.p3 + p.planes3 * (r / p.red2);
                     const int a2 = sp2 % p.a_ne2, a3 = sp3 % p.a_ne3;
                     const int b2 = sp2 % p.b_ne2, b3 = sp3 % p.b_ne3;
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1u;
-                    if (!mbar_wait(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
-                    const uint32_t st = smem_base + s * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&bars->full[s], QTYPE == 0 ? RAW_TX_BYTES : B_BYTES);
+                    const int s = it % G::STAGES;
+                    const uint32_t ph = (it / G::STAGES) & 1u;
+                    if (!mbar_wait_scoped<PAIR>(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
+                    const uint32_t st = smem_base + s * G::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&bars->full[s], QTYPE == 0 ? G::RAW_TX_BYTES : G::B_BYTES);
                     const int k0 = kb * BK;
                     if constexpr (QTYPE == 0) {
                         if (!p.a_mn) {
-                            tma_load_4d(st + OFF_A_RAW, &tmA, &bars->full[s], k0, tc.m0, a2, a3);
+                            tma_load_4d(st + G::OFF_A_RAW, &tmA, &bars->full[s], k0, am0, a2, a3);
                         } else if (p.a_tma5) {
-                            tma_load_5d(st + OFF_A_RAW, &tmA, &bars->full[s], 0, k0, tc.m0 / 32, a2, a3);
+                            tma_load_5d(st + G::OFF_A_RAW, &tmA, &bars->full[s], 0, k0, am0 / 32, a2, a3);
                         } else {
 #pragma unroll
                             for (int c = 0; c < BM / 32; ++c)
-                                tma_load_4d(st + OFF_A_RAW + c * 2048, &tmA, &bars->full[s], tc.m0 + 32 * c, k0, a2,
+                                tma_load_4d(st + G::OFF_A_RAW + c * 2048, &tmA, &bars->full[s], am0 + 32 * c, k0, a2,
                                             a3);
                         }
                     }
                     if (!p.b_mn) {
-                        tma_load_4d(st + OFF_B_RAW, &tmB, &bars->full[s], k0, tc.n0, b2, b3);
+                        tma_load_4d(st + G::OFF_B_RAW, &tmB, &bars->full[s], k0, bn0, b2, b3);
                     } else if (p.b_tma5) {
-                        tma_load_5d(st + OFF_B_RAW, &tmB, &bars->full[s], 0, k0, tc.n0 / 32, b2, b3);
+                        tma_load_5d(st + G::OFF_B_RAW, &tmB, &bars->full[s], 0, k0, bn0 / 32, b2, b3);
                     } else {
 #pragma unroll
-                        for (int c = 0; c < BN / 32; ++c)
-                            tma_load_4d(st + OFF_B_RAW + c * 2048, &tmB, &bars->full[s], tc.n0 + 32 * c, k0, b2, b3);
+                        for (int c = 0; c < G::BN_CTA / 32; ++c)
+                            tma_load_4d(st + G::OFF_B_RAW + c * 2048, &tmB, &bars->full[s], bn0 + 32 * c, k0, b2, b3);
                     }
                     if (++kb == p.k_blocks) {
                         kb = 0;
@@ -318,22 +353,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             // Drain: the last load issued into each stage must have landed before the CTA exits.
             const uint32_t n_issued = it;
-            for (uint32_t q = (n_issued > STAGES ? n_issued - STAGES : 0); q < n_issued; ++q)
-                mbar_wait_drain(&bars->full[q % STAGES], (q / STAGES) & 1u);
+            for (uint32_t q = (n_issued > G::STAGES ? n_issued - G::STAGES : 0); q < n_issued; ++q)
+                mbar_wait_drain(&bars->full[q % G::STAGES], (q / G::STAGES) & 1u);
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------------- UMMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = make_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
+        // ---------------------------------------------------------------- UMMA issuer (leader only)
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = make_idesc_tf32(G::TILE_M, BN, p.a_mn, p.b_mn);
             // uses0/uses1: chunks committed so far into TMEM buffer 0/1 (scalars, kept in registers)
             uint32_t it = 0, tcount = 0, uses0 = 0, uses1 = 0;
             bool ok = true;
-            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step, ++tcount) {
                 const int tb = tcount & 1;  // this tile's running-total buffer; chunks >= 1 use tb ^ 1
                 for (int kb0 = 0; kb0 < p.kv_blocks && ok; kb0 += CHUNK_KB) {
                     const int b = kb0 == 0 ? tb : tb ^ 1;
                     const uint32_t ub = b ? uses1 : uses0;
-                    if (!mbar_wait(&bars->acc_empty[b], (ub & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
+                    if (!mbar_wait_scoped<PAIR>(&bars->acc_empty[b], (ub & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
                         ok = false;
                         break;
                     }
@@ -341,41 +376,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t d_tmem = tmem_base + b * BN;
                     const int kb1 = min(p.kv_blocks, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
-                        const int s = it % STAGES;
-                        if (!mbar_wait(&bars->split[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
+                        const int s = it % G::STAGES;
+                        if (!mbar_wait_scoped<PAIR>(&bars->split[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t st = smem_base + s * STAGE_BYTES;
+                        const uint32_t st = smem_base + s * G::STAGE_BYTES;
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
-                            const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + OFF_A_RAW, kk) : desc_kmajor(st + OFF_A_RAW, kk);
-                            const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + OFF_A_TAIL, kk) : desc_kmajor(st + OFF_A_TAIL, kk);
-                            const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + OFF_B_RAW, kk) : desc_kmajor(st + OFF_B_RAW, kk);
-                            const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + OFF_B_TAIL, kk) : desc_kmajor(st + OFF_B_TAIL, kk);
-                            umma_tf32(d_tmem, a_tail, b_raw, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-                            umma_tf32(d_tmem, a_raw, b_tail, idesc, 1u);
-                            umma_tf32(d_tmem, a_raw, b_raw, idesc, 1u);
+                            const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + G::OFF_A_RAW, kk) : desc_kmajor(st + G::OFF_A_RAW, kk);
+                            const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + G::OFF_A_TAIL, kk) : desc_kmajor(st + G::OFF_A_TAIL, kk);
+                            const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + G::OFF_B_RAW, kk) : desc_kmajor(st + G::OFF_B_RAW, kk);
+                            const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + G::OFF_B_TAIL, kk) : desc_kmajor(st + G::OFF_B_TAIL, kk);
+                            umma_tf32<CG>(d_tmem, a_tail, b_raw, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            umma_tf32<CG>(d_tmem, a_raw, b_tail, idesc, 1u);
+                            umma_tf32<CG>(d_tmem, a_raw, b_raw, idesc, 1u);
                         }
-                        umma_commit(&bars->empty[s]);  // frees the stage once these MMAs have read it
+                        // frees the stage (in both CTAs) once these MMAs have read it
+                        if constexpr (PAIR) {
+                            umma_commit_pair_both(&bars->empty[s], 0x3);
+                        } else {
+                            umma_commit(&bars->empty[s]);
+                        }
                     }
                     if (!ok) break;
-                    umma_commit(&bars->acc_full[b]);  // this chunk is complete in TMEM buffer b
+                    // this chunk is complete in TMEM buffer b
+                    if constexpr (PAIR) {
+                        umma_commit_pair_both(&bars->acc_full[b], 0x3);
+                    } else {
+                        umma_commit(&bars->acc_full[b]);
+                    }
                     if (b) ++uses1; else ++uses0;
                 }
             }
             // All MMAs of this thread must be complete before TMEM is released.
-            umma_commit(&bars->mma_done);
+            if constexpr (PAIR) umma_commit_pair_local(&bars->mma_done);
+            else umma_commit(&bars->mma_done);
             mbar_wait_drain(&bars->mma_done, 0);
         }
     } else if (warp < EPI_WARP0) {
-        // ---------------------------------------------------------------- split warpgroup
+        // ---------------------------------------------------------------- split warps
         const int t = threadIdx.x - SPLIT_WARP0 * 32;
-        constexpr int nA = A_BYTES / 16, nAll = (A_BYTES + B_BYTES) / 16;
+        constexpr int nA = G::A_BYTES / 16, nAll = (G::A_BYTES + G::B_BYTES) / 16;
+        // the leader's split barrier of stage s, as this CTA addresses it
+        auto arrive_split = [&](int s) {
+            if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(&bars->split[s], 0));
+            else mbar_arrive(&bars->split[s]);
+        };
         if constexpr (QTYPE != 0) {
-            // Fused kernel: the six warps decode the stage's A quads (up to 3 per thread) from the
-            // packed blocks into head + tail tiles, then split the TMA-loaded B tile. The packed
+            // Fused kernel: the split warps decode the stage's A quads (up to 2 per thread) from
+            // the packed blocks into head + tail tiles, then split the TMA-loaded B tile. The packed
             // words of the next stage are loaded before the current stage is decoded, so their L2
             // latency overlaps the decode and the waits.
             constexpr int NT = SPLIT_WARPS * 32;
@@ -383,13 +434,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int qoff[QPT];
 #pragma unroll
             for (int i = 0; i < QPT; ++i) qoff[i] = (t + NT * i) < A_QUADS ? quad_offset<QTRANS>(t + NT * i) : 0;
-            int64_t tile = blockIdx.x;
+            int64_t tile = tile0;
             int kb = 0;
+            const int row_off = BM * static_cast<int>(rank);
             const uint8_t* base[QPT];  // this tile's packed-row pointers
 #pragma unroll
             for (int i = 0; i < QPT; ++i)
                 base[i] = (tile < p.total_tiles && t + NT * i < A_QUADS)
-                              ? quad_tile_base<QTYPE, QTRANS>(p, tile_coord(p, tile).m0, t + NT * i) : nullptr;
+                              ? quad_tile_base<QTYPE, QTRANS>(p, tile_coord<CG>(p, tile).m0 + row_off, t + NT * i)
+                              : nullptr;
             QuadWords cur[QPT];
             const uint8_t* cblk[QPT];
             int cj0[QPT];
@@ -404,8 +457,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 int nkb = kb + 1;
                 if (nkb == p.k_blocks) {
                     nkb = 0;
-                    ntile += gridDim.x;
-                    const int nm0 = ntile < p.total_tiles ? tile_coord(p, ntile).m0 : 0;
+                    ntile += tile_step;
+                    const int nm0 = ntile < p.total_tiles ? tile_coord<CG>(p, ntile).m0 + row_off : 0;
 #pragma unroll
                     for (int i = 0; i < QPT; ++i)
                         base[i] = (ntile < p.total_tiles && t + NT * i < A_QUADS)
@@ -419,9 +472,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     nblk[i] = quad_block<QTYPE, QTRANS>(p, base[i], nkb * BK, t + NT * i, nj0[i]);
                     if (nblk[i] != nullptr) load_quad_words<QTYPE>(nblk[i], nj0[i], nxt[i]);
                 }
-                const int s = it % STAGES;
-                uint8_t* st = smem + s * STAGE_BYTES;
-                if (it >= STAGES && !mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) break;
+                const int s = it % G::STAGES;
+                uint8_t* st = smem + s * G::STAGE_BYTES;
+                if (it >= G::STAGES &&
+                    !mbar_wait_scoped<PAIR>(&bars->empty[s], ((it / G::STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY))
+                    break;
 #pragma unroll
                 for (int i = 0; i < QPT; ++i) {
                     if (t + NT * i >= A_QUADS) continue;
@@ -429,11 +484,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (cblk[i] != nullptr) decode_quad_words_cvt<QTYPE>(cur[i], cj0[i], w);
                     store_quad_head_tail(st, qoff[i], w);
                 }
-                if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
-                for (int i = nA + t; i < nAll; i += NT) split_one(st, i, nA);
+                if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
+                for (int i = nA + t; i < nAll; i += NT) split_one<G>(st, i, nA);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->split[s]);
+                if (lane == 0) arrive_split(s);
 #pragma unroll
                 for (int i = 0; i < QPT; ++i) {
                     cur[i] = nxt[i];
@@ -446,22 +501,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         } else {
             // F32 kernel: all split warps split the A and B tiles.
-            const int i_begin = t;
-            const int i_step  = SPLIT_WARPS * 32;
+            const int i_step = SPLIT_WARPS * 32;
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step) {
                 for (int kb = 0; kb < p.kv_blocks; ++kb, ++it) {
-                    const int s = it % STAGES;
-                    if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
+                    const int s = it % G::STAGES;
+                    if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
                         ok = false;
                         break;
                     }
-                    uint8_t* st = smem + s * STAGE_BYTES;
-                    for (int i = i_begin; i < nAll; i += i_step) split_one(st, i, nA);
+                    uint8_t* st = smem + s * G::STAGE_BYTES;
+                    for (int i = t; i < nAll; i += i_step) split_one<G>(st, i, nA);
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->split[s]);
+                    if (lane == 0) arrive_split(s);
                 }
             }
         }
@@ -469,35 +523,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- epilogue
         // Per tile: chunk 0 lands in buffer tb (the running total T), every further chunk in tb^1 (X)
         // and is added into T with round-to-nearest fp32 adds; the final sum goes to global memory.
+        // Two teams of four warps split the 256 columns, so a chunk's promotion (which the MMA
+        // issuer waits for before it reuses X) takes half as long.
         const int q = warp & 3;  // TMEM lane quarter this warp may access (warp id mod 4)
+        const int team = (warp - EPI_WARP0) >> 2;
         const int row = q * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
         uint32_t tcount = 0, uses_t = 0, uses_x = 0;  // chunks consumed from this tile's T / X buffer roles
         uint32_t uses0 = 0, uses1 = 0;                // ... per physical buffer (scalars, in registers)
-        uint32_t gcount = 0;                          // column groups staged for TMA stores so far
-        const bool epi_leader = (threadIdx.x == EPI_WARP0 * 32);
+        uint32_t gcount = 0;                          // column groups this team staged for TMA stores
+        const bool team_leader = (threadIdx.x == (EPI_WARP0 + 4 * team) * 32);
+        const int team_bar = EPI_BAR_TEAM0 + team;
+        uint8_t* stage_buf = smem + G::EPI_OFF + team * EPI_BUF_BYTES;
+        // the leader's acc_empty barrier of buffer b, as this CTA addresses it
+        auto release_acc = [&](int b) {
+            if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[b], 0));
+            else mbar_arrive(&bars->acc_empty[b]);
+        };
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++tcount) {
+        for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step, ++tcount) {
             const int tb = tcount & 1, xb = tb ^ 1;
-            const TileCoord tc = tile_coord(p, tile);
-            const int m = tc.m0 + row;
+            const TileCoord tc = tile_coord<CG>(p, tile);
+            const int dm0 = tc.m0 + BM * static_cast<int>(rank);  // this CTA's rows of D
+            const int m = dm0 + row;
             char* drow = p.d + static_cast<int64_t>(tc.p2) * p.d_s2 + static_cast<int64_t>(tc.p3) * p.d_s3 +
                          static_cast<int64_t>(m) * p.d_sm;
             const int n_valid = min(BN, p.N - tc.n0);
-            const int n_groups = (n_valid + 31) / 32;  // uniform across the warp
+            // uniform across a team; none when this CTA's rows all lie past M (the second CTA of a
+            // pair on the last row tile): nothing to add or store, and no store box starts outside D
+            const int n_groups = dm0 < p.M ? (n_valid + 31) / 32 : 0;
+            const int c_begin = 4 * team, c_end = min(n_groups, 4 * team + 4);
             const uint32_t t_addr = tmem_base + lane_off + tb * BN;
             const uint32_t x_addr = tmem_base + lane_off + xb * BN;
             uses_t = tb ? uses1 : uses0;
-            if (!mbar_wait(&bars->acc_full[tb], uses_t & 1u, TRC_DEVERR_WAIT_ACCUM)) break;
+            // every wait is followed by a vote of all epilogue warps, so that they all leave or all
+            // stay (a team meets again at its named barrier of the TMA-store staging)
+            if (!named_barrier_and(EPI_BAR_ALL, EPI_WARPS * 32,
+                                   mbar_wait_scoped<PAIR>(&bars->acc_full[tb], uses_t & 1u, TRC_DEVERR_WAIT_ACCUM)))
+                break;
             if (tb) ++uses1; else ++uses0;
             tc_fence_after();
             for (int kb0 = CHUNK_KB; kb0 < p.kv_blocks; kb0 += CHUNK_KB) {
                 uses_x = xb ? uses1 : uses0;
-                if (!mbar_wait(&bars->acc_full[xb], uses_x & 1u, TRC_DEVERR_WAIT_ACCUM)) { ok = false; break; }
+                if (!named_barrier_and(EPI_BAR_ALL, EPI_WARPS * 32,
+                                       mbar_wait_scoped<PAIR>(&bars->acc_full[xb], uses_x & 1u, TRC_DEVERR_WAIT_ACCUM))) {
+                    ok = false;
+                    break;
+                }
                 if (xb) ++uses1; else ++uses0;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < n_groups; ++c) {
+                for (int c = c_begin; c < c_end; ++c) {
                     uint32_t x[32], t[32];
                     tmem_ld_32x32b_x32(x_addr + c * 32, x);
                     tmem_ld_32x32b_x32(t_addr + c * 32, t);
@@ -509,31 +585,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->acc_empty[xb]);  // chunk buffer free for the next chunk
+                if (lane == 0) release_acc(xb);  // chunk buffer free for the next chunk
             }
             if (!ok) break;
 #pragma unroll 1
-            for (int c = 0; c < n_groups; ++c) {
+            for (int c = c_begin; c < c_end; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_addr + c * 32, r);
                 tmem_ld_wait();
                 if (p.tma_store) {
                     // Stage the 128 x 32 group column-major (each column's 128 rows contiguous, the
-                    // layout of the TMA box) and let one thread store or reduce-add it.
-                    const int buf = gcount & 1;
-                    if (gcount >= EPI_BUFS) {
-                        if (epi_leader) bulk_wait_group_read<EPI_BUFS - 1>();  // this buffer's last store has read it
-                        named_barrier_sync(1, 128);
+                    // layout of the TMA box) and let the team leader store or reduce-add it.
+                    if (gcount > 0) {
+                        if (team_leader) bulk_wait_group_read<0>();  // the previous store has read the buffer
+                        named_barrier_sync(team_bar, 128);
                     }
-                    float* sb = reinterpret_cast<float*>(smem + EPI_OFF + buf * EPI_BUF_BYTES);
+                    float* sb = reinterpret_cast<float*>(stage_buf);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) sb[e * BM + row] = __uint_as_float(r[e]);
                     fence_proxy_async_smem();
-                    named_barrier_sync(1, 128);
-                    if (epi_leader) {
-                        const uint32_t src = smem_base + EPI_OFF + buf * EPI_BUF_BYTES;
-                        if (p.accumulate) tma_reduce_add_4d(&tmD, src, tc.m0, tc.n0 + c * 32, tc.p2, tc.p3);
-                        else tma_store_4d(&tmD, src, tc.m0, tc.n0 + c * 32, tc.p2, tc.p3);
+                    named_barrier_sync(team_bar, 128);
+                    if (team_leader) {
+                        const uint32_t src = smem_u32(stage_buf);
+                        if (p.accumulate) tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        else tma_store_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
                         bulk_commit_group();
                     }
                     ++gcount;
@@ -551,15 +626,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty[tb]);
+            if (lane == 0) release_acc(tb);
         }
-        if (epi_leader) bulk_wait_group_all();  // every TMA store has completed before the CTA exits
+        if (team_leader) bulk_wait_group_all();  // every TMA store has completed before the CTA exits
     }
 
     tc_fence_before();
     __syncthreads();
+    // CG = 2: the leader's MMAs (which write both CTAs' TMEM and read both CTAs' shared memory) and
+    // every remote arrival are complete before either CTA frees TMEM or exits.
+    if constexpr (PAIR) cluster_sync();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+    if (warp == 1) tmem_dealloc<CG>(tmem_base, TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ host side
@@ -685,31 +763,78 @@ bool encode_output(void* data, int64_t M, int64_t N, int64_t P2, int64_t P3, int
 }
 
 // Launches one instantiation; the >48 KiB dynamic shared memory opt-in is set once per device.
-template <int QTYPE, int QTRANS>
+// Persistent launch: one CTA per SM (CG = 1) or one CTA pair per two SMs (CG = 2, a cluster of 2).
+template <int QTYPE, int QTRANS, int CG>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmD, const TcParams& p,
               cudaStream_t stream) {
+    using G = Geo<CG>;
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
+    static int        max_pairs[64] = {};
+    auto kernel = tf32x3_gemm_kernel<QTYPE, QTRANS, CG>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e);
+    const int sms = sm_count_current();
+    if (sms <= 0) return TRC_CUDA_ECUDA;
+    int pairs = sms / 2;
     {
         std::lock_guard<std::mutex> lock(mu);
         const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
         if (bit == 0 || (configured & bit) == 0) {
-            e = cudaFuncSetAttribute(tf32x3_gemm_kernel<QTYPE, QTRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SMEM_BYTES);
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
             if (e != cudaSuccess) return cuda_fail(e);
+            if constexpr (CG == 2) {
+                // how many CTA pairs of this size fit on the device at once (a persistent grid larger
+                // than that would only queue)
+                cudaLaunchConfig_t cfg = {};
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 2;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.gridDim = dim3(2 * static_cast<unsigned>(sms / 2));
+                cfg.blockDim = dim3(NUM_THREADS);
+                cfg.dynamicSmemBytes = G::SMEM_BYTES;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                int n = 0;
+                e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+                if (e != cudaSuccess) return cuda_fail(e);
+                if (n <= 0) return TRC_CUDA_EUNSUPPORTED;
+                if (dev < 64) max_pairs[dev] = n;
+            }
             configured |= bit;
         }
+        if (CG == 2 && dev < 64 && max_pairs[dev] > 0) pairs = std::min(pairs, max_pairs[dev]);
     }
-    const int sms = sm_count_current();
-    if (sms <= 0) return TRC_CUDA_ECUDA;
-    const int64_t grid = std::min<int64_t>(p.total_tiles, sms);
-    tf32x3_gemm_kernel<QTYPE, QTRANS><<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tmD, p);
+    if constexpr (CG == 1) {
+        const int64_t grid = std::min<int64_t>(p.total_tiles, sms);
+        kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmD, p);
+    } else {
+        const int64_t clusters = std::min<int64_t>(p.total_tiles, std::max(1, pairs));
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+        cfg.blockDim = dim3(NUM_THREADS);
+        cfg.dynamicSmemBytes = G::SMEM_BYTES;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmD, p);
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
     note_launch();
     return check_launch();
 }
+
+// CTA pairs when the tile grid has more than one 128-row tile (a single row tile would leave the
+// second CTA of every pair without rows).
+bool use_pair(int64_t M, bool allow_pair) { return allow_pair && M > BM; }
 
 }  // namespace
 
@@ -726,8 +851,12 @@ bool mul_mat_tc_eligible(const trc_cuda_view& a_in, const trc_cuda_view& b_in, c
     return encode_operand(A, BM, mn, tm) && encode_operand(B, BN, mn, tm);
 }
 
-int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
-               cudaStream_t stream) {
+namespace {
+
+template <int CG>
+int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
+                    cudaStream_t stream) {
+    using G = Geo<CG>;
     // Put D's unit-stride dimension on the TMEM lanes so that epilogue stores coalesce: if D is
     // contiguous along ggml's j (ne1) rather than i (ne0), compute D^T = b^T a with roles swapped.
     const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
@@ -737,23 +866,19 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     // Output planes; when d has fewer planes than b, the source planes p with p % d.ne == q are
     // summed into output plane q (repeat_back fused into the K loop).
     const int64_t planes2 = d.ne[2], planes3 = d.ne[3];
-    if (planes2 <= 0 || planes3 <= 0 || b_in.ne[2] % planes2 != 0 || b_in.ne[3] % planes3 != 0) return TRC_CUDA_EINVAL;
     const int64_t red2 = b_in.ne[2] / planes2, red3 = b_in.ne[3] / planes3;
-    if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
-    if (planes2 >= (1 << 30) || planes3 >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
-    if ((K + BK - 1) / BK * red2 * red3 >= (int64_t(1) << 30)) return TRC_CUDA_EUNSUPPORTED;
 
     CUtensorMap tmA, tmB;
     bool a_mn = false, b_mn = false, a5 = false, b5 = false;
     if (!encode_operand(A, BM, a_mn, tmA, &a5)) return TRC_CUDA_EUNSUPPORTED;
-    if (!encode_operand(B, BN, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
+    if (!encode_operand(B, G::BN_CTA, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
 
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
-    p.m_tiles  = static_cast<int>((M + BM - 1) / BM);
+    p.m_tiles  = static_cast<int>((M + G::TILE_M - 1) / G::TILE_M);
     p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
     p.planes2 = static_cast<int>(planes2);
@@ -780,20 +905,20 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, planes2, planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
-    return launch_tc<0, 0>(tmA, tmB, tmD, p, stream);
+    return launch_tc<0, 0, CG>(tmA, tmB, tmD, p, stream);
 }
 
-int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
-                 const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, cudaStream_t stream) {
+template <int CG>
+int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                      const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, cudaStream_t stream) {
+    using G = Geo<CG>;
     const int64_t M = a_transposed ? w_ne0 : w_ne1;
     const int64_t K = a_transposed ? w_ne1 : w_ne0;
     const int64_t N = b.ne[1];
-    if (M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30) || N <= 0) return TRC_CUDA_EUNSUPPORTED;
-    if ((reinterpret_cast<uint64_t>(w_blocks) & 1u) != 0) return TRC_CUDA_EINVAL;
     CUtensorMap tmA, tmB;
     std::memset(&tmA, 0, sizeof(tmA));
     bool b_mn = false, b5 = false;
-    if (!encode_operand(b, BN, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
+    if (!encode_operand(b, G::BN_CTA, b_mn, tmB, &b5)) return TRC_CUDA_EUNSUPPORTED;
     const size_t bb = trc_cuda_block_bytes(type);
 
     TcParams p;
@@ -801,7 +926,7 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
-    p.m_tiles  = static_cast<int>((M + BM - 1) / BM);
+    p.m_tiles  = static_cast<int>((M + G::TILE_M - 1) / G::TILE_M);
     p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
     p.planes2 = static_cast<int>(b.ne[2]);
@@ -831,9 +956,10 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
 
-#define TRC_Q_CASE(T)                                                                   \
-    case T:                                                                             \
-        return a_transposed ? launch_tc<T, 1>(tmA, tmB, tmD, p, stream) : launch_tc<T, 0>(tmA, tmB, tmD, p, stream);
+#define TRC_Q_CASE(T)                                                                                 \
+    case T:                                                                                           \
+        return a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmD, p, stream)                           \
+                            : launch_tc<T, 0, CG>(tmA, tmB, tmD, p, stream);
     switch (type) {
         TRC_Q_CASE(2)
         TRC_Q_CASE(3)
@@ -843,6 +969,37 @@ int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, i
         default: return TRC_CUDA_EUNSUPPORTED;
     }
 #undef TRC_Q_CASE
+}
+
+}  // namespace
+
+int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
+               bool allow_pair, cudaStream_t stream) {
+    const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
+    const trc_cuda_view& A = swap ? b_in : a_in;
+    const trc_cuda_view& B = swap ? a_in : b_in;
+    const int64_t M = A.ne[1], N = B.ne[1], K = a_in.ne[0];
+    const int64_t planes2 = d.ne[2], planes3 = d.ne[3];
+    if (planes2 <= 0 || planes3 <= 0 || b_in.ne[2] % planes2 != 0 || b_in.ne[3] % planes3 != 0) return TRC_CUDA_EINVAL;
+    const int64_t red2 = b_in.ne[2] / planes2, red3 = b_in.ne[3] / planes3;
+    if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
+    if (planes2 >= (1 << 30) || planes3 >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
+    if ((K + BK - 1) / BK * red2 * red3 >= (int64_t(1) << 30)) return TRC_CUDA_EUNSUPPORTED;
+    return use_pair(M, allow_pair) ? mul_mat_tc_impl<2>(a_in, b_in, d, accumulate, stream)
+                                   : mul_mat_tc_impl<1>(a_in, b_in, d, accumulate, stream);
+}
+
+int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                 const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, bool allow_pair,
+                 cudaStream_t stream) {
+    const int64_t M = a_transposed ? w_ne0 : w_ne1;
+    const int64_t K = a_transposed ? w_ne1 : w_ne0;
+    const int64_t N = b.ne[1];
+    if (M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30) || N <= 0) return TRC_CUDA_EUNSUPPORTED;
+    if ((reinterpret_cast<uint64_t>(w_blocks) & 1u) != 0) return TRC_CUDA_EINVAL;
+    return use_pair(M, allow_pair)
+               ? mul_mat_q_tc_impl<2>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, accumulate, stream)
+               : mul_mat_q_tc_impl<1>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, accumulate, stream);
 }
 
 }  // namespace trc

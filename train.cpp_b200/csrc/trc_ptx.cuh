@@ -90,6 +90,68 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     }
 }
 
+// Cluster-scope variants, for barriers that receive arrivals from the other CTA of a CTA pair
+// (remote mbarrier.arrive, or tcgen05.commit issued by the pair's leader).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+template <bool CLUSTER>
+__device__ __forceinline__ bool mbar_wait_scoped(uint64_t* bar, uint32_t parity, int code) {
+    if constexpr (!CLUSTER) {
+        return mbar_wait(bar, parity, code);
+    } else {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        const uint64_t t0 = globaltimer();
+        for (uint32_t spin = 1;; ++spin) {
+            if (mbar_try_wait_cluster(bar, parity)) return true;
+            if ((spin & 255u) == 0) {
+                if (device_error_set()) return false;
+                if (globaltimer() - t0 > TRC_WAIT_LIMIT_NS) {
+                    set_device_error(code);
+                    return false;
+                }
+            }
+        }
+    }
+}
+
+// Rank of this CTA in its cluster, and the shared::cluster address of a variable of this CTA's
+// shared memory as it lies in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+    return out;
+}
+
+// Arrive on an mbarrier of any CTA of the cluster. The default (release, CTA-scope) form: the
+// data the arrival publishes was made visible to the async proxy by fence.proxy.async (split
+// tiles) or tcgen05.wait + fence (drained TMEM) before it, and the consumer is the pair's tensor
+// core. A cluster-scope release fence here stalled every split warp at every stage (measured:
+// 127 -> 224 TFLOP/s for the CTA-pair GEMM at 4096^3).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Cluster-wide barrier of all threads of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Wait that ignores errors raised elsewhere (used to drain in-flight copies before exit).
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
     const uint64_t t0 = globaltimer();
@@ -164,6 +226,21 @@ __device__ __forceinline__ void named_barrier_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// AND of `ok` over the `count` threads of named barrier `id` (every one of them must call it):
+// lets a group of warps that each did a bounded wait take the same branch afterwards.
+__device__ __forceinline__ bool named_barrier_and(int id, int count, bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(ok)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
@@ -174,18 +251,34 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ------------------------------------------------------------------ tcgen05 (TMEM + UMMA)
+// TMEM allocation. CG = 2: the warp with the same warp index in both CTAs of a pair executes it,
+// with the same shared-memory slot, and each CTA receives its own TMEM address in the slot.
+template <int CG = 1>
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
-                 "r"(ncols)
-                 : "memory");
+    if constexpr (CG == 1)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+                     "r"(ncols)
+                     : "memory");
+    else
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+                     "r"(ncols)
+                     : "memory");
 }
 
+template <int CG = 1>
 __device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CG == 1)
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    else
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 
+template <int CG = 1>
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    if constexpr (CG == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    else
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -196,21 +289,48 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, issued by one thread.
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, issued by one thread. CG = 2: issued by the
+// leader CTA of a pair; each CTA supplies its half of A (M/2 rows) and of B (N/2 rows) at the
+// same shared-memory offsets, and each CTA's TMEM receives its M/2 rows of D.
+template <int CG = 1>
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if constexpr (CG == 1)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
 }
 
 // Arrive on an mbarrier once every previously issued tcgen05.mma of this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
+                 : "memory");
+}
+
+// The same for cta_group::2 MMAs, arriving on this CTA's barrier only.
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// cta_group::2 MMAs, arriving on the barrier at the same shared-memory offset in every CTA of
+// `cta_mask` (bit r = cluster rank r): how the leader of a CTA pair signals both CTAs. This is an
+// MMA-completion signal, not a copy: no data moves.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"(cta_mask)
                  : "memory");
 }
 
