@@ -21,17 +21,22 @@
 // double buffering survives: tile i keeps its total in buffer i%2 and its chunks in buffer
 // (i+1)%2, and tile i+1's first chunk can start while tile i's total is being stored.
 //
-// Structure (one persistent CTA per SM, 14 warps):
-//   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (4-stage ring, 64-byte swizzle)
-//   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
+// Structure (persistent, 18 warps per CTA):
+//   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (a ring of 4-6 stages)
+//   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.kind::tf32)
 //   warps 2-9   split warps: write the tails tA, tB of each stage next to the raw tiles (fused
 //               variant: also decode the packed weight tile into head + tail)
-//   warps 10-13 epilogue: TMEM -> registers (tcgen05.ld) -> shared memory -> TMA store (or strided
-//               stores when TMA cannot address D)
-// Tile 128 (M, TMEM lanes) x 256 (N) x 16 (K) per stage; two 256-column fp32 TMEM buffers (all 512
-// columns). Shared-memory operand layouts: K-major tiles use the 64-byte swizzle (64 B rows);
-// MN-major tiles use the 128-byte swizzle with 32-byte atoms, the one layout tcgen05 accepts for
-// MN-major TF32 operands (32-element MN chunks of 16 K-rows x 128 B).
+//   warps 10-17 epilogue, two teams of four (one per column half): TMEM -> registers (tcgen05.ld)
+//               -> shared memory -> TMA store (or strided stores when TMA cannot address D)
+// CTA pairs (default when M spans more than 128 rows): a cluster of two CTAs computes a 256 x 256
+// tile with tcgen05 cta_group::2. Each CTA stages its 128 rows of A and 128 of the 256 rows of B;
+// the leader's single thread issues the MMAs for both SMs, so each SM stages, splits and feeds the
+// tensor core half the B bytes of a one-CTA 128 x 256 tile. One CTA per 128 x 256 tile
+// (cta_group::1) is kept for M <= 128 and on request (TRC_CUDA_MM_ONE_CTA).
+// Two 256-column fp32 TMEM buffers (all 512 columns). Shared-memory operand layouts: K-major tiles
+// use the 64-byte swizzle (64 B rows); MN-major tiles use the 128-byte swizzle with 32-byte atoms,
+// the one layout tcgen05 accepts for MN-major TF32 operands (32-element MN chunks of 16 K-rows x
+// 128 B).
 // Every mbarrier wait is bounded (trc_ptx.cuh); a timeout sets the device error word and the kernel
 // drains its in-flight copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -127,14 +132,23 @@ struct TileCoord {
     int m0, n0, p2, p3;  // m0: first row of the (CG*128-row) tile
 };
 
+// Tiles of a plane are visited in bands of GROUP_M row tiles, column by column inside a band, so
+// the tiles in flight at once (one per SM or SM pair) share a few row and column panels of A and
+// B, and those panels stay in L2 (a plain row-major order streams all of B once per row tile).
+constexpr int GROUP_M = 8;
+
 template <int CG>
 __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile) {
     const int64_t per_plane = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
     const int64_t plane     = tile / per_plane;
-    const int64_t r         = tile - plane * per_plane;
+    const int     r         = static_cast<int>(tile - plane * per_plane);
+    const int     per_band  = GROUP_M * p.n_tiles;
+    const int     band      = r / per_band;
+    const int     rb        = r - band * per_band;
+    const int     band_m    = min(GROUP_M, p.m_tiles - band * GROUP_M);  // row tiles in this band
     TileCoord c;
-    c.m0 = static_cast<int>(r / p.n_tiles) * Geo<CG>::TILE_M;
-    c.n0 = static_cast<int>(r % p.n_tiles) * BN;
+    c.m0 = (band * GROUP_M + rb % band_m) * Geo<CG>::TILE_M;
+    c.n0 = (rb / band_m) * BN;
     c.p2 = static_cast<int>(plane % p.planes2);
     c.p3 = static_cast<int>(plane / p.planes2);
     return c;
@@ -238,6 +252,14 @@ __device__ __forceinline__ int quad_offset(int q) {
         const int kr = q >> 5, mq = q & 31;  // MN-major: 32-element chunk mq/8, K-row kr, 32-byte units ^ (kr & 3)
         return (mq >> 3) * 2048 + kr * 128 + ((((mq & 7) >> 1) ^ (kr & 3)) << 5) + ((mq & 1) << 4);
     }
+}
+
+// Index of the first of quad q's four weights within its block, at k-block kb (the j0 that
+// quad_block returns).
+template <int QTRANS>
+__device__ __forceinline__ int quad_j0(int kb, int q) {
+    if constexpr (QTRANS == 0) return ((kb * BK) & 16) + 4 * (q & 3);
+    else return (q & 7) * 4;
 }
 
 // Decoded weights are finite for finite scales, so the tail needs no special-value handling
@@ -427,51 +449,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if constexpr (QTYPE != 0) {
             // Fused kernel: the split warps decode the stage's A quads (up to 2 per thread) from
             // the packed blocks into head + tail tiles, then split the TMA-loaded B tile. The packed
-            // words of the next stage are loaded before the current stage is decoded, so their L2
-            // latency overlaps the decode and the waits.
+            // words are loaded two stages ahead of their decode (a stage takes about one loaded L2
+            // latency), so the loads overlap two stages of decode, split and waits.
             constexpr int NT = SPLIT_WARPS * 32;
             constexpr int QPT = (A_QUADS + NT - 1) / NT;
             int qoff[QPT];
 #pragma unroll
             for (int i = 0; i < QPT; ++i) qoff[i] = (t + NT * i) < A_QUADS ? quad_offset<QTRANS>(t + NT * i) : 0;
+            const int row_off = BM * static_cast<int>(rank);
+            // look-ahead cursor: the (tile, k-block) whose packed words are loaded next
+            int64_t ltile = tile0;
+            int lkb = 0;
+            const uint8_t* lbase[QPT];  // packed-row pointers of ltile
+            auto set_base = [&]() {
+                const int m0 = ltile < p.total_tiles ? tile_coord<CG>(p, ltile).m0 + row_off : 0;
+#pragma unroll
+                for (int i = 0; i < QPT; ++i)
+                    lbase[i] = (ltile < p.total_tiles && t + NT * i < A_QUADS)
+                                   ? quad_tile_base<QTYPE, QTRANS>(p, m0, t + NT * i) : nullptr;
+            };
+            // loads the cursor's words into w and advances the cursor; bit i of the result: quad i
+            // lies inside the matrix (else it is decoded as zeros)
+            auto load_next = [&](QuadWords (&w)[QPT]) -> uint32_t {
+                uint32_t valid = 0;
+                if (ltile < p.total_tiles) {
+#pragma unroll
+                    for (int i = 0; i < QPT; ++i) {
+                        int j0 = 0;
+                        const uint8_t* blk = quad_block<QTYPE, QTRANS>(p, lbase[i], lkb * BK, t + NT * i, j0);
+                        if (blk != nullptr) {
+                            load_quad_words<QTYPE>(blk, j0, w[i]);
+                            valid |= 1u << i;
+                        }
+                    }
+                }
+                if (++lkb == p.k_blocks) {
+                    lkb = 0;
+                    ltile += tile_step;
+                    set_base();
+                }
+                return valid;
+            };
+            set_base();
+            QuadWords w0[QPT], w1[QPT];
+            uint32_t v0 = load_next(w0);
+            uint32_t v1 = load_next(w1);
             int64_t tile = tile0;
             int kb = 0;
-            const int row_off = BM * static_cast<int>(rank);
-            const uint8_t* base[QPT];  // this tile's packed-row pointers
-#pragma unroll
-            for (int i = 0; i < QPT; ++i)
-                base[i] = (tile < p.total_tiles && t + NT * i < A_QUADS)
-                              ? quad_tile_base<QTYPE, QTRANS>(p, tile_coord<CG>(p, tile).m0 + row_off, t + NT * i)
-                              : nullptr;
-            QuadWords cur[QPT];
-            const uint8_t* cblk[QPT];
-            int cj0[QPT];
-#pragma unroll
-            for (int i = 0; i < QPT; ++i) {
-                cblk[i] = quad_block<QTYPE, QTRANS>(p, base[i], 0, t + NT * i, cj0[i]);
-                if (cblk[i] != nullptr) load_quad_words<QTYPE>(cblk[i], cj0[i], cur[i]);
-            }
             uint32_t it = 0;
             while (tile < p.total_tiles) {
-                int64_t ntile = tile;
-                int nkb = kb + 1;
-                if (nkb == p.k_blocks) {
-                    nkb = 0;
-                    ntile += tile_step;
-                    const int nm0 = ntile < p.total_tiles ? tile_coord<CG>(p, ntile).m0 + row_off : 0;
-#pragma unroll
-                    for (int i = 0; i < QPT; ++i)
-                        base[i] = (ntile < p.total_tiles && t + NT * i < A_QUADS)
-                                      ? quad_tile_base<QTYPE, QTRANS>(p, nm0, t + NT * i) : nullptr;
-                }
-                QuadWords nxt[QPT];
-                const uint8_t* nblk[QPT];
-                int nj0[QPT];
-#pragma unroll
-                for (int i = 0; i < QPT; ++i) {
-                    nblk[i] = quad_block<QTYPE, QTRANS>(p, base[i], nkb * BK, t + NT * i, nj0[i]);
-                    if (nblk[i] != nullptr) load_quad_words<QTYPE>(nblk[i], nj0[i], nxt[i]);
-                }
+                QuadWords w2[QPT];
+                const uint32_t v2 = load_next(w2);
                 const int s = it % G::STAGES;
                 uint8_t* st = smem + s * G::STAGE_BYTES;
                 if (it >= G::STAGES &&
@@ -481,7 +509,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int i = 0; i < QPT; ++i) {
                     if (t + NT * i >= A_QUADS) continue;
                     float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (cblk[i] != nullptr) decode_quad_words_cvt<QTYPE>(cur[i], cj0[i], w);
+                    if ((v0 >> i) & 1u) decode_quad_words_cvt<QTYPE>(w0[i], quad_j0<QTRANS>(kb, t + NT * i), w);
                     store_quad_head_tail(st, qoff[i], w);
                 }
                 if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
@@ -491,12 +519,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (lane == 0) arrive_split(s);
 #pragma unroll
                 for (int i = 0; i < QPT; ++i) {
-                    cur[i] = nxt[i];
-                    cblk[i] = nblk[i];
-                    cj0[i] = nj0[i];
+                    w0[i] = w1[i];
+                    w1[i] = w2[i];
                 }
-                tile = ntile;
-                kb = nkb;
+                v0 = v1;
+                v1 = v2;
+                if (++kb == p.k_blocks) {
+                    kb = 0;
+                    tile += tile_step;
+                }
                 ++it;
             }
         } else {
@@ -881,6 +912,7 @@ int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const 
     p.m_tiles  = static_cast<int>((M + G::TILE_M - 1) / G::TILE_M);
     p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+    if (static_cast<int64_t>(p.m_tiles) * p.n_tiles * GROUP_M >= (int64_t(1) << 31)) return TRC_CUDA_EUNSUPPORTED;
     p.planes2 = static_cast<int>(planes2);
     p.planes3 = static_cast<int>(planes3);
     p.red2 = static_cast<int>(red2);
@@ -929,6 +961,7 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     p.m_tiles  = static_cast<int>((M + G::TILE_M - 1) / G::TILE_M);
     p.n_tiles  = static_cast<int>((N + BN - 1) / BN);
     p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+    if (static_cast<int64_t>(p.m_tiles) * p.n_tiles * GROUP_M >= (int64_t(1) << 31)) return TRC_CUDA_EUNSUPPORTED;
     p.planes2 = static_cast<int>(b.ne[2]);
     p.planes3 = static_cast<int>(b.ne[3]);
     p.red2 = 1;
