@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstdint>
 
 #include "trc_internal.h"
@@ -100,6 +101,8 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
     }
 }
 
+// The persistent grid is sized from the occupancy the compiled kernel really has (a grid of more
+// CTAs than can be resident would run a ragged second wave).
 template <bool PEERS>
 __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DqBatch batch) {
     __shared__ __align__(128) uint8_t buf[2][kBufBytes];
@@ -192,6 +195,23 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     if constexpr (PEERS) __threadfence_system();
 }
 
+// CTAs of dequant_kernel<PEERS> resident per SM on the current device (queried once per device).
+template <bool PEERS>
+int resident_ctas() {
+    static std::mutex mu;
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, dequant_kernel<PEERS>, kThreads, 0) != cudaSuccess)
+            return 0;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
 }  // namespace
 
 int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream) {
@@ -250,7 +270,9 @@ int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void*
         }
         if (batch.n_jobs == 0) continue;
         batch.total_runs = runs;
-        const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * 8);
+        const int per_sm = n_peers > 0 ? resident_ctas<true>() : resident_ctas<false>();
+        if (per_sm <= 0) return TRC_CUDA_ECUDA;
+        const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * per_sm);
         if (n_peers > 0) dequant_kernel<true><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
         else dequant_kernel<false><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
         note_launch();
