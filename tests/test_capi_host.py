@@ -77,3 +77,36 @@ def test_ggml_view_mapping_is_reversed_torch_layout():
     assert trc_cuda.ggml_ne(t) == [7, 5, 3, 2]
     with pytest.raises(trc_cuda.TrcCudaError):
         trc_cuda.view_of(t)  # host tensors are rejected: device memory only
+
+
+def test_dequant_to_peers_argument_checks_on_host():
+    """trc_cuda_dequant_many_to_peers rejects bad peer tables before any device call."""
+    L = trc_cuda.lib()
+    job = (trc_cuda.DequantJob * 1)()
+    job[0].blocks = 0x10000
+    job[0].out = 0x20000
+    job[0].n_blocks = 4
+    job[0].type = 2
+    base = ctypes.c_void_p(0x20000)
+    peers = (ctypes.c_void_p * 9)(*([0x40000] * 9))
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, base, peers, 9, None) == -1     # more than 8 peers
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, base, peers, -1, None) == -1    # negative count
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, None, peers, 1, None) == -1     # no local base
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, base, None, 1, None) == -1      # no peer table
+    odd = (ctypes.c_void_p * 1)(0x40008)                                             # 8 bytes off the 16-byte grid
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, base, odd, 1, None) == -1
+    null_peer = (ctypes.c_void_p * 1)(None)
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, base, null_peer, 1, None) == -1
+    above = ctypes.c_void_p(0x20010)                                                 # output below the local base
+    assert L.trc_cuda_dequant_many_to_peers(job, 1, above, peers, 1, None) == -1
+
+
+def test_mul_mat_flag_values_match_header():
+    import re
+    from pathlib import Path
+
+    hdr = (Path(__file__).resolve().parents[1] / "include" / "trc_cuda.h").read_text()
+    flags = dict(re.findall(r"(TRC_CUDA_MM_\w+)\s*=\s*(\d+)u", hdr))
+    assert int(flags["TRC_CUDA_MM_ACCUMULATE"]) == trc_cuda.MM_ACCUMULATE
+    assert int(flags["TRC_CUDA_MM_SIMT"]) == trc_cuda.MM_SIMT
+    assert int(flags["TRC_CUDA_MM_ONE_CTA"]) == trc_cuda.MM_ONE_CTA
