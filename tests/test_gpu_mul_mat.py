@@ -231,3 +231,35 @@ def test_cta_pair_transposed_output_accumulate_and_plane_reduction(tc, accumulat
         assert normwise(got, want) <= TOL, normwise(got, want)
     assert normwise(outs[0], outs[1]) <= 1e-6
     assert tc.device_error() == 0
+
+
+# ---- split-K (few tiles, long reductions): two CTAs per tile reduce-add into a zeroed D
+
+@pytest.mark.parametrize("k,m,n,one", [(8192, 128, 512, False), (4096, 256, 256, False), (4096, 256, 256, True)])
+def test_split_k_few_tiles(tc, k, m, n, one):
+    rng = np.random.default_rng(k + m + n)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    want = oracle.mul_mat(a, b)
+    A, B = dev(a), dev(b)
+    out = tc.ggml_empty(tc.mul_mat_out_ne(A, B))
+    out.fill_(float("nan"))  # the kernel zeroes D itself before the split parts are added
+    got = tc.mul_mat(A, B, out=out, one_cta=one).cpu().numpy()
+    again = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(got, want) <= TOL, normwise(got, want)
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))  # deterministic
+
+
+def test_split_k_plane_reduction_one_plane_group(tc):
+    """The GQA dA product at one ne[3] plane per rank (the 8-GPU shape, reduced in size): M = 128
+    after the orientation swap, few tiles, K = 2048 x 4 source planes."""
+    rng = np.random.default_rng(11)
+    G = rng.standard_normal((1, 8, 1024, 512)).astype(np.float32)     # ne [512, 1024, 8, 1]
+    Bm = rng.standard_normal((1, 8, 1024, 128)).astype(np.float32)    # ne [128, 1024, 8, 1]
+    dA = torch.full((1, 2, 512, 128), float("nan"), device="cuda")     # ne [128, 512, 2, 1]
+    tc.mul_mat_repeat_back(dev(G).transpose(-1, -2), dev(Bm).transpose(-1, -2), dA.transpose(-1, -2))
+    prod = oracle.mul_mat(np.swapaxes(G, -1, -2), np.swapaxes(Bm, -1, -2))   # numpy [1, 8, 128, 512]
+    want = np.swapaxes(oracle.repeat_back(prod, [512, 128, 2, 1]), -1, -2)
+    assert tc.device_error() == 0
+    assert normwise(dA.cpu().numpy(), want) <= TOL

@@ -102,6 +102,10 @@ struct TcParams {
     int     a_tma5, b_tma5;    // MN-major operand loaded by one 5-D TMA per stage (else one per 32-row chunk)
     int     accumulate;
     int64_t total_tiles;
+    // split-K: each tile's kv range is cut into `splits` parts of kv_per_split k-blocks, computed by
+    // different CTAs (work units) and reduce-added into D (zeroed beforehand by the host)
+    int     splits, kv_per_split;
+    int64_t total_units;       // total_tiles x splits
     char*   d;
     int64_t d_sm, d_sn, d_s2, d_s3;  // byte strides of D along M, N, plane2, plane3
     int     tma_store;               // 1: D is written (or reduce-added) by TMA from shared memory
@@ -152,6 +156,20 @@ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile)
     c.p2 = static_cast<int>(plane % p.planes2);
     c.p3 = static_cast<int>(plane / p.planes2);
     return c;
+}
+
+struct UnitSpan {
+    int64_t tile;
+    int     kv0, kv1;  // the unit's virtual k-blocks [kv0, kv1)
+};
+
+__device__ __forceinline__ UnitSpan unit_span(const TcParams& p, int64_t unit) {
+    UnitSpan u;
+    const int64_t sp = unit / p.total_tiles;
+    u.tile = unit - sp * p.total_tiles;
+    u.kv0  = static_cast<int>(sp) * p.kv_per_split;
+    u.kv1  = min(p.kv_blocks, u.kv0 + p.kv_per_split);
+    return u;
 }
 
 // K-major tile (rows x 16 fp32, 64 B per row, 8-row swizzle atoms of 512 B): advance 32 B per K=8.
@@ -331,12 +349,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step) {
-                const TileCoord tc = tile_coord<CG>(p, tile);
+            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
+                const UnitSpan us = unit_span(p, unit);
+                const TileCoord tc = tile_coord<CG>(p, us.tile);
                 const int am0 = tc.m0 + BM * static_cast<int>(rank);              // this CTA's A rows
                 const int bn0 = tc.n0 + G::BN_CTA * static_cast<int>(rank);       // this CTA's B rows
-                int r = 0, kb = 0;  // source-plane round and k-block of the virtual k-block vkb
-                for (int vkb = 0; vkb < p.kv_blocks; ++vkb, ++it) {
+                // source-plane round and k-block of the virtual k-block vkb
+                int r = us.kv0 / p.k_blocks, kb = us.kv0 - r * p.k_blocks;
+                for (int vkb = us.kv0; vkb < us.kv1; ++vkb, ++it) {
                     const int sp2 = tc.p2 + p.planes2 * (r % p.red2), sp3 = tc.p3 + p.planes3 * (r / p.red2);
                     const int a2 = sp2 % p.a_ne2, a3 = sp3 % p.a_ne3;
                     const int b2 = sp2 % p.b_ne2, b3 = sp3 % p.b_ne3;
@@ -385,10 +405,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // uses0/uses1: chunks committed so far into TMEM buffer 0/1 (scalars, kept in registers)
             uint32_t it = 0, tcount = 0, uses0 = 0, uses1 = 0;
             bool ok = true;
-            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step, ++tcount) {
-                const int tb = tcount & 1;  // this tile's running-total buffer; chunks >= 1 use tb ^ 1
-                for (int kb0 = 0; kb0 < p.kv_blocks && ok; kb0 += CHUNK_KB) {
-                    const int b = kb0 == 0 ? tb : tb ^ 1;
+            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step, ++tcount) {
+                const UnitSpan us = unit_span(p, unit);
+                const int tb = tcount & 1;  // this unit's running-total buffer; chunks >= 1 use tb ^ 1
+                for (int kb0 = us.kv0; kb0 < us.kv1 && ok; kb0 += CHUNK_KB) {
+                    const int b = kb0 == us.kv0 ? tb : tb ^ 1;
                     const uint32_t ub = b ? uses1 : uses0;
                     if (!mbar_wait_scoped<PAIR>(&bars->acc_empty[b], (ub & 1u) ^ 1u, TRC_DEVERR_WAIT_ACCFREE)) {
                         ok = false;
@@ -396,7 +417,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * BN;
-                    const int kb1 = min(p.kv_blocks, kb0 + CHUNK_KB);
+                    const int kb1 = min(us.kv1, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = it % G::STAGES;
                         if (!mbar_wait_scoped<PAIR>(&bars->split[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
@@ -535,8 +556,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int i_step = SPLIT_WARPS * 32;
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step) {
-                for (int kb = 0; kb < p.kv_blocks; ++kb, ++it) {
+            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
+                const UnitSpan us = unit_span(p, unit);
+                for (int kb = us.kv0; kb < us.kv1; ++kb, ++it) {
                     const int s = it % G::STAGES;
                     if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
                         ok = false;
@@ -572,9 +594,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else mbar_arrive(&bars->acc_empty[b]);
         };
         bool ok = true;
-        for (int64_t tile = tile0; tile < p.total_tiles && ok; tile += tile_step, ++tcount) {
+        for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step, ++tcount) {
+            const UnitSpan us = unit_span(p, unit);
             const int tb = tcount & 1, xb = tb ^ 1;
-            const TileCoord tc = tile_coord<CG>(p, tile);
+            const TileCoord tc = tile_coord<CG>(p, us.tile);
             const int dm0 = tc.m0 + BM * static_cast<int>(rank);  // this CTA's rows of D
             const int m = dm0 + row;
             char* drow = p.d + static_cast<int64_t>(tc.p2) * p.d_s2 + static_cast<int64_t>(tc.p3) * p.d_s3 +
@@ -594,7 +617,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 break;
             if (tb) ++uses1; else ++uses0;
             tc_fence_after();
-            for (int kb0 = CHUNK_KB; kb0 < p.kv_blocks; kb0 += CHUNK_KB) {
+            for (int kb0 = us.kv0 + CHUNK_KB; kb0 < us.kv1; kb0 += CHUNK_KB) {
                 uses_x = xb ? uses1 : uses0;
                 if (!named_barrier_and(EPI_BAR_ALL, EPI_WARPS * 32,
                                        mbar_wait_scoped<PAIR>(&bars->acc_full[xb], uses_x & 1u, TRC_DEVERR_WAIT_ACCUM))) {
@@ -638,7 +661,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     named_barrier_sync(team_bar, 128);
                     if (team_leader) {
                         const uint32_t src = smem_u32(stage_buf);
-                        if (p.accumulate) tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        if (p.accumulate || p.splits > 1) tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
                         else tma_store_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
                         bulk_commit_group();
                     }
@@ -794,6 +817,20 @@ bool encode_output(void* data, int64_t M, int64_t N, int64_t P2, int64_t P3, int
 }
 
 // Launches one instantiation; the >48 KiB dynamic shared memory opt-in is set once per device.
+// True when the view's elements fill a gap-free byte range starting at d.data (a permutation of a
+// contiguous tensor); `bytes` receives its size.
+bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
+    int64_t count = 1, span = 4;
+    for (int i = 0; i < 4; ++i) {
+        if (d.ne[i] <= 0 || d.nb[i] <= 0) return false;
+        count *= d.ne[i];
+        span += (d.ne[i] - 1) * d.nb[i];
+    }
+    if (span != count * 4) return false;
+    bytes = static_cast<size_t>(span);
+    return true;
+}
+
 // Persistent launch: one CTA per SM (CG = 1) or one CTA pair per two SMs (CG = 2, a cluster of 2).
 template <int QTYPE, int QTRANS, int CG>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmD, const TcParams& p,
@@ -840,10 +877,10 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
         if (CG == 2 && dev < 64 && max_pairs[dev] > 0) pairs = std::min(pairs, max_pairs[dev]);
     }
     if constexpr (CG == 1) {
-        const int64_t grid = std::min<int64_t>(p.total_tiles, sms);
+        const int64_t grid = std::min<int64_t>(p.total_units, sms);
         kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmD, p);
     } else {
-        const int64_t clusters = std::min<int64_t>(p.total_tiles, std::max(1, pairs));
+        const int64_t clusters = std::min<int64_t>(p.total_units, std::max(1, pairs));
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -937,6 +974,23 @@ int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const 
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, planes2, planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
+
+    // Split-K when the tiles fill at most half the SMs (or SM pairs) and the reduction is long:
+    // two CTAs per tile, each reduce-adding its partial sum into a zeroed D. Two parts only and no
+    // ACCUMULATE, so the result does not depend on which part lands first (0 + a + b = 0 + b + a).
+    p.splits = 1;
+    p.kv_per_split = p.kv_blocks;
+    const int sms = sm_count_current();
+    const int64_t capacity = CG == 2 ? sms / 2 : sms;
+    size_t dense_bytes = 0;
+    if (!accumulate && p.tma_store && sms > 0 && p.total_tiles * 2 <= capacity && p.kv_blocks >= 2 * CHUNK_KB &&
+        dense_extent(d, dense_bytes)) {
+        p.splits = 2;
+        p.kv_per_split = ((p.kv_blocks + 1) / 2 + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB;
+        const cudaError_t e = cudaMemsetAsync(d.data, 0, dense_bytes, stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    p.total_units = p.total_tiles * p.splits;
     return launch_tc<0, 0, CG>(tmA, tmB, tmD, p, stream);
 }
 
@@ -988,6 +1042,9 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
+    p.splits = 1;
+    p.kv_per_split = p.kv_blocks;
+    p.total_units = p.total_tiles;
 
 #define TRC_Q_CASE(T)                                                                                 \
     case T:                                                                                           \
