@@ -244,6 +244,59 @@ int trc_cuda_sum(const trc_cuda_view* src, float* dst, void* workspace, size_t w
  * (src/core/trc_backend_reg.cpp:539-544) for device-local F32 tensors. */
 int trc_cuda_fill(float* dst, int64_t n, float value, void* stream);
 
+/* ------------------------------------------------------------------ the rest of a training step
+ * The graph ops a Linear training step emits besides mul_mat and its backward, for a model that
+ * lives on the device: a loss's element-wise unaries, row sums, and the optimizer graph train.cpp
+ * builds when parameters, gradients and states share one non-CPU device
+ * (src/optim/trc_optim.cpp:330-420, 760-860). Results are bit-exact with the CPU backend except
+ * trc_cuda_sum_sqr_acc (see there). */
+
+enum {
+    TRC_CUDA_UNARY_SQR = 0,   /* x * x                 fn_sqr   (src/backends/cpu/trc_cpu_ops.cpp:86) */
+    TRC_CUDA_UNARY_SQRT = 1,  /* sqrt(x)               fn_sqrt  (:87) */
+    TRC_CUDA_UNARY_ABS = 2,   /* |x|                   fn_abs   (:85) */
+    TRC_CUDA_UNARY_NEG = 3,   /* -x                    fn_neg   (:84) */
+    TRC_CUDA_UNARY_SGN = 4,   /* sign(x), 0 for 0/NaN  fn_sgn   (:93) */
+    TRC_CUDA_UNARY_STEP = 5,  /* x > 0 ? 1 : 0         fn_step  (:94) */
+    TRC_CUDA_UNARY_SCALE = 6  /* x * param             compute_scale (:139-149) */
+};
+
+/* dst = op(src) element by element (same ne; any strides). Replaces compute_unary / compute_scale
+ * (src/backends/cpu/trc_cpu_ops.cpp:119-149) for OP_SQR, OP_SQRT, OP_ABS, OP_NEG, OP_SGN, OP_STEP,
+ * OP_SCALE. */
+int trc_cuda_unary(int op, const trc_cuda_view* src, const trc_cuda_view* dst, float param, void* stream);
+
+/* dst[0, i1, i2, i3] = sum over i0 of src (take_mean: divided by src.ne0), each row summed in
+ * double in index order and rounded once to float. Replaces compute_sum_rows_or_mean
+ * (src/backends/cpu/trc_cpu_ops.cpp:317-333), OP_SUM_ROWS and OP_MEAN. */
+int trc_cuda_sum_rows(const trc_cuda_view* src, const trc_cuda_view* dst, int take_mean, void* stream);
+
+/* In-place AdamW on n contiguous floats; params6 (HOST) = {step_sz, bc2_sqrt, decay, beta1, beta2,
+ * eps} as the optimizer writes them into the node's op_params. Replaces compute_opt_step_adamw
+ * (src/backends/cpu/trc_cpu_ops.cpp:1506-1538), OP_OPT_STEP_ADAMW. */
+int trc_cuda_opt_step_adamw(float* param, const float* grad, float* m, float* v, int64_t n, const float* params6,
+                            void* stream);
+
+/* In-place SGD on n contiguous floats; params6 (HOST) = {lr, momentum, dampening, weight_decay,
+ * nesterov, is_first}. momentum may be null when params6[1] == 0. Replaces compute_opt_step_sgd
+ * (src/backends/cpu/trc_cpu_ops.cpp:1540-1573), OP_OPT_STEP_SGD. */
+int trc_cuda_opt_step_sgd(float* param, const float* grad, float* momentum, int64_t n, const float* params6,
+                          void* stream);
+
+/* acc[0] += (float) sum of (double) a[i]^2 over n contiguous floats. Replaces compute_sum_sqr_acc
+ * (src/backends/cpu/trc_cpu_ops.cpp:1578-1591), OP_SUM_SQR_ACC. The double sum is taken in a parallel
+ * order: it equals the reference's sequential one after rounding to float except when the two
+ * double sums round to different floats (then they differ by one float ulp). workspace: device
+ * memory of at least trc_cuda_sum_sqr_workspace_bytes(n) bytes. */
+size_t trc_cuda_sum_sqr_workspace_bytes(int64_t n);
+int    trc_cuda_sum_sqr_acc(float* acc, const float* a, int64_t n, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* a[i] *= min(1, max_norm / (sqrt(norm[0]) + eps)) over n contiguous floats, norm read on the device.
+ * Replaces compute_clip_scale_inplace (src/backends/cpu/trc_cpu_ops.cpp:1594-1611),
+ * OP_CLIP_SCALE_INPLACE. */
+int trc_cuda_clip_scale_inplace(float* a, int64_t n, const float* norm, float max_norm, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,19 @@ def oracle_lib() -> ctypes.CDLL:
         L.oracle_repeat_back.argtypes = [_P, _NE, _NB, _P, _NE]
         L.oracle_acc.restype = None
         L.oracle_acc.argtypes = [_P, _P, _NE, _NB, _SZ, _SZ, _SZ, _SZ]
+        _F = ctypes.c_float
+        L.oracle_unary.restype = None
+        L.oracle_unary.argtypes = [_I, _P, _I64, _F, _P]
+        L.oracle_sum_rows.restype = None
+        L.oracle_sum_rows.argtypes = [_P, _I64, _I64, _I, _P]
+        L.oracle_adamw.restype = None
+        L.oracle_adamw.argtypes = [_P, _P, _P, _P, _I64, _P]
+        L.oracle_sgd.restype = None
+        L.oracle_sgd.argtypes = [_P, _P, _P, _I64, _P]
+        L.oracle_sum_sqr_acc.restype = None
+        L.oracle_sum_sqr_acc.argtypes = [_P, _P, _I64]
+        L.oracle_clip_scale.restype = None
+        L.oracle_clip_scale.argtypes = [_P, _I64, _F, _F, _F]
         _oracle = L
     return _oracle
 
@@ -83,6 +96,19 @@ def ref_lib() -> ctypes.CDLL:
         L.ref_mul_mat.argtypes = [_P, _P, _I, _P, _P, _I, _P]
         L.ref_mul_mat_step.restype = _I
         L.ref_mul_mat_step.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P]
+        _F = ctypes.c_float
+        L.ref_unary.restype = _I
+        L.ref_unary.argtypes = [_I, _P, _P, _F, _P]
+        L.ref_sum_rows.restype = _I
+        L.ref_sum_rows.argtypes = [_P, _P, _I, _P]
+        L.ref_opt_step_adamw.restype = _I
+        L.ref_opt_step_adamw.argtypes = [_P, _P, _P, _P, _I64, _P]
+        L.ref_opt_step_sgd.restype = _I
+        L.ref_opt_step_sgd.argtypes = [_P, _P, _P, _I64, _P]
+        L.ref_sum_sqr_acc.restype = _I
+        L.ref_sum_sqr_acc.argtypes = [_P, _P, _I64]
+        L.ref_clip_scale_inplace.restype = _I
+        L.ref_clip_scale_inplace.argtypes = [_P, _I64, _F, _F, _F]
         _ref = L
     return _ref
 
@@ -219,3 +245,109 @@ def ref_mul_mat_step(a: np.ndarray, b: np.ndarray, g: np.ndarray):
     if rc != 0:
         raise RuntimeError("reference training step failed")
     return d, da, db
+
+
+# ------------------------------------------------------------------ the rest of a training step
+
+UNARY_SQR, UNARY_SQRT, UNARY_ABS, UNARY_NEG, UNARY_SGN, UNARY_STEP, UNARY_SCALE = range(7)
+
+
+def _f32(x) -> np.ndarray:
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def _p6(params) -> np.ndarray:
+    p = _f32(params)
+    assert p.size == 6
+    return p
+
+
+def unary(op: int, x: np.ndarray, param: float = 0.0) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty_like(x)
+    oracle_lib().oracle_unary(op, x.ctypes.data, x.size, param, out.ctypes.data)
+    return out
+
+
+def sum_rows(x: np.ndarray, take_mean: bool = False) -> np.ndarray:
+    """Row sums (or means) over the last axis; result keeps the other axes with a last axis of 1."""
+    x = _f32(x)
+    out = np.empty(x.shape[:-1] + (1,), dtype=np.float32)
+    oracle_lib().oracle_sum_rows(x.ctypes.data, x.shape[-1], x.size // max(1, x.shape[-1]), int(take_mean),
+                                 out.ctypes.data)
+    return out
+
+
+def adamw(p, g, m, v, params6):
+    p, g, m, v = (_f32(a).copy() for a in (p, g, m, v))
+    oracle_lib().oracle_adamw(p.ctypes.data, g.ctypes.data, m.ctypes.data, v.ctypes.data, p.size,
+                              _p6(params6).ctypes.data)
+    return p, m, v
+
+
+def sgd(p, g, mom, params6):
+    p, g, mom = (_f32(a).copy() for a in (p, g, mom))
+    oracle_lib().oracle_sgd(p.ctypes.data, g.ctypes.data, mom.ctypes.data, p.size, _p6(params6).ctypes.data)
+    return p, mom
+
+
+def sum_sqr_acc(acc: float, x: np.ndarray) -> np.float32:
+    a = np.array([acc], dtype=np.float32)
+    x = _f32(x)
+    oracle_lib().oracle_sum_sqr_acc(a.ctypes.data, x.ctypes.data, x.size)
+    return a[0]
+
+
+def clip_scale(x: np.ndarray, norm: float, max_norm: float, eps: float) -> np.ndarray:
+    x = _f32(x).copy()
+    oracle_lib().oracle_clip_scale(x.ctypes.data, x.size, norm, max_norm, eps)
+    return x
+
+
+def ref_unary(op: int, x: np.ndarray, param: float = 0.0) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty_like(x)
+    ne = list(x.shape)[::-1] + [1] * (4 - x.ndim)
+    if ref_lib().ref_unary(op, x.ctypes.data, _NE(*ne), param, out.ctypes.data) != 0:
+        raise RuntimeError("reference unary failed")
+    return out
+
+
+def ref_sum_rows(x: np.ndarray, take_mean: bool = False) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty(x.shape[:-1] + (1,), dtype=np.float32)
+    ne = list(x.shape)[::-1] + [1] * (4 - x.ndim)
+    if ref_lib().ref_sum_rows(x.ctypes.data, _NE(*ne), int(take_mean), out.ctypes.data) != 0:
+        raise RuntimeError("reference sum_rows failed")
+    return out
+
+
+def ref_adamw(p, g, m, v, params6):
+    p, g, m, v = (_f32(a).copy() for a in (p, g, m, v))
+    if ref_lib().ref_opt_step_adamw(p.ctypes.data, g.ctypes.data, m.ctypes.data, v.ctypes.data, p.size,
+                                    _p6(params6).ctypes.data) != 0:
+        raise RuntimeError("reference opt_step_adamw failed")
+    return p, m, v
+
+
+def ref_sgd(p, g, mom, params6):
+    p, g, mom = (_f32(a).copy() for a in (p, g, mom))
+    if ref_lib().ref_opt_step_sgd(p.ctypes.data, g.ctypes.data, mom.ctypes.data, p.size,
+                                  _p6(params6).ctypes.data) != 0:
+        raise RuntimeError("reference opt_step_sgd failed")
+    return p, mom
+
+
+def ref_sum_sqr_acc(acc: float, x: np.ndarray) -> np.float32:
+    a = np.array([acc], dtype=np.float32)
+    x = _f32(x)
+    if ref_lib().ref_sum_sqr_acc(a.ctypes.data, x.ctypes.data, x.size) != 0:
+        raise RuntimeError("reference sum_sqr_acc failed")
+    return a[0]
+
+
+def ref_clip_scale(x: np.ndarray, norm: float, max_norm: float, eps: float) -> np.ndarray:
+    x = _f32(x).copy()
+    if ref_lib().ref_clip_scale_inplace(x.ctypes.data, x.size, norm, max_norm, eps) != 0:
+        raise RuntimeError("reference clip_scale_inplace failed")
+    return x

@@ -11,6 +11,9 @@
 //   * mul_mat forward + composed backward through the reference autograd
 //                                        src/core/trc_autograd.cpp:487-503 (OP_MUL_MAT rule),
 //                                        loss = sum(mul(D, G)) injects dL/dD = G exactly (:247-257, :420)
+//   * the rest of a training step on the CPU device: unaries (neg/abs_op/sqr/sqrt_op/sgn/step/scale),
+//     sum_rows / mean, opt_step_adamw / opt_step_sgd and the grad-norm clip pair sum_sqr_acc /
+//     clip_scale_inplace (src/ops/trc_ops.cpp, src/backends/cpu/trc_cpu_ops.cpp)
 //
 // Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm load this.
 #include "traincpp/traincpp.h"
@@ -120,6 +123,138 @@ int ref_mul_mat_step(const float* a, const int64_t* a_ne, const float* b, const 
     graph_free(g);
     context_free(ctx);
     return ok ? 0 : -1;
+}
+
+} // extern "C"
+
+namespace {
+
+// One node evaluated on the reference CPU device: `build` creates the inputs and the node,
+// `upload` sets the inputs after allocation, `read` reads the results back.
+template <class Build, class Upload, class Read>
+int run_node(Build build, Upload upload, Read read) {
+    Context* ctx = context_new((size_t) 1 << 20);
+    Graph*   g   = graph_new(ctx);
+    Tensor*  out = build(ctx);
+    graph_build_forward_expand(ctx, g, out);
+    Device* cpu = device_cpu();
+    Buffer* buf = buffer_alloc_ctx_tensors(ctx, cpu->default_buffer_type());
+    upload();
+    const bool ok = cpu->graph_compute(g);
+    read(out);
+    buffer_free(buf);
+    graph_free(g);
+    context_free(ctx);
+    return ok ? 0 : -1;
+}
+
+} // namespace
+
+extern "C" {
+
+// op: 0 sqr, 1 sqrt, 2 abs, 3 neg, 4 sgn, 5 step, 6 scale(param) -- the library's TRC_CUDA_UNARY_* codes.
+int ref_unary(int op, const float* x, const int64_t* ne, float param, float* out) {
+    Tensor* a = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            a = new_tensor_4d(ctx, TYPE_F32, ne[0], ne[1], ne[2], ne[3]);
+            switch (op) {
+                case 0: return sqr(ctx, a);
+                case 1: return sqrt_op(ctx, a);
+                case 2: return abs_op(ctx, a);
+                case 3: return neg(ctx, a);
+                case 4: return sgn(ctx, a);
+                case 5: return step(ctx, a);
+                default: return scale(ctx, a, param);
+            }
+        },
+        [&] { tensor_set(a, x, 0, nbytes4(ne)); },
+        [&](Tensor* o) { tensor_get(o, out, 0, tensor_nbytes(o)); });
+}
+
+int ref_sum_rows(const float* x, const int64_t* ne, int take_mean, float* out) {
+    Tensor* a = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            a = new_tensor_4d(ctx, TYPE_F32, ne[0], ne[1], ne[2], ne[3]);
+            return take_mean ? mean(ctx, a) : sum_rows(ctx, a);
+        },
+        [&] { tensor_set(a, x, 0, nbytes4(ne)); },
+        [&](Tensor* o) { tensor_get(o, out, 0, tensor_nbytes(o)); });
+}
+
+// In place on p, m, v (n floats each); params6 as the optimizer writes them.
+int ref_opt_step_adamw(float* p, const float* g, float* m, float* v, int64_t n, const float* ps) {
+    Tensor *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            P = new_tensor_1d(ctx, TYPE_F32, n);
+            G = new_tensor_1d(ctx, TYPE_F32, n);
+            M = new_tensor_1d(ctx, TYPE_F32, n);
+            V = new_tensor_1d(ctx, TYPE_F32, n);
+            return opt_step_adamw(ctx, P, G, M, V, ps[0], ps[1], ps[2], ps[3], ps[4], ps[5]);
+        },
+        [&] {
+            tensor_set(P, p, 0, n * sizeof(float));
+            tensor_set(G, g, 0, n * sizeof(float));
+            tensor_set(M, m, 0, n * sizeof(float));
+            tensor_set(V, v, 0, n * sizeof(float));
+        },
+        [&](Tensor*) {
+            tensor_get(P, p, 0, n * sizeof(float));
+            tensor_get(M, m, 0, n * sizeof(float));
+            tensor_get(V, v, 0, n * sizeof(float));
+        });
+}
+
+int ref_opt_step_sgd(float* p, const float* g, float* mom, int64_t n, const float* ps) {
+    Tensor *P = nullptr, *G = nullptr, *M = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            P = new_tensor_1d(ctx, TYPE_F32, n);
+            G = new_tensor_1d(ctx, TYPE_F32, n);
+            M = new_tensor_1d(ctx, TYPE_F32, n);
+            return opt_step_sgd(ctx, P, G, M, ps[0], ps[1], ps[2], ps[3], ps[4] != 0.0f, ps[5] != 0.0f);
+        },
+        [&] {
+            tensor_set(P, p, 0, n * sizeof(float));
+            tensor_set(G, g, 0, n * sizeof(float));
+            tensor_set(M, mom, 0, n * sizeof(float));
+        },
+        [&](Tensor*) {
+            tensor_get(P, p, 0, n * sizeof(float));
+            tensor_get(M, mom, 0, n * sizeof(float));
+        });
+}
+
+int ref_sum_sqr_acc(float* acc, const float* x, int64_t n) {
+    Tensor *ACC = nullptr, *A = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            ACC = new_tensor_1d(ctx, TYPE_F32, 1);
+            A   = new_tensor_1d(ctx, TYPE_F32, n);
+            return sum_sqr_acc(ctx, ACC, A);
+        },
+        [&] {
+            tensor_set(ACC, acc, 0, sizeof(float));
+            tensor_set(A, x, 0, n * sizeof(float));
+        },
+        [&](Tensor*) { tensor_get(ACC, acc, 0, sizeof(float)); });
+}
+
+int ref_clip_scale_inplace(float* x, int64_t n, float norm, float max_norm, float eps) {
+    Tensor *A = nullptr, *N = nullptr;
+    return run_node(
+        [&](Context* ctx) {
+            A = new_tensor_1d(ctx, TYPE_F32, n);
+            N = new_tensor_1d(ctx, TYPE_F32, 1);
+            return clip_scale_inplace(ctx, A, N, max_norm, eps);
+        },
+        [&] {
+            tensor_set(A, x, 0, n * sizeof(float));
+            tensor_set(N, &norm, 0, sizeof(float));
+        },
+        [&](Tensor*) { tensor_get(A, x, 0, n * sizeof(float)); });
 }
 
 } // extern "C"

@@ -6,6 +6,7 @@
  */
 #include "trc_oracle.h"
 
+#include <math.h>
 #include <pthread.h>
 #include <string.h>
 
@@ -249,4 +250,78 @@ void oracle_acc(void* dst, const void* b, const int64_t b_ne[4], const size_t b_
                           (size_t) idx[3] * nb3;
         st(dst, od, ld(dst, od) + ld(b, lin_off(i, b_ne, b_nb)));
     }
+}
+
+/* ---------------------------------------------------------------- the rest of a training step
+ * Built with -ffp-contract=off: every operation below is one IEEE single (or double) operation in
+ * the order the reference writes it, as the reference's own x86 build evaluates it. */
+
+/* fn_neg / fn_abs / fn_sqr / fn_sqrt / fn_sgn / fn_step (src/backends/cpu/trc_cpu_ops.cpp:84-94)
+ * applied by compute_unary (:119-137); compute_scale (:139-149). */
+void oracle_unary(int op, const float* x, int64_t n, float param, float* out) {
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = x[i];
+        float r;
+        switch (op) {
+            case 0: r = v * v; break;
+            case 1: r = sqrtf(v); break;
+            case 2: r = fabsf(v); break;
+            case 3: r = -v; break;
+            case 4: r = v > 0.0f ? 1.0f : (v < 0.0f ? -1.0f : 0.0f); break;
+            case 5: r = v > 0.0f ? 1.0f : 0.0f; break;
+            default: r = v * param; break;
+        }
+        out[i] = r;
+    }
+}
+
+/* row_sum_f32 (src/backends/cpu/trc_cpu_ops.cpp:284-300) + compute_sum_rows_or_mean (:317-333). */
+void oracle_sum_rows(const float* x, int64_t ne0, int64_t rows, int take_mean, float* out) {
+    for (int64_t r = 0; r < rows; ++r) {
+        double sum = 0.0;
+        for (int64_t i = 0; i < ne0; ++i) sum += x[r * ne0 + i];
+        out[r] = take_mean ? (float) (sum / (double) ne0) : (float) sum;
+    }
+}
+
+/* compute_opt_step_adamw (src/backends/cpu/trc_cpu_ops.cpp:1506-1538). */
+void oracle_adamw(float* p, const float* g, float* m, float* v, int64_t n, const float ps[6]) {
+    const float step_sz = ps[0], bc2_sqrt = ps[1], decay = ps[2], beta1 = ps[3], beta2 = ps[4], eps = ps[5];
+    for (int64_t i = 0; i < n; ++i) {
+        const float gi = g[i];
+        m[i] += (gi - m[i]) * (1.0f - beta1);
+        v[i] = v[i] * beta2 + gi * gi * (1.0f - beta2);
+        const float pv    = p[i] * decay;
+        const float denom = sqrtf(v[i]) / bc2_sqrt + eps;
+        p[i]              = pv - step_sz * (m[i] / denom);
+    }
+}
+
+/* compute_opt_step_sgd (src/backends/cpu/trc_cpu_ops.cpp:1540-1573). */
+void oracle_sgd(float* p, const float* g, float* mom, int64_t n, const float ps[6]) {
+    const float lr = ps[0], mc = ps[1], damp = ps[2], wd = ps[3], nesterov = ps[4], is_first = ps[5];
+    for (int64_t i = 0; i < n; ++i) {
+        float d = g[i] + wd * p[i];
+        if (mc != 0.0f) {
+            if (is_first != 0.0f) mom[i] = d;
+            else mom[i] = mc * mom[i] + (1.0f - damp) * d;
+            d = nesterov != 0.0f ? d + mc * mom[i] : mom[i];
+        }
+        p[i] -= lr * d;
+    }
+}
+
+/* compute_sum_sqr_acc (src/backends/cpu/trc_cpu_ops.cpp:1578-1591). */
+void oracle_sum_sqr_acc(float* acc, const float* x, int64_t n) {
+    double s = 0.0;
+    for (int64_t i = 0; i < n; ++i) s += (double) x[i] * (double) x[i];
+    acc[0] = acc[0] + (float) s;
+}
+
+/* compute_clip_scale_inplace (src/backends/cpu/trc_cpu_ops.cpp:1594-1611). */
+void oracle_clip_scale(float* x, int64_t n, float norm, float max_norm, float eps) {
+    const float total = sqrtf(norm);
+    float scale = max_norm / (total + eps);
+    if (scale > 1.0f) scale = 1.0f;
+    for (int64_t i = 0; i < n; ++i) x[i] *= scale;
 }

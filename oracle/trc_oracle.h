@@ -14,6 +14,12 @@
  *   oracle_cont           src/backends/cpu/trc_cpu_ops.cpp:219-236 (compute_dup)
  *   oracle_repeat_back    src/backends/cpu/trc_cpu_ops.cpp:932-951
  *   oracle_acc            src/backends/cpu/trc_cpu_ops.cpp:954-998
+ *   oracle_unary          src/backends/cpu/trc_cpu_ops.cpp:84-94, 119-149 (fn_sqr .. fn_step, compute_scale)
+ *   oracle_sum_rows       src/backends/cpu/trc_cpu_ops.cpp:284-300, 317-333 (row_sum_f32, compute_sum_rows_or_mean)
+ *   oracle_adamw          src/backends/cpu/trc_cpu_ops.cpp:1506-1538 (compute_opt_step_adamw)
+ *   oracle_sgd            src/backends/cpu/trc_cpu_ops.cpp:1540-1573 (compute_opt_step_sgd)
+ *   oracle_sum_sqr_acc    src/backends/cpu/trc_cpu_ops.cpp:1578-1591 (compute_sum_sqr_acc)
+ *   oracle_clip_scale     src/backends/cpu/trc_cpu_ops.cpp:1594-1611 (compute_clip_scale_inplace)
  *
  * Parity status: pinned. tests/test_oracle.py checks this library against the reference's own
  * known-answer tests (tests/test_gguf.cpp:355-444 of the reference) and against the reference
@@ -59,6 +65,23 @@ void oracle_repeat_back(const void* a, const int64_t a_ne[4], const size_t a_nb[
  * + i3*nb3] += b[i]. dst is the byte base of the contiguous destination tensor. */
 void oracle_acc(void* dst, const void* b, const int64_t b_ne[4], const size_t b_nb[4],
                 size_t nb1, size_t nb2, size_t nb3, size_t offset);
+
+/* Element-wise unary over n contiguous floats; op: 0 sqr, 1 sqrt, 2 abs, 3 neg, 4 sgn, 5 step,
+ * 6 scale by param. */
+void oracle_unary(int op, const float* x, int64_t n, float param, float* out);
+
+/* out[r] = sum (take_mean: mean) of row r of a contiguous [ne0, rows] array, in double, in order. */
+void oracle_sum_rows(const float* x, int64_t ne0, int64_t rows, int take_mean, float* out);
+
+/* In-place optimizer steps over n floats; params6 as the reference optimizer writes them. */
+void oracle_adamw(float* p, const float* g, float* m, float* v, int64_t n, const float params6[6]);
+void oracle_sgd(float* p, const float* g, float* mom, int64_t n, const float params6[6]);
+
+/* acc[0] += (float) sum (double) x^2, sequential. */
+void oracle_sum_sqr_acc(float* acc, const float* x, int64_t n);
+
+/* x *= min(1, max_norm / (sqrt(norm) + eps)). */
+void oracle_clip_scale(float* x, int64_t n, float norm, float max_norm, float eps);
 
 #ifdef __cplusplus
 }

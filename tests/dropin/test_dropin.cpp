@@ -256,6 +256,115 @@ void training_steps(Device* cpu, Device* cuda) {
     }
 }
 
+// A Linear model trained for several steps the way the reference trains (its optimizer test
+// fixture: graph_reset + graph_compute, then optim_clip_grad_norm and optim_step;
+// tests/test_optim.cpp of train.cpp): y = W x + b, loss = mean((y - t)^2). On the CUDA device every
+// node -- forward, autograd backward, the optimizer's OP_OPT_STEP_* graph and the clip graph's
+// OP_SUM_SQR_ACC / OP_CLIP_SCALE_INPLACE -- runs on the device.
+struct LoopOut {
+    std::vector<float> w, b;
+    float              loss0 = 0, loss1 = 0;
+};
+
+LoopOut train_loop(Device* dev, bool use_sgd, int steps, float clip) {
+    constexpr int64_t IN = 256, OUT = 160, BATCH = 48;
+    Context* ctx = context_new((size_t) 1 << 24);
+    Graph*   g   = graph_new(ctx);
+    Tensor*  W   = new_tensor_2d(ctx, TYPE_F32, IN, OUT);
+    Tensor*  b   = new_tensor_2d(ctx, TYPE_F32, OUT, 1);
+    Tensor*  x   = new_tensor_2d(ctx, TYPE_F32, IN, BATCH);
+    Tensor*  y   = new_tensor_2d(ctx, TYPE_F32, OUT, BATCH);
+    Tensor*  params[2] = {W, b};
+    tensor_set_param(W);
+    tensor_set_param(b);
+    Tensor* pred = add(ctx, mul_mat(ctx, W, x), b);
+    Tensor* loss = scale(ctx, sum(ctx, sqr(ctx, sub(ctx, pred, y))), 1.0f / (float) (OUT * BATCH));
+    tensor_set_loss(loss);
+    graph_build_forward_expand(ctx, g, loss);
+    graph_build_backward_expand(g);
+    Buffer* buf = buffer_alloc_ctx_tensors(ctx, dev->default_buffer_type());
+    if (const Tensor* bad = graph_first_unsupported(g, dev)) fail(std::string("graph_first_unsupported: ") + op_name(bad->op));
+    const auto vw = gauss((size_t) (IN * OUT), 21, 0.05f), vb = gauss((size_t) OUT, 22, 0.1f);
+    const auto vx = gauss((size_t) (IN * BATCH), 23), vy = gauss((size_t) (OUT * BATCH), 24);
+    tensor_set(W, vw.data(), 0, vw.size() * 4);
+    tensor_set(b, vb.data(), 0, vb.size() * 4);
+    tensor_set(x, vx.data(), 0, vx.size() * 4);
+    tensor_set(y, vy.data(), 0, vy.size() * 4);
+    Optimizer* opt = nullptr;
+    if (use_sgd) {
+        SgdOptions o;
+        o.lr = 0.05f;
+        o.momentum = 0.9f;
+        o.weight_decay = 1e-4f;
+        o.nesterov = true;
+        opt = optim_sgd_new(ctx, params, 2, o);
+    } else {
+        AdamwOptions o;
+        o.lr = 1e-2f;
+        opt = optim_adamw_new(ctx, params, 2, o);
+    }
+    LoopOut r;
+    graph_reset(g);
+    dev->graph_compute(g);
+    tensor_get(loss, &r.loss0, 0, 4);
+    for (int it = 0; it < steps; ++it) {
+        graph_reset(g);
+        dev->graph_compute(g);
+        optim_clip_grad_norm(opt, clip);
+        optim_step(opt);
+    }
+    graph_reset(g);
+    dev->graph_compute(g);
+    tensor_get(loss, &r.loss1, 0, 4);
+    r.w.resize(vw.size());
+    r.b.resize(vb.size());
+    tensor_get(W, r.w.data(), 0, r.w.size() * 4);
+    tensor_get(b, r.b.data(), 0, r.b.size() * 4);
+    optim_free(opt);
+    buffer_free(buf);
+    graph_free(g);
+    context_free(ctx);
+    return r;
+}
+
+void training_loops(Device* cpu, Device* cuda) {
+    const char* simt = std::getenv("TRC_CUDA_MM_SIMT");
+    const bool  exact = simt != nullptr && *simt != '\0' && *simt != '0';
+    std::printf("  training loops: Linear + MSE, optimizer and grad-norm clip on the device (%s)\n",
+                exact ? "SIMT mul_mat: bit-identical" : "tcgen05 mul_mat: within 1e-5");
+    struct Case {
+        const char* name;
+        bool        sgd;
+        float       clip;
+    };
+    const Case cases[] = {{"adamw, 12 steps, clip 0.5", false, 0.5f}, {"sgd nesterov, 12 steps, no clip", true, 1e9f}};
+    for (const Case& c : cases) {
+        const LoopOut want = train_loop(cpu, c.sgd, 12, c.clip);
+        const LoopOut got  = train_loop(cuda, c.sgd, 12, c.clip);
+        const std::string n = c.name;
+        if (!(want.loss1 < want.loss0)) fail(n + ": the reference's loss did not decrease");
+        if (exact) {
+            const bool same = std::memcmp(got.w.data(), want.w.data(), want.w.size() * 4) == 0 &&
+                              std::memcmp(got.b.data(), want.b.data(), want.b.size() * 4) == 0 &&
+                              std::memcmp(&got.loss1, &want.loss1, 4) == 0;
+            if (!same) {
+                fail(n + ": parameters not bit-identical to the CPU device");
+                compare((n + " W").c_str(), got.w, want.w);
+            } else {
+                std::printf("    [ OK ] %-34s W, b and loss bit-identical (loss %.6g -> %.6g)\n", c.name,
+                            (double) want.loss0, (double) want.loss1);
+            }
+        } else {
+            // AdamW divides every update by sqrt(v): on weights whose gradient is near zero, a last-bit
+            // difference of the 3xTF32 GEMM moves the step by O(lr), so after 12 steps W agrees to
+            // ~2e-5 normwise; b, the loss and SGD stay at the per-op 1e-5 bar.
+            compare((n + " W").c_str(), got.w, want.w, false, c.sgd ? 1e-5 : 1e-4);
+            compare((n + " b").c_str(), got.b, want.b);
+            compare((n + " loss").c_str(), {got.loss1}, {want.loss1});
+        }
+    }
+}
+
 void gguf_warm_start(Device* cpu, Device* cuda, const char* path) {
     std::printf("  GGUF warm start: device dequant vs the reference loader (%s)\n", path);
     GgufFile* f = gguf_open(path, true);
@@ -336,6 +445,7 @@ int main(int argc, char** argv) {
     }
     conformance_matmul(cpu, cuda);
     training_steps(cpu, cuda);
+    training_loops(cpu, cuda);
     if (argc > 2) gguf_warm_start(cpu, cuda, argv[2]);
     std::printf("%s: %d failure(s)\n", g_failures == 0 ? "PASS" : "FAIL", g_failures);
     return g_failures == 0 ? 0 : 1;

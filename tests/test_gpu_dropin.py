@@ -55,3 +55,13 @@ def test_allocation_failure_aborts_with_core_message():
     r = run(["alloc_fail"], {"TRC_CUDA_FAIL_ALLOC": "1"})
     assert r.returncode != 0
     assert "分配失败" in r.stderr, r.stderr
+
+
+def test_dropin_bit_identical_with_simt_mul_mat(gguf_path):
+    """With TRC_CUDA_MM_SIMT=1 every mul_mat sums in the reference's order, so whole training loops
+    on the CUDA device (autograd backward, optimizer and grad-norm clip graphs included) end with
+    parameters bit-identical to the reference CPU device."""
+    r = run(["all", str(gguf_path)], {"TRC_CUDA_MM_SIMT": "1"})
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "bit-identical (loss" in r.stdout

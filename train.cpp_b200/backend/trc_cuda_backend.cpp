@@ -207,6 +207,34 @@ public:
             case OP_MUL:
             case OP_DIV:
                 return all_f32(t) && t->src[1] != nullptr && tensor_can_repeat(t->src[1], t->src[0]);
+            case OP_SQR:
+            case OP_SQRT:
+            case OP_ABS:
+            case OP_NEG:
+            case OP_SGN:
+            case OP_STEP:
+            case OP_SCALE:
+                return all_f32(t) && t->src[0] != nullptr && tensor_are_same_shape(t, t->src[0]);
+            case OP_SUM_ROWS:
+            case OP_MEAN:
+                return all_f32(t) && t->src[0] != nullptr;
+            case OP_OPT_STEP_ADAMW:
+            case OP_OPT_STEP_SGD: {
+                // the optimizer graph's nodes (src/optim/trc_optim.cpp:372-388): flat in-place updates
+                const int nstate = t->op == OP_OPT_STEP_ADAMW ? 4 : 3;
+                if (!all_f32(t)) return false;
+                for (int i = 0; i < nstate; ++i) {
+                    const Tensor* s = t->src[i];
+                    if (s == nullptr || !tensor_is_contiguous(s) ||
+                        tensor_nelements(s) != tensor_nelements(t->src[0]))
+                        return false;
+                }
+                return true;
+            }
+            case OP_SUM_SQR_ACC:
+                return all_f32(t) && t->src[1] != nullptr && tensor_is_contiguous(t->src[1]);
+            case OP_CLIP_SCALE_INPLACE:
+                return all_f32(t) && t->src[0] != nullptr && tensor_is_contiguous(t->src[0]);
             default:
                 return false;
         }
@@ -349,7 +377,7 @@ private:
                 const auto it = fused_gemm_.find(t);
                 if (it == fused_gemm_.end()) {
                     const trc_cuda_view d = view_of(t);
-                    CB_TRC(trc_cuda_mul_mat(&a, &b, &d, 0, stream_), "trc_cuda_mul_mat");
+                    CB_TRC(trc_cuda_mul_mat(&a, &b, &d, mm_flags(), stream_), "trc_cuda_mul_mat");
                 } else {
                     const Fused& f = it->second;
                     trc_cuda_view d = view_of(f.target);
@@ -357,7 +385,7 @@ private:
                         std::swap(d.ne[0], d.ne[1]);
                         std::swap(d.nb[0], d.nb[1]);
                     }
-                    const uint32_t flags = f.accumulate ? TRC_CUDA_MM_ACCUMULATE : 0u;
+                    const uint32_t flags = (f.accumulate ? TRC_CUDA_MM_ACCUMULATE : 0u) | mm_flags();
                     if (f.reduce)
                         CB_TRC(trc_cuda_mul_mat_repeat_back(&a, &b, &d, flags, stream_), "trc_cuda_mul_mat_repeat_back (fused)");
                     else
@@ -412,10 +440,82 @@ private:
                        "trc_cuda_acc");
                 return;
             }
+            case OP_SQR:
+            case OP_SQRT:
+            case OP_ABS:
+            case OP_NEG:
+            case OP_SGN:
+            case OP_STEP:
+            case OP_SCALE: {
+                const int op = t->op == OP_SQR    ? TRC_CUDA_UNARY_SQR
+                             : t->op == OP_SQRT   ? TRC_CUDA_UNARY_SQRT
+                             : t->op == OP_ABS    ? TRC_CUDA_UNARY_ABS
+                             : t->op == OP_NEG    ? TRC_CUDA_UNARY_NEG
+                             : t->op == OP_SGN    ? TRC_CUDA_UNARY_SGN
+                             : t->op == OP_STEP   ? TRC_CUDA_UNARY_STEP
+                                                  : TRC_CUDA_UNARY_SCALE;
+                float param = 0.0f;
+                if (t->op == OP_SCALE) std::memcpy(&param, t->op_params, sizeof(float));  // src/ops/trc_ops.cpp:113
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                CB_TRC(trc_cuda_unary(op, &a, &d, param, stream_), "trc_cuda_unary");
+                return;
+            }
+            case OP_SUM_ROWS:
+            case OP_MEAN: {
+                const trc_cuda_view a = view_of(t->src[0]), d = view_of(t);
+                CB_TRC(trc_cuda_sum_rows(&a, &d, t->op == OP_MEAN ? 1 : 0, stream_), "trc_cuda_sum_rows");
+                return;
+            }
+            case OP_OPT_STEP_ADAMW:
+            case OP_OPT_STEP_SGD: {
+                // the node is a full view of the parameter; op_params float[6] (src/ops/trc_ops.cpp:792-811)
+                float ps[6];
+                std::memcpy(ps, t->op_params, sizeof(ps));
+                float* p = static_cast<float*>(view_of(t).data);
+                const float* g = static_cast<const float*>(view_of(t->src[1]).data);
+                float* m = static_cast<float*>(view_of(t->src[2]).data);
+                const int64_t n = tensor_nelements(t->src[0]);
+                if (t->op == OP_OPT_STEP_ADAMW) {
+                    float* v = static_cast<float*>(view_of(t->src[3]).data);
+                    CB_TRC(trc_cuda_opt_step_adamw(p, g, m, v, n, ps, stream_), "trc_cuda_opt_step_adamw");
+                } else {
+                    CB_TRC(trc_cuda_opt_step_sgd(p, g, m, n, ps, stream_), "trc_cuda_opt_step_sgd");
+                }
+                return;
+            }
+            case OP_SUM_SQR_ACC: {
+                // the node is a full view of the one-element accumulator (src/ops/trc_ops.cpp:815-828)
+                float* acc = static_cast<float*>(view_of(t).data);
+                const Tensor* a = t->src[1];
+                const int64_t n = tensor_nelements(a);
+                const size_t ws = trc_cuda_sum_sqr_workspace_bytes(n);
+                CB_TRC(trc_cuda_sum_sqr_acc(acc, static_cast<const float*>(view_of(a).data), n, scratch(ws), ws, stream_),
+                       "trc_cuda_sum_sqr_acc");
+                return;
+            }
+            case OP_CLIP_SCALE_INPLACE: {
+                float ps[2];  // max_norm, eps (src/ops/trc_ops.cpp:830-844)
+                std::memcpy(ps, t->op_params, sizeof(ps));
+                float* a = static_cast<float*>(view_of(t).data);
+                const float* norm = static_cast<const float*>(view_of(t->src[1]).data);
+                CB_TRC(trc_cuda_clip_scale_inplace(a, tensor_nelements(t->src[0]), norm, ps[0], ps[1], stream_),
+                       "trc_cuda_clip_scale_inplace");
+                return;
+            }
             default:
                 CB_ABORT("CUDA: 不支持的算子 %s（张量 %s）；请先用 graph_first_unsupported 预检", op_name(t->op),
                          t->name);
         }
+    }
+
+    // TRC_CUDA_MM_SIMT=1 runs every mul_mat on the SIMT kernel, which sums in the reference's order,
+    // so whole training runs can be compared bit for bit with the CPU device.
+    static uint32_t mm_flags() {
+        static const uint32_t flags = [] {
+            const char* e = std::getenv("TRC_CUDA_MM_SIMT");
+            return (e != nullptr && *e != '\0' && *e != '0') ? static_cast<uint32_t>(TRC_CUDA_MM_SIMT) : 0u;
+        }();
+        return flags;
     }
 
     int            ordinal_;

@@ -22,7 +22,7 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU_SOURCES = ["capi.cu", "runtime.cu", "dequant.cu", "elementwise.cu", "mul_mat_simt.cu", "gemm_tf32x3.cu",
-              "static_staging.cu"]
+              "static_staging.cu", "train_ops.cu"]
 
 
 def _run(cmd: list[str], log: Path | None = None) -> None:

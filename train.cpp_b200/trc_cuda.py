@@ -97,6 +97,13 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_rt_ipc_open": (I, [P, ctypes.POINTER(P)]),
         "trc_cuda_rt_ipc_close": (I, [P]),
         "trc_cuda_rt_can_access_peer": (I, [I, I, ctypes.POINTER(I)]),
+        "trc_cuda_unary": (I, [I, VP, VP, ctypes.c_float, P]),
+        "trc_cuda_sum_rows": (I, [VP, VP, I, P]),
+        "trc_cuda_opt_step_adamw": (I, [P, P, P, P, I64, P, P]),
+        "trc_cuda_opt_step_sgd": (I, [P, P, P, I64, P, P]),
+        "trc_cuda_sum_sqr_workspace_bytes": (SZ, [I64]),
+        "trc_cuda_sum_sqr_acc": (I, [P, P, I64, P, SZ, P]),
+        "trc_cuda_clip_scale_inplace": (I, [P, I64, P, ctypes.c_float, ctypes.c_float, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -522,3 +529,86 @@ def exported_symbols() -> list[str]:
 
 if os.environ.get("TRC_CUDA_PRELOAD") == "1":  # opt-in eager load (used by smoke checks)
     lib()
+
+
+# ------------------------------------------------------------------ the rest of a training step
+
+UNARY_SQR, UNARY_SQRT, UNARY_ABS, UNARY_NEG, UNARY_SGN, UNARY_STEP, UNARY_SCALE = range(7)
+
+
+def unary(op: int, src: torch.Tensor, out: torch.Tensor | None = None, param: float = 0.0,
+          stream=None) -> torch.Tensor:
+    """sqr / sqrt / abs / neg / sgn / step / scale(param), element by element (any strides)."""
+    if out is None:
+        out = ggml_empty(ggml_ne(src), device=src.device)
+    vs, vd = view_of(src), view_of(out)
+    _check(lib().trc_cuda_unary(op, ctypes.byref(vs), ctypes.byref(vd), param, _stream(stream)), "trc_cuda_unary")
+    return out
+
+
+def sqr(src: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    return unary(UNARY_SQR, src, out, 0.0, stream)
+
+
+def scale(src: torch.Tensor, s: float, out=None, stream=None) -> torch.Tensor:
+    return unary(UNARY_SCALE, src, out, s, stream)
+
+
+def sum_rows(src: torch.Tensor, out: torch.Tensor | None = None, mean: bool = False, stream=None) -> torch.Tensor:
+    """ggml sum_rows (or mean): one value per row, summed in double in index order."""
+    ne = ggml_ne(src)
+    if out is None:
+        out = ggml_empty([1, ne[1], ne[2], ne[3]], device=src.device)
+    vs, vd = view_of(src), view_of(out)
+    _check(lib().trc_cuda_sum_rows(ctypes.byref(vs), ctypes.byref(vd), 1 if mean else 0, _stream(stream)),
+           "trc_cuda_sum_rows")
+    return out
+
+
+def _params6(params) -> ctypes.Array:
+    vals = [float(x) for x in params]
+    if len(vals) != 6:
+        raise TrcCudaError("optimizer steps take six op parameters")
+    return (ctypes.c_float * 6)(*vals)
+
+
+def _flat(t: torch.Tensor, what: str) -> int:
+    if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+        raise TrcCudaError(f"{what} must be a contiguous float32 CUDA tensor")
+    return t.data_ptr()
+
+
+def opt_step_adamw_(param: torch.Tensor, grad: torch.Tensor, m: torch.Tensor, v: torch.Tensor, params6,
+                    stream=None) -> None:
+    """In-place AdamW step (the optimizer's OP_OPT_STEP_ADAMW node); params6 = {step_sz, bc2_sqrt,
+    decay, beta1, beta2, eps}."""
+    n = param.numel()
+    if not (grad.numel() == m.numel() == v.numel() == n):
+        raise TrcCudaError("opt_step_adamw: tensors differ in size")
+    _check(lib().trc_cuda_opt_step_adamw(_flat(param, "param"), _flat(grad, "grad"), _flat(m, "m"), _flat(v, "v"), n,
+                                         _params6(params6), _stream(stream)), "trc_cuda_opt_step_adamw")
+
+
+def opt_step_sgd_(param: torch.Tensor, grad: torch.Tensor, momentum: torch.Tensor, params6, stream=None) -> None:
+    """In-place SGD step (OP_OPT_STEP_SGD); params6 = {lr, momentum, dampening, weight_decay,
+    nesterov, is_first}."""
+    n = param.numel()
+    if not (grad.numel() == momentum.numel() == n):
+        raise TrcCudaError("opt_step_sgd: tensors differ in size")
+    _check(lib().trc_cuda_opt_step_sgd(_flat(param, "param"), _flat(grad, "grad"), _flat(momentum, "momentum"), n,
+                                       _params6(params6), _stream(stream)), "trc_cuda_opt_step_sgd")
+
+
+def sum_sqr_acc_(acc: torch.Tensor, a: torch.Tensor, stream=None) -> None:
+    """acc[0] += sum of a^2 (double accumulation), the clip graph's OP_SUM_SQR_ACC."""
+    n = a.numel()
+    ws_bytes = int(lib().trc_cuda_sum_sqr_workspace_bytes(n))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device)
+    _check(lib().trc_cuda_sum_sqr_acc(_flat(acc, "acc"), _flat(a, "a"), n, ws.data_ptr(), ws_bytes, _stream(stream)),
+           "trc_cuda_sum_sqr_acc")
+
+
+def clip_scale_(a: torch.Tensor, norm: torch.Tensor, max_norm: float, eps: float = 1e-6, stream=None) -> None:
+    """a *= min(1, max_norm / (sqrt(norm[0]) + eps)), the clip graph's OP_CLIP_SCALE_INPLACE."""
+    _check(lib().trc_cuda_clip_scale_inplace(_flat(a, "a"), a.numel(), _flat(norm, "norm"), max_norm, eps,
+                                             _stream(stream)), "trc_cuda_clip_scale_inplace")
