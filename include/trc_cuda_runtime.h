@@ -34,10 +34,19 @@ int trc_cuda_rt_free_host(void* ptr);
 /* kind: 0 host->device, 1 device->host, 2 device->device. Synchronous. */
 int trc_cuda_rt_memcpy(void* dst, const void* src, size_t bytes, int kind);
 int trc_cuda_rt_memset(void* dst, int value, size_t bytes);
+/* Asynchronous on `stream`; a host side must be pinned (trc_cuda_rt_malloc_host) to overlap. */
+int trc_cuda_rt_memcpy_async(void* dst, const void* src, size_t bytes, int kind, void* stream);
 
 int trc_cuda_rt_stream_create(void** stream);           /* non-blocking stream of the current device */
 int trc_cuda_rt_stream_destroy(void* stream);
 int trc_cuda_rt_stream_sync(void* stream);
+
+/* Events (timing disabled): mark a point of a stream's work and wait for it from the host, e.g.
+ * before a pinned staging buffer that an asynchronous copy reads is refilled. */
+int trc_cuda_rt_event_create(void** event);
+int trc_cuda_rt_event_destroy(void* event);
+int trc_cuda_rt_event_record(void* event, void* stream);
+int trc_cuda_rt_event_sync(void* event);
 
 /* Peer memory between the processes of one node (one process per GPU), for the dequant
  * all-gather over NVLink (trc_cuda_dequant_many_to_peers). Plain CUDA IPC mappings: peer loads

@@ -7,7 +7,7 @@
 // backend conformance suite compares its Vulkan device with the CPU
 // (tests/test_backend_conformance.cpp:43-128 of train.cpp).
 //
-// usage: test_dropin [all|alloc_fail] [path/to/quantized.gguf]
+// usage: test_dropin [all|alloc_fail|shard] [path/to/quantized.gguf]
 // Exit status 0 when every case passes.
 #include "traincpp/traincpp.h"
 #include "trc_cuda_backend.h"
@@ -421,6 +421,57 @@ void gguf_warm_start(Device* cpu, Device* cuda, const char* path) {
     gguf_close(f);
 }
 
+// The sharded model loader: every rank's share (gguf_shard_tensors) streamed from the file with
+// cuda_gguf_load_tensors through a small staging buffer (so tensors span several chunks), each
+// tensor bit-identical to the reference's gguf_load_tensor, the ranks' shares a partition of the
+// file. Prints "shard <world> <rank>: <indices>" for the caller to compare with its own LPT plan.
+void gguf_sharded_load(Device* cuda, const char* path, int world) {
+    std::printf("  sharded GGUF load over %d ranks (%s)\n", world, path);
+    GgufFile* meta = gguf_open(path, false);  // header only: nothing of the data segment on the host
+    GgufFile* full = gguf_open(path, true);   // the reference loader's view
+    if (meta == nullptr || full == nullptr) {
+        fail("gguf_open failed");
+        return;
+    }
+    std::vector<int> owner(static_cast<size_t>(gguf_tensor_count(meta)), -1);
+    for (int r = 0; r < world; ++r) {
+        const std::vector<int64_t> mine = gguf_shard_tensors(meta, r, world);
+        std::printf("shard %d %d:", world, r);
+        for (int64_t ti : mine) std::printf(" %lld", (long long) ti);
+        std::printf("\n");
+        Context* ctx = context_new(1 << 20);
+        std::vector<const char*> names;
+        std::vector<Tensor*> dsts, refs;
+        for (int64_t ti : mine) {
+            if (owner[static_cast<size_t>(ti)] != -1) fail("tensor dealt to two ranks");
+            owner[static_cast<size_t>(ti)] = r;
+            const GgufTensorInfo* info = gguf_tensor_info(meta, ti);
+            names.push_back(info->name);
+            dsts.push_back(gguf_new_tensor(ctx, meta, info->name, TYPE_F32));
+            refs.push_back(gguf_new_tensor(ctx, full, info->name, TYPE_F32));
+        }
+        Buffer* buf = buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
+        const int before = g_failures;
+        const bool ok = cuda_gguf_load_tensors(meta, path, names.data(), dsts.data(), names.size(), size_t(1) << 20);
+        if (!ok) fail("cuda_gguf_load_tensors failed");
+        for (size_t i = 0; i < names.size(); ++i) {
+            if (!gguf_load_tensor(full, names[i], refs[i])) fail("reference gguf_load_tensor failed");
+            const size_t n = (size_t) tensor_nelements(dsts[i]);
+            std::vector<float> a(n), b(n);
+            tensor_get(dsts[i], a.data(), 0, n * 4);
+            tensor_get(refs[i], b.data(), 0, n * 4);
+            if (std::memcmp(a.data(), b.data(), n * 4) != 0) fail(std::string("sharded load of ") + names[i] + " differs");
+        }
+        if (g_failures == before) std::printf("    [ OK ] rank %d: %zu tensors bit-identical\n", r, names.size());
+        buffer_free(buf);
+        context_free(ctx);
+    }
+    for (int o : owner)
+        if (o < 0) fail("a tensor was dealt to no rank");
+    gguf_close(meta);
+    gguf_close(full);
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -442,6 +493,11 @@ int main(int argc, char** argv) {
         buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
         std::printf("allocation unexpectedly succeeded\n");
         return 0;
+    }
+    if (mode == "shard" && argc > 2) {
+        for (int world : {1, 2, 3}) gguf_sharded_load(cuda, argv[2], world);
+        std::printf("%s: %d failure(s)\n", g_failures == 0 ? "PASS" : "FAIL", g_failures);
+        return g_failures == 0 ? 0 : 1;
     }
     conformance_matmul(cpu, cuda);
     training_steps(cpu, cuda);

@@ -65,3 +65,47 @@ def test_dropin_bit_identical_with_simt_mul_mat(gguf_path):
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "bit-identical (loss" in r.stdout
+
+
+@pytest.fixture(scope="module")
+def model_gguf(tmp_path_factory):
+    """A small model-like file: 14 tensors of every legacy type, sizes spread over two orders of
+    magnitude (several larger than the loader's 1 MiB test staging), and one F32 tensor (which the
+    reference loader handles)."""
+    p = tmp_path_factory.mktemp("gguf") / "model.gguf"
+    shapes = [(4096, 600), (1024, 96), (4096, 64), (512, 40), (4096, 33), (256, 7), (2048, 512), (4096, 128),
+              (1024, 1024), (64, 64), (4096, 300), (128, 11), (2048, 256)]
+    types = [synth.TYPE_Q5_1, synth.TYPE_Q4_0, synth.TYPE_Q8_0, synth.TYPE_Q5_0, synth.TYPE_Q4_1]
+    tensors = []
+    for i, ne in enumerate(shapes):
+        t = types[i % len(types)]
+        tensors.append((f"t{i}", t, ne, synth.random_blocks(t, ne[0] * ne[1] // 32, seed=700 + i)))
+    f32 = synth.normal((48, 64), seed=799)
+    tensors.append(("norm.weight", synth.TYPE_F32, (64, 48), f32))
+    synth.write_gguf(p, tensors)
+    return p, tensors
+
+
+def test_sharded_model_load(model_gguf):
+    """cuda_gguf_load_tensors over each rank's share (gguf_shard_tensors) at 1, 2 and 3 ranks:
+    bit-identical to the reference loader, and the C++ plan equals sharding.lpt_shards over the same
+    load bytes (packed or F32 bytes read + F32 bytes written)."""
+    import re
+
+    import sharding
+
+    path, tensors = model_gguf
+    r = run(["shard", str(path)])
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    sizes = []
+    for _, t, ne, data in tensors:
+        n = ne[0] * ne[1]
+        sizes.append(data.nbytes + 4 * n)
+    for world in (1, 2, 3):
+        want = sharding.lpt_shards(sizes, world)
+        for rank in range(world):
+            m = re.search(rf"^shard {world} {rank}:(.*)$", r.stdout, re.M)
+            assert m, r.stdout
+            got = [int(x) for x in m.group(1).split()]
+            assert got == want[rank], (world, rank, got, want[rank])

@@ -60,3 +60,22 @@ def test_fused_config_shape_slice(tc):
     dy = (np.random.default_rng(1).standard_normal((16, w_ne1)) * 1e-2).astype(np.float32)
     got_t = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True).cpu().numpy()
     assert normwise(got_t, oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)) <= 1e-5
+
+
+def test_cfg1_cpu_runnable_config_in_full(tc):
+    """BASELINE config 1 end to end: one Q4_0 weight ne=[4096,4096] (d ~ U[1e-3, 1e-2], uniform
+    nibbles), dequantized on the device bit-exact, then mul_mat with X ne=[4096,512] ~ N(0,1) within
+    1e-5 normwise of the reference summation (the oracle, threaded), both through the two-step path
+    and through the fused dequant-in-prologue kernel."""
+    qtype, ne0, ne1, n = synth.TYPE_Q4_0, 4096, 4096, 512
+    blocks = synth.random_blocks(qtype, ne0 * ne1 // 32, seed=2024)
+    Wf = oracle.dequant(qtype, blocks).reshape(ne1, ne0)
+    got_w = tc.gguf_tensor_to_f32(qtype, dev(blocks)).cpu().numpy().reshape(ne1, ne0)
+    assert np.array_equal(got_w.view(np.uint32), Wf.view(np.uint32))
+    x = synth.normal((n, ne0), seed=2025)
+    want = oracle.mul_mat(Wf, x)
+    two_step = tc.mul_mat(dev(Wf), dev(x)).cpu().numpy()
+    fused = tc.mul_mat_q(qtype, dev(blocks), ne0, ne1, dev(x)).cpu().numpy()
+    assert normwise(two_step, want) <= 1e-5
+    assert normwise(fused, want) <= 1e-5
+    assert tc.device_error() == 0

@@ -17,6 +17,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -634,6 +635,124 @@ bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name
     CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
     if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
     return true;
+}
+
+// Algorithmic bytes of loading one file tensor: what is read (packed or F32) plus the F32 written.
+static int64_t load_bytes(const GgufFile* f, int64_t ti) {
+    const GgufTensorInfo* info = gguf_tensor_info(f, ti);
+    return static_cast<int64_t>(info->nbytes) + 4 * gguf_tensor_nelements(f, ti);
+}
+
+std::vector<int64_t> gguf_shard_tensors(const GgufFile* f, int rank, int world) {
+    if (f == nullptr || world <= 0 || rank < 0 || rank >= world) CB_ABORT("gguf_shard_tensors: 参数无效");
+    const int64_t n = gguf_tensor_count(f);
+    std::vector<int64_t> order(static_cast<size_t>(n));
+    for (int64_t i = 0; i < n; ++i) order[static_cast<size_t>(i)] = i;
+    // largest first, ties by file order; each tensor to the least-loaded rank, ties to the lowest rank
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int64_t a, int64_t b) { return load_bytes(f, a) > load_bytes(f, b); });
+    std::vector<int64_t> loads(static_cast<size_t>(world), 0);
+    std::vector<int64_t> mine;
+    for (const int64_t ti : order) {
+        const auto least = std::min_element(loads.begin(), loads.end());
+        *least += load_bytes(f, ti);
+        if (least - loads.begin() == rank) mine.push_back(ti);
+    }
+    std::sort(mine.begin(), mine.end());
+    return mine;
+}
+
+bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* const* names, Tensor* const* dsts,
+                            size_t count, size_t staging_bytes) {
+    if (f == nullptr || path == nullptr || (count > 0 && (names == nullptr || dsts == nullptr)))
+        CB_ABORT("cuda_gguf_load_tensors: 参数为空");
+    struct Job {
+        const GgufTensorInfo* info;
+        int64_t               n_units;  // 32-weight blocks, or floats for an F32 file tensor
+        float*                out;
+    };
+    std::vector<Job> jobs;
+    std::vector<size_t> fallback;  // tensors the reference loader handles (not quantized / not on CUDA)
+    CudaDevice* dev = nullptr;
+    for (size_t i = 0; i < count; ++i) {
+        const int64_t ti = gguf_find_tensor(f, names[i]);
+        if (ti < 0) {
+            std::fprintf(stderr, "[traincpp] GGUF: 张量不存在 %s\n", names[i]);
+            return false;
+        }
+        const GgufTensorInfo* info = gguf_tensor_info(f, ti);
+        CudaBuffer* buf = cuda_buffer_of(dsts[i]);
+        if ((!is_legacy_quant(info->type) && info->type != TYPE_F32) || dsts[i]->type != TYPE_F32 || buf == nullptr) {
+            fallback.push_back(i);
+            continue;
+        }
+        if (!tensor_is_contiguous(dsts[i]) || tensor_nelements(dsts[i]) != gguf_tensor_nelements(f, ti)) {
+            std::fprintf(stderr, "[traincpp] GGUF: 目标张量 %s 必须连续且元素数一致\n", names[i]);
+            return false;
+        }
+        CudaDevice* d = static_cast<CudaDevice*>(buf->buffer_type()->device());
+        if (dev != nullptr && d != dev) CB_ABORT("cuda_gguf_load_tensors: 目标张量须在同一 CUDA 设备上");
+        dev = d;
+        const bool quant = info->type != TYPE_F32;
+        jobs.push_back({info, quant ? gguf_tensor_nelements(f, ti) / 32 : gguf_tensor_nelements(f, ti),
+                        reinterpret_cast<float*>(buf->device_ptr() + dsts[i]->data_offset)});
+    }
+    bool ok = true;
+    if (!jobs.empty()) {
+        const size_t S = std::max<size_t>(staging_bytes / 16 * 16, 4096);
+        FILE* fp = std::fopen(path, "rb");
+        if (fp == nullptr) {
+            std::fprintf(stderr, "[traincpp] GGUF: 无法打开 %s\n", path);
+            return false;
+        }
+        CB_CUDA(trc_cuda_rt_set_device(dev->ordinal()));
+        void* host[2] = {nullptr, nullptr};
+        void* done[2] = {nullptr, nullptr};
+        for (int k = 0; k < 2; ++k) {
+            CB_CUDA(trc_cuda_rt_malloc_host(&host[k], S));
+            CB_CUDA(trc_cuda_rt_event_create(&done[k]));
+        }
+        uint8_t* staging = static_cast<uint8_t*>(dev->scratch(2 * S));
+        // chunks of whole blocks; chunk c uses pinned buffer and device staging c % 2, refilled only
+        // after the copy of chunk c - 2 has read it (its event)
+        uint64_t c = 0;
+        for (const Job& J : jobs) {
+            const bool    quant = J.info->type != TYPE_F32;
+            const size_t  bb = quant ? trc_cuda_block_bytes(static_cast<int>(J.info->type)) : sizeof(float);
+            const int64_t per_chunk = static_cast<int64_t>(S / bb);
+            for (int64_t b0 = 0; ok && b0 < J.n_units; b0 += per_chunk, ++c) {
+                const int64_t nb = std::min(per_chunk, J.n_units - b0);
+                const int k = static_cast<int>(c & 1u);
+                if (c >= 2) CB_CUDA(trc_cuda_rt_event_sync(done[k]));
+                const long pos = static_cast<long>(gguf_data_offset(f) + J.info->offset + static_cast<uint64_t>(b0) * bb);
+                const size_t bytes = static_cast<size_t>(nb) * bb;
+                if (std::fseek(fp, pos, SEEK_SET) != 0 || std::fread(host[k], 1, bytes, fp) != bytes) {
+                    std::fprintf(stderr, "[traincpp] GGUF: 张量 %s 数据越界\n", J.info->name);
+                    ok = false;
+                    break;
+                }
+                if (quant)
+                    CB_TRC(trc_cuda_load_quant(static_cast<int>(J.info->type), host[k], nb, staging + k * S,
+                                               J.out + b0 * 32, dev->stream()),
+                           "trc_cuda_load_quant");
+                else  // F32 file tensor: a plain copy (the reference's F32 branch, src/io/trc_gguf.cpp:1079)
+                    CB_CUDA(trc_cuda_rt_memcpy_async(J.out + b0, host[k], bytes, 0, dev->stream()));
+                CB_CUDA(trc_cuda_rt_event_record(done[k], dev->stream()));
+            }
+            if (!ok) break;
+        }
+        std::fclose(fp);
+        CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
+        for (int k = 0; k < 2; ++k) {
+            trc_cuda_rt_event_destroy(done[k]);
+            trc_cuda_rt_free_host(host[k]);
+        }
+        int code = 0;
+        CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
+        if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
+    }
+    for (const size_t i : fallback) ok = ok && gguf_load_tensor(f, names[i], dsts[i]);
+    return ok;
 }
 
 }  // namespace traincpp

@@ -14,6 +14,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace traincpp {
 
@@ -32,6 +33,23 @@ int cuda_register_devices();
 // bit-exact with the reference. Non-quantized file types and non-CUDA destinations fall back to
 // the reference's own gguf_load_tensor. Returns false (and logs) where the reference would.
 bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name, Tensor* dst);
+
+// The file tensors rank `rank` of `world` loads when a whole model is dealt to one process per GPU:
+// a byte-balanced greedy LPT over each tensor's load bytes (bytes read + F32 bytes written),
+// largest first, ties by file order, each tensor to the least-loaded rank (ties to the lowest).
+// Returns this rank's tensor indices in file order; the ranks' lists partition the file.
+std::vector<int64_t> gguf_shard_tensors(const GgufFile* f, int rank, int world);
+
+// Streams `count` file tensors into their F32 destinations on one CUDA device (the GGUF reader can
+// have been opened with load_data = false: nothing of the data segment is held on the host).
+// Packed blocks are read from `path` in chunks of whole blocks into two pinned staging buffers of
+// `staging_bytes`; the file read of the next chunk overlaps the copy and dequant of the current one
+// on the device; F32 file tensors are copied the same way. Other file types (F16), and destinations
+// that are not on a CUDA buffer, go through the reference's gguf_load_tensor (which needs the data
+// segment loaded). Bit-exact with gguf_load_tensor; returns false (and logs) where the reference
+// would.
+bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* const* names, Tensor* const* dsts,
+                            size_t count, size_t staging_bytes = size_t(64) << 20);
 
 }  // namespace traincpp
 

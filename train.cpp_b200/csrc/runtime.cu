@@ -90,6 +90,14 @@ int trc_cuda_rt_memcpy(void* dst, const void* src, size_t bytes, int kind) {
     return rt(cudaMemcpy(dst, src, bytes, k));
 }
 
+int trc_cuda_rt_memcpy_async(void* dst, const void* src, size_t bytes, int kind, void* stream) {
+    if (bytes == 0) return TRC_CUDA_OK;
+    if (dst == nullptr || src == nullptr || kind < 0 || kind > 2) return TRC_CUDA_EINVAL;
+    const cudaMemcpyKind k = kind == 0 ? cudaMemcpyHostToDevice : kind == 1 ? cudaMemcpyDeviceToHost
+                                                                             : cudaMemcpyDeviceToDevice;
+    return rt(cudaMemcpyAsync(dst, src, bytes, k, static_cast<cudaStream_t>(stream)));
+}
+
 int trc_cuda_rt_memset(void* dst, int value, size_t bytes) {
     if (bytes == 0) return TRC_CUDA_OK;
     if (dst == nullptr) return TRC_CUDA_EINVAL;
@@ -107,6 +115,26 @@ int trc_cuda_rt_stream_create(void** stream) {
 int trc_cuda_rt_stream_destroy(void* stream) { return rt(cudaStreamDestroy(static_cast<cudaStream_t>(stream))); }
 
 int trc_cuda_rt_stream_sync(void* stream) { return rt(cudaStreamSynchronize(static_cast<cudaStream_t>(stream))); }
+
+int trc_cuda_rt_event_create(void** event) {
+    if (event == nullptr) return TRC_CUDA_EINVAL;
+    cudaEvent_t e = nullptr;
+    const int st = rt(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    *event = e;
+    return st;
+}
+
+int trc_cuda_rt_event_destroy(void* event) { return rt(cudaEventDestroy(static_cast<cudaEvent_t>(event))); }
+
+int trc_cuda_rt_event_record(void* event, void* stream) {
+    if (event == nullptr) return TRC_CUDA_EINVAL;
+    return rt(cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)));
+}
+
+int trc_cuda_rt_event_sync(void* event) {
+    if (event == nullptr) return TRC_CUDA_EINVAL;
+    return rt(cudaEventSynchronize(static_cast<cudaEvent_t>(event)));
+}
 
 static_assert(sizeof(cudaIpcMemHandle_t) == TRC_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
 
