@@ -201,27 +201,36 @@ __device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
 // A-tile offsets (the same in both geometries), used by the fused decode.
 constexpr int OFF_A_RAW = 0, OFF_A_TAIL = BM * BK * 4;
 
-// decode_quad_words with the fp16 fields converted by the hardware (cvt.f32.f16): the same value
-// for every finite scale and minimum, in one instruction instead of the portable bit decode.
+// decode_quad_words in few instructions, with the same results: the fp16 fields go through the
+// hardware converter (cvt.f32.f16, exact for every finite half), the four integer codes are
+// gathered into the four bytes of one word (Q5: the high bits spread to bit 4 of each byte by one
+// multiply), and each byte becomes the float 2^23 + code with one byte permute; subtracting
+// 2^23 + offset (8 / 16 / 128 for Q4_0 / Q5_0 / Q8_0, whose int8 byte is stored with its sign bit
+// flipped) gives the weight's integer q exactly. q * d is then the reference's product (exact), and
+// q * d + m one fused multiply-add (the product is exact, so it rounds once, like the reference).
 template <int TYPE>
 __device__ __forceinline__ void decode_quad_words_cvt(const QuadWords& r, int j0, float (&w)[4]) {
     const float    d = __half2float(__ushort_as_half(static_cast<unsigned short>(r.d)));
     const uint32_t q = r.q0 | (r.q1 << 16);
+    uint32_t codes;
     if constexpr (TYPE == 8) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = static_cast<float>(static_cast<int>(static_cast<int8_t>((q >> (8 * e)) & 0xFFu))) * d;
+        codes = q ^ 0x80808080u;
     } else {
-        const int shift = j0 >= 16 ? 4 : 0;
-        float m = 0.0f;
-        if constexpr (TYPE == 3 || TYPE == 7) m = __half2float(__ushort_as_half(static_cast<unsigned short>(r.m)));
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int v = static_cast<int>((q >> (8 * e + shift)) & 0xFu);
-            if constexpr (TYPE == 6 || TYPE == 7) v |= static_cast<int>(((r.qh >> ((j0 & 15) + e)) & 1u) << 4);
-            if constexpr (TYPE == 2) w[e] = static_cast<float>(v - 8) * d;
-            if constexpr (TYPE == 6) w[e] = static_cast<float>(v - 16) * d;
-            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(v), d, m);
+        codes = (j0 >= 16 ? (q >> 4) : q) & 0x0F0F0F0Fu;
+        if constexpr (TYPE == 6 || TYPE == 7) {
+            const uint32_t hb = (r.qh >> (j0 & 15)) & 0xFu;       // high bits of weights j0 .. j0+3
+            codes |= ((hb * 0x00204081u) & 0x01010101u) << 4;     // bit e -> bit 4 of byte e
         }
+    }
+    constexpr float kBias = 8388608.0f + (TYPE == 2 ? 8.0f : TYPE == 6 ? 16.0f : TYPE == 8 ? 128.0f : 0.0f);
+    float m = 0.0f;
+    if constexpr (TYPE == 3 || TYPE == 7) m = __half2float(__ushort_as_half(static_cast<unsigned short>(r.m)));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        // 0x4B0000cc: byte 0 = code e, bytes 1-2 = 0, byte 3 = 0x4B (the exponent of 2^23)
+        const float qf = __fsub_rn(__uint_as_float(__byte_perm(codes, 0x4B000000u, 0x7440u + e)), kBias);
+        if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(qf, d, m);
+        else w[e] = __fmul_rn(qf, d);
     }
 }
 
