@@ -155,9 +155,13 @@ enum {
     TRC_CUDA_MM_ACCUMULATE = 1u, /* d += a*b instead of d = a*b */
     TRC_CUDA_MM_SIMT       = 2u, /* force the fp32 SIMT kernel (exact reference summation order);
                                     the default picks the tcgen05 3xTF32 kernel when the layout allows */
-    TRC_CUDA_MM_ONE_CTA    = 4u  /* tcgen05 kernel with one CTA per 128 x 256 tile (cta_group::1); the
+    TRC_CUDA_MM_ONE_CTA    = 4u, /* tcgen05 kernel with one CTA per 128 x 256 tile (cta_group::1); the
                                     default runs 256 x 256 tiles on CTA pairs (cta_group::2, a cluster
                                     of two SMs sharing the B tile) when M spans more than 128 rows */
+    TRC_CUDA_MM_NO_PRETAIL = 8u  /* fused trc_cuda_mul_mat_q: split B into TF32 head and tail inside
+                                    every tile instead of once before the launch (the default computes
+                                    B's tails in one pass into stream-ordered scratch when B is reused
+                                    by two or more row tiles; same results) */
 };
 
 /* ggml mul_mat: for every plane (i2, i3) of b,

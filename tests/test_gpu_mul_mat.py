@@ -263,3 +263,49 @@ def test_split_k_plane_reduction_one_plane_group(tc):
     want = np.swapaxes(oracle.repeat_back(prod, [512, 128, 2, 1]), -1, -2)
     assert tc.device_error() == 0
     assert normwise(dA.cpu().numpy(), want) <= TOL
+
+
+# ---- B's tails computed once before the launch vs inside every tile: the same values, bit for bit
+# (the fused kernel takes the precomputed tails; for the F32 kernel the flag must change nothing)
+
+@pytest.mark.parametrize("k,m,n,ta,tb,planes,one", [
+    (332, 300, 520, False, False, (1, 1), False),
+    (300, 260, 72, True, True, (1, 1), False),      # MN-major B through the 5-D map
+    (520, 384, 300, True, False, (2, 3), False),    # planes
+    (520, 384, 300, False, True, (2, 1), True),     # one CTA per tile
+    (256, 512, 100, False, True, (1, 1), False),    # MN-major B of 100 rows: per-chunk loads, padded rows
+])
+def test_pretail_bit_identical(tc, k, m, n, ta, tb, planes, one):
+    rng = np.random.default_rng(k * 7 + n)
+    p2, p3 = planes
+    a = rng.standard_normal((p3, p2, m, k) if not ta else (p3, p2, k, m)).astype(np.float32)
+    b = rng.standard_normal((p3, p2, n, k) if not tb else (p3, p2, k, n)).astype(np.float32)
+    A, B = op(dev(a), ta), op(dev(b), tb)
+    got = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
+    base = tc.mul_mat(A, B, one_cta=one, no_pretail=True).cpu().numpy()
+    assert tc.device_error() == 0
+    assert np.array_equal(got.view(np.uint32), base.view(np.uint32))
+    assert normwise(got, oracle.mul_mat(npop(a, ta), npop(b, tb))) <= TOL
+
+
+@pytest.mark.parametrize("transposed,b_mn,one,n", [(False, False, False, 264), (True, False, False, 264),
+                                                   (False, True, False, 96), (True, True, True, 100),
+                                                   (False, False, True, 72)])
+def test_pretail_bit_identical_fused(tc, transposed, b_mn, one, n):
+    """The fused kernel with B's tails precomputed vs split in every tile: K-major and MN-major B
+    (a transposed view; 100 rows takes the per-chunk loads and padded tail rows), pair and one CTA."""
+    import synth
+
+    w_ne0, w_ne1 = 1024, 520
+    blocks = dev(synth.random_blocks(synth.TYPE_Q5_0, w_ne0 * w_ne1 // 32, seed=9))
+    k = w_ne1 if transposed else w_ne0
+    xn = np.random.default_rng(3).standard_normal((n, k)).astype(np.float32)
+    x = dev(np.ascontiguousarray(xn.T)).t() if b_mn else dev(xn)  # same values, contiguous along n
+    got = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one).cpu().numpy()
+    base = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one,
+                        no_pretail=True).cpu().numpy()
+    assert tc.device_error() == 0
+    assert np.array_equal(got.view(np.uint32), base.view(np.uint32))
+    Wf = oracle.dequant(synth.TYPE_Q5_0, blocks.cpu().numpy()).reshape(w_ne1, w_ne0)
+    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, xn)
+    assert normwise(got, want) <= TOL

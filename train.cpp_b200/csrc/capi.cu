@@ -150,7 +150,7 @@ int trc_cuda_mul_mat(const trc_cuda_view* a, const trc_cuda_view* b, const trc_c
         return mul_mat_simt(*a, *b, *d, false, s);
     }
     if ((flags & TRC_CUDA_MM_SIMT) == 0) {
-        st = mul_mat_tc(*a, *b, *d, acc, (flags & TRC_CUDA_MM_ONE_CTA) == 0, s);
+        st = mul_mat_tc(*a, *b, *d, flags, s);
         if (st != TRC_CUDA_EUNSUPPORTED) return st;
     }
     return mul_mat_simt(*a, *b, *d, acc, s);
@@ -172,7 +172,7 @@ int trc_cuda_mul_mat_repeat_back(const trc_cuda_view* a, const trc_cuda_view* b,
         return mul_mat_simt(*a, *b, *d, false, s);
     }
     if ((flags & TRC_CUDA_MM_SIMT) == 0) {
-        const int st = mul_mat_tc(*a, *b, *d, acc, (flags & TRC_CUDA_MM_ONE_CTA) == 0, s);
+        const int st = mul_mat_tc(*a, *b, *d, flags, s);
         if (st != TRC_CUDA_EUNSUPPORTED) return st;
     }
     return mul_mat_simt(*a, *b, *d, acc, s);
@@ -195,8 +195,7 @@ int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_
     if (b->ne[0] != K || d->ne[0] != M || d->ne[1] != b->ne[1] || d->ne[2] != b->ne[2] || d->ne[3] != b->ne[3])
         return TRC_CUDA_EINVAL;
     if (nelements(*d) == 0) return TRC_CUDA_OK;
-    return mul_mat_q_tc(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, (flags & TRC_CUDA_MM_ACCUMULATE) != 0,
-                        (flags & TRC_CUDA_MM_ONE_CTA) == 0, static_cast<cudaStream_t>(stream));
+    return mul_mat_q_tc(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, flags, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

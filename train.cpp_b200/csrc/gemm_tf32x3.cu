@@ -100,6 +100,8 @@ struct TcParams {
     int     a_ne2, a_ne3, b_ne2, b_ne3;
     int     a_mn, b_mn;        // 1 = operand contiguous along M (resp. N)
     int     a_tma5, b_tma5;    // MN-major operand loaded by one 5-D TMA per stage (else one per 32-row chunk)
+    int     b_pretail;         // 1: B's TF32 tails were computed once before the launch and come
+                               // through tmBt (same geometry as tmB); the split warps skip B
     int     accumulate;
     int64_t total_tiles;
     // split-K: each tile's kv range is cut into `splits` parts of kv_per_split k-blocks, computed by
@@ -315,7 +317,8 @@ __device__ __forceinline__ void store_quad_head_tail(uint8_t* st, int off, const
 template <int QTYPE, int QTRANS, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmD, const __grid_constant__ TcParams p) {
+                       const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmD,
+                       const __grid_constant__ TcParams p) {
     using G = Geo<CG>;
     constexpr bool PAIR = CG == 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -340,6 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         fence_barrier_init();
         if (QTYPE == 0) prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (p.b_pretail) prefetch_tmap(&tmBt);
         if (p.tma_store) prefetch_tmap(&tmD);
     }
     if (warp == 1) {
@@ -373,7 +377,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!mbar_wait_scoped<PAIR>(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
                     const uint32_t st = smem_base + s * G::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&bars->full[s], QTYPE == 0 ? G::RAW_TX_BYTES : G::B_BYTES);
+                    mbar_arrive_expect_tx(&bars->full[s], (QTYPE == 0 ? G::RAW_TX_BYTES : G::B_BYTES) +
+                                                              (p.b_pretail ? G::B_BYTES : 0));
                     const int k0 = kb * BK;
                     if constexpr (QTYPE == 0) {
                         if (!p.a_mn) {
@@ -387,14 +392,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                             a3);
                         }
                     }
-                    if (!p.b_mn) {
-                        tma_load_4d(st + G::OFF_B_RAW, &tmB, &bars->full[s], k0, bn0, b2, b3);
-                    } else if (p.b_tma5) {
-                        tma_load_5d(st + G::OFF_B_RAW, &tmB, &bars->full[s], 0, k0, bn0 / 32, b2, b3);
-                    } else {
+                    // B raw, and with b_pretail B's precomputed tail through a map of the same geometry
+                    for (int part = 0; part < (p.b_pretail ? 2 : 1); ++part) {
+                        const CUtensorMap* mb = part == 0 ? &tmB : &tmBt;
+                        const uint32_t dstb = st + (part == 0 ? G::OFF_B_RAW : G::OFF_B_TAIL);
+                        if (!p.b_mn) {
+                            tma_load_4d(dstb, mb, &bars->full[s], k0, bn0, b2, b3);
+                        } else if (p.b_tma5) {
+                            tma_load_5d(dstb, mb, &bars->full[s], 0, k0, bn0 / 32, b2, b3);
+                        } else {
 #pragma unroll
-                        for (int c = 0; c < G::BN_CTA / 32; ++c)
-                            tma_load_4d(st + G::OFF_B_RAW + c * 2048, &tmB, &bars->full[s], bn0 + 32 * c, k0, b2, b3);
+                            for (int c = 0; c < G::BN_CTA / 32; ++c)
+                                tma_load_4d(dstb + c * 2048, mb, &bars->full[s], bn0 + 32 * c, k0, b2, b3);
+                        }
                     }
                     if (++kb == p.k_blocks) {
                         kb = 0;
@@ -543,7 +553,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     store_quad_head_tail(st, qoff[i], w);
                 }
                 if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
-                for (int i = nA + t; i < nAll; i += NT) split_one<G>(st, i, nA);
+                if (!p.b_pretail)
+                    for (int i = nA + t; i < nAll; i += NT) split_one<G>(st, i, nA);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) arrive_split(s);
@@ -574,7 +585,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     uint8_t* st = smem + s * G::STAGE_BYTES;
-                    for (int i = t; i < nAll; i += i_step) split_one<G>(st, i, nA);
+                    const int i_end = p.b_pretail ? nA : nAll;  // B's tails arrive precomputed
+                    for (int i = t; i < i_end; i += i_step) split_one<G>(st, i, nA);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) arrive_split(s);
@@ -826,6 +838,89 @@ bool encode_output(void* data, int64_t M, int64_t N, int64_t P2, int64_t P3, int
 }
 
 // Launches one instantiation; the >48 KiB dynamic shared memory opt-in is set once per device.
+// Tails of a B operand, written once before the GEMM: the same logical shape as `src`, unit stride
+// along src's unit-stride dimension (ne0 when K-major, ne1 when MN-major), rows padded to 16 bytes.
+__global__ void pretail_kernel(View4 src, float* dst, int mn, int64_t pitch_elems, int64_t n) {
+    const int64_t nf = mn ? src.ne[1] : src.ne[0];  // fast (unit-stride) dimension
+    const int64_t ns = mn ? src.ne[0] : src.ne[1];
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t f = i % nf;
+        int64_t r = i / nf;
+        const int64_t sl = r % ns;
+        r /= ns;
+        const int64_t i2 = r % src.ne[2], i3 = r / src.ne[2];
+        const int64_t i0 = mn ? sl : f, i1 = mn ? f : sl;
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(src.data + i0 * src.nb[0] + i1 * src.nb[1] + i2 * src.nb[2] +
+                                                              i3 * src.nb[3]);
+        dst[((i3 * src.ne[2] + i2) * ns + sl) * pitch_elems + f] = __uint_as_float(tf32_tail_bits(u));
+    }
+}
+
+// Computes B's tails into stream-ordered scratch (freed on the stream after the GEMM) and encodes
+// their tensor map. False (nothing allocated) when it does not pay or memory is short.
+struct Pretail {
+    void*       buf = nullptr;
+    CUtensorMap map;
+};
+
+// The tails come from the device's default memory pool; freed blocks stay in the pool (release
+// threshold raised once per device, a setting of this process only) so that steady-state calls do
+// not map memory again.
+void retain_pool_once() {
+    static std::mutex mu;
+    static uint64_t   done = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done & (uint64_t(1) << dev)) return;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t threshold = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    }
+    cudaGetLastError();
+    done |= uint64_t(1) << dev;
+}
+
+bool make_pretail(const trc_cuda_view& B, int box_rows, bool b_mn, bool b_tma5, cudaStream_t stream, Pretail& out) {
+    retain_pool_once();
+    const int64_t nf = b_mn ? B.ne[1] : B.ne[0], ns = b_mn ? B.ne[0] : B.ne[1];
+    const int64_t pitch = (nf + 3) / 4 * 4;  // floats; 16-byte rows for TMA
+    const int64_t planes = B.ne[2] * B.ne[3];
+    const size_t bytes = static_cast<size_t>(pitch * ns * planes) * sizeof(float);
+    if (cudaMallocAsync(&out.buf, bytes, stream) != cudaSuccess) {
+        cudaGetLastError();
+        out.buf = nullptr;
+        return false;
+    }
+    trc_cuda_view tv;
+    tv.data = out.buf;
+    for (int i = 0; i < 4; ++i) tv.ne[i] = B.ne[i];
+    const int64_t row = pitch * 4, plane = row * ns;
+    tv.nb[b_mn ? 1 : 0] = 4;
+    tv.nb[b_mn ? 0 : 1] = row;
+    tv.nb[2] = plane;
+    tv.nb[3] = plane * B.ne[2];
+    bool mn = false, t5 = false;
+    if (!encode_operand(tv, box_rows, mn, out.map, &t5) || mn != b_mn || t5 != b_tma5) {
+        cudaFreeAsync(out.buf, stream);
+        out.buf = nullptr;
+        return false;
+    }
+    const int64_t n = nf * ns * planes;
+    const int sms = std::max(1, sm_count_current());
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(sms) * 16));
+    pretail_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(to_view4(B), static_cast<float*>(out.buf),
+                                                                     b_mn ? 1 : 0, pitch, n);
+    note_launch();
+    if (check_launch() != TRC_CUDA_OK) {
+        cudaFreeAsync(out.buf, stream);
+        out.buf = nullptr;
+        return false;
+    }
+    return true;
+}
+
 // True when the view's elements fill a gap-free byte range starting at d.data (a permutation of a
 // contiguous tensor); `bytes` receives its size.
 bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
@@ -842,7 +937,8 @@ bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
 
 // Persistent launch: one CTA per SM (CG = 1) or one CTA pair per two SMs (CG = 2, a cluster of 2).
 template <int QTYPE, int QTRANS, int CG>
-int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmD, const TcParams& p,
+int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBt, const CUtensorMap& tmD,
+              const TcParams& p,
               cudaStream_t stream) {
     using G = Geo<CG>;
     static std::mutex mu;
@@ -887,7 +983,7 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
     }
     if constexpr (CG == 1) {
         const int64_t grid = std::min<int64_t>(p.total_units, sms);
-        kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmD, p);
+        kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmBt, tmD, p);
     } else {
         const int64_t clusters = std::min<int64_t>(p.total_units, std::max(1, pairs));
         cudaLaunchConfig_t cfg = {};
@@ -902,7 +998,7 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmD, p);
+        e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmBt, tmD, p);
         if (e != cudaSuccess) return cuda_fail(e);
     }
     note_launch();
@@ -930,10 +1026,18 @@ bool mul_mat_tc_eligible(const trc_cuda_view& a_in, const trc_cuda_view& b_in, c
 
 namespace {
 
+// The fused kernel takes B's tails precomputed (one extra pass over B) when B is reused by at least
+// two row tiles and the caller did not opt out: its split warps then only decode A. Measured on
+// B200 (Q5_0 4096 x 14336, 2048 tokens): forward +27 %, dX +16 %. The F32 kernel keeps splitting
+// B in the loop: with its split warps busy on A anyway, the tails' extra TMA traffic cost more than
+// the split work it saved (4096^3: -14 %).
+bool want_pretail(uint32_t flags, int m_tiles) { return (flags & TRC_CUDA_MM_NO_PRETAIL) == 0 && m_tiles >= 2; }
+
 template <int CG>
-int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
+int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, uint32_t flags,
                     cudaStream_t stream) {
     using G = Geo<CG>;
+    const bool accumulate = (flags & TRC_CUDA_MM_ACCUMULATE) != 0;
     // Put D's unit-stride dimension on the TMEM lanes so that epilogue stores coalesce: if D is
     // contiguous along ggml's j (ne1) rather than i (ne0), compute D^T = b^T a with roles swapped.
     const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
@@ -1000,13 +1104,14 @@ int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const 
         if (e != cudaSuccess) return cuda_fail(e);
     }
     p.total_units = p.total_tiles * p.splits;
-    return launch_tc<0, 0, CG>(tmA, tmB, tmD, p, stream);
+    return launch_tc<0, 0, CG>(tmA, tmB, tmB, tmD, p, stream);
 }
 
 template <int CG>
 int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
-                      const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, cudaStream_t stream) {
+                      const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags, cudaStream_t stream) {
     using G = Geo<CG>;
+    const bool accumulate = (flags & TRC_CUDA_MM_ACCUMULATE) != 0;
     const int64_t M = a_transposed ? w_ne0 : w_ne1;
     const int64_t K = a_transposed ? w_ne1 : w_ne0;
     const int64_t N = b.ne[1];
@@ -1054,26 +1159,34 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     p.splits = 1;
     p.kv_per_split = p.kv_blocks;
     p.total_units = p.total_tiles;
+    Pretail pt;
+    if (want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
+    const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
 
+    int st = TRC_CUDA_EUNSUPPORTED;
 #define TRC_Q_CASE(T)                                                                                 \
     case T:                                                                                           \
-        return a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmD, p, stream)                           \
-                            : launch_tc<T, 0, CG>(tmA, tmB, tmD, p, stream);
+        st = a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmBt, tmD, p, stream)                       \
+                          : launch_tc<T, 0, CG>(tmA, tmB, tmBt, tmD, p, stream);                      \
+        break;
     switch (type) {
         TRC_Q_CASE(2)
         TRC_Q_CASE(3)
         TRC_Q_CASE(6)
         TRC_Q_CASE(7)
         TRC_Q_CASE(8)
-        default: return TRC_CUDA_EUNSUPPORTED;
+        default: break;
     }
 #undef TRC_Q_CASE
+    if (pt.buf != nullptr) cudaFreeAsync(pt.buf, stream);
+    return st;
 }
 
 }  // namespace
 
-int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, bool accumulate,
-               bool allow_pair, cudaStream_t stream) {
+int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_cuda_view& d, uint32_t flags,
+               cudaStream_t stream) {
+    const bool allow_pair = (flags & TRC_CUDA_MM_ONE_CTA) == 0;
     const bool swap = d.nb[0] != 4 && d.nb[1] == 4;
     const trc_cuda_view& A = swap ? b_in : a_in;
     const trc_cuda_view& B = swap ? a_in : b_in;
@@ -1084,21 +1197,21 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     if (M <= 0 || N <= 0 || K <= 0 || M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
     if (planes2 >= (1 << 30) || planes3 >= (1 << 30)) return TRC_CUDA_EUNSUPPORTED;
     if ((K + BK - 1) / BK * red2 * red3 >= (int64_t(1) << 30)) return TRC_CUDA_EUNSUPPORTED;
-    return use_pair(M, allow_pair) ? mul_mat_tc_impl<2>(a_in, b_in, d, accumulate, stream)
-                                   : mul_mat_tc_impl<1>(a_in, b_in, d, accumulate, stream);
+    return use_pair(M, allow_pair) ? mul_mat_tc_impl<2>(a_in, b_in, d, flags, stream)
+                                   : mul_mat_tc_impl<1>(a_in, b_in, d, flags, stream);
 }
 
 int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
-                 const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, bool allow_pair,
-                 cudaStream_t stream) {
+                 const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags, cudaStream_t stream) {
+    const bool allow_pair = (flags & TRC_CUDA_MM_ONE_CTA) == 0;
     const int64_t M = a_transposed ? w_ne0 : w_ne1;
     const int64_t K = a_transposed ? w_ne1 : w_ne0;
     const int64_t N = b.ne[1];
     if (M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 30) || N <= 0) return TRC_CUDA_EUNSUPPORTED;
     if ((reinterpret_cast<uint64_t>(w_blocks) & 1u) != 0) return TRC_CUDA_EINVAL;
     return use_pair(M, allow_pair)
-               ? mul_mat_q_tc_impl<2>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, accumulate, stream)
-               : mul_mat_q_tc_impl<1>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, accumulate, stream);
+               ? mul_mat_q_tc_impl<2>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, flags, stream)
+               : mul_mat_q_tc_impl<1>(type, w_blocks, w_ne0, w_ne1, a_transposed, b, d, flags, stream);
 }
 
 }  // namespace trc

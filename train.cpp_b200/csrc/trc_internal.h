@@ -62,14 +62,12 @@ int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void*
 int mul_mat_simt(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate,
                  cudaStream_t stream);
 // Returns TRC_CUDA_EUNSUPPORTED when the layout cannot be fed by TMA (caller then uses SIMT).
-// allow_pair: the kernel may run tiles on CTA pairs (tcgen05 cta_group::2) when M spans more than one
-// 128-row tile; false keeps one CTA per tile.
-int mul_mat_tc(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate,
-               bool allow_pair, cudaStream_t stream);
+// flags: TRC_CUDA_MM_ACCUMULATE, TRC_CUDA_MM_ONE_CTA (no CTA pairs), TRC_CUDA_MM_NO_PRETAIL.
+int mul_mat_tc(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags,
+               cudaStream_t stream);
 // True when mul_mat_tc can address these views with TMA (no launch).
 bool mul_mat_tc_eligible(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d);
 int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
-                 const trc_cuda_view& b, const trc_cuda_view& d, bool accumulate, bool allow_pair,
-                 cudaStream_t stream);
+                 const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags, cudaStream_t stream);
 
 }  // namespace trc

@@ -36,7 +36,7 @@ TYPE_NAMES = {TYPE_Q4_0: "q4_0", TYPE_Q4_1: "q4_1", TYPE_Q5_0: "q5_0", TYPE_Q5_1
 BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_Q8_0: 34}
 QK = 32  # weights per block
 
-MM_ACCUMULATE, MM_SIMT, MM_ONE_CTA = 1, 2, 4
+MM_ACCUMULATE, MM_SIMT, MM_ONE_CTA, MM_NO_PRETAIL = 1, 2, 4, 8
 BIN_ADD, BIN_SUB, BIN_MUL, BIN_DIV = 0, 1, 2, 3
 
 
@@ -355,12 +355,13 @@ def mul_mat_out_ne(a: torch.Tensor, b: torch.Tensor) -> list[int]:
     return [na[1], nb_[1], nb_[2], nb_[3]]
 
 
-def _mm_flags(accumulate: bool, simt: bool, one_cta: bool) -> int:
-    return (MM_ACCUMULATE if accumulate else 0) | (MM_SIMT if simt else 0) | (MM_ONE_CTA if one_cta else 0)
+def _mm_flags(accumulate: bool, simt: bool, one_cta: bool, no_pretail: bool = False) -> int:
+    return ((MM_ACCUMULATE if accumulate else 0) | (MM_SIMT if simt else 0) | (MM_ONE_CTA if one_cta else 0) |
+            (MM_NO_PRETAIL if no_pretail else 0))
 
 
 def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False,
-            simt: bool = False, stream=None, one_cta: bool = False) -> torch.Tensor:
+            simt: bool = False, stream=None, one_cta: bool = False, no_pretail: bool = False) -> torch.Tensor:
     """ggml mul_mat: out[i, j, i2, i3] = sum_k a[k, i, i2 % a2, i3 % a3] * b[k, j, i2, i3]."""
     na, nb_ = ggml_ne(a), ggml_ne(b)
     if na[0] != nb_[0]:
@@ -369,7 +370,7 @@ def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, a
         raise TrcCudaError("mul_mat: a's planes do not broadcast onto b's (b.ne % a.ne must be 0)")
     if out is None:
         out = ggml_empty(mul_mat_out_ne(a, b), device=a.device)
-    flags = _mm_flags(accumulate, simt, one_cta)
+    flags = _mm_flags(accumulate, simt, one_cta, no_pretail)
     va, vb, vd = view_of(a), view_of(b), view_of(out)
     _check(lib().trc_cuda_mul_mat(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), flags, _stream(stream)),
            "trc_cuda_mul_mat")
@@ -377,10 +378,11 @@ def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, a
 
 
 def mul_mat_repeat_back(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, accumulate: bool = False,
-                        simt: bool = False, stream=None, one_cta: bool = False) -> torch.Tensor:
+                        simt: bool = False, stream=None, one_cta: bool = False,
+                        no_pretail: bool = False) -> torch.Tensor:
     """out (+)= repeat_back(mul_mat(a, b), shape of out): the broadcast-plane reduction of the
     composed backward's dA fused into the GEMM (out may have fewer planes than b)."""
-    flags = _mm_flags(accumulate, simt, one_cta)
+    flags = _mm_flags(accumulate, simt, one_cta, no_pretail)
     va, vb, vd = view_of(a), view_of(b), view_of(out)
     _check(lib().trc_cuda_mul_mat_repeat_back(ctypes.byref(va), ctypes.byref(vb), ctypes.byref(vd), flags,
                                               _stream(stream)), "trc_cuda_mul_mat_repeat_back")
@@ -401,7 +403,7 @@ def mul_mat_kernel(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, simt: bo
 
 def mul_mat_q(qtype: int, w_blocks: torch.Tensor, w_ne0: int, w_ne1: int, b: torch.Tensor,
               transposed: bool = False, out: torch.Tensor | None = None, accumulate: bool = False,
-              stream=None, one_cta: bool = False) -> torch.Tensor:
+              stream=None, one_cta: bool = False, no_pretail: bool = False) -> torch.Tensor:
     """Fused dequant + mul_mat with a = W (transposed=False) or a = transpose(W), W being the frozen
     quantized weight of ggml shape [w_ne0, w_ne1] held as packed blocks on the device."""
     K, M = (w_ne1, w_ne0) if transposed else (w_ne0, w_ne1)
@@ -412,7 +414,7 @@ def mul_mat_q(qtype: int, w_blocks: torch.Tensor, w_ne0: int, w_ne1: int, b: tor
         out = ggml_empty([M, nb_[1], nb_[2], nb_[3]], device=b.device)
     vb, vd = view_of(b), view_of(out)
     _check(lib().trc_cuda_mul_mat_q(qtype, w_blocks.data_ptr(), w_ne0, w_ne1, 1 if transposed else 0,
-                                    ctypes.byref(vb), ctypes.byref(vd), _mm_flags(accumulate, False, one_cta),
+                                    ctypes.byref(vb), ctypes.byref(vd), _mm_flags(accumulate, False, one_cta, no_pretail),
                                     _stream(stream)), "trc_cuda_mul_mat_q")
     return out
 
