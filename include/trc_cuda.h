@@ -75,6 +75,12 @@ int trc_cuda_last_cuda_error(void);
  * *code means a kernel gave up a bounded wait; its results are not valid. Synchronous. */
 int trc_cuda_device_error(int* code, int reset);
 
+/* Failure-detection self-test: launches one CTA that waits, with the library's bounded mbarrier
+ * wait, on a barrier nothing arrives on. After limit_ns (at most 5 s) the wait gives up, the device
+ * error word records 8 (TRC_DEVERR_SELFTEST) and the kernel returns: *completed = 0 shows that the
+ * wait ran out, and the context stays usable. No fault, trap or hang is involved. Synchronous. */
+int trc_cuda_selftest_wait_timeout(uint64_t limit_ns, int* completed);
+
 /* Number of kernels this library has launched in this process (all devices). The bench reports
  * the difference across its timed region as the count of native launches. */
 uint64_t trc_cuda_launch_count(void);

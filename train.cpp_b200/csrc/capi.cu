@@ -20,6 +20,18 @@ thread_local int      g_last_cuda_error = 0;
 
 void note_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
 
+// One CTA waits, with the library's bounded wait, on an mbarrier no thread ever arrives on: the
+// wait runs out after limit_ns, records TRC_DEVERR_SELFTEST and the kernel returns normally.
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int* out) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) out[0] = mbar_wait_limit(&bar, 0, TRC_DEVERR_SELFTEST, limit_ns) ? 1 : 0;
+}
+
 int cuda_fail(cudaError_t e) {
     g_last_cuda_error = static_cast<int>(e);
     return TRC_CUDA_ECUDA;
@@ -63,6 +75,18 @@ const char* trc_cuda_status_string(int status) {
 }
 
 int trc_cuda_last_cuda_error(void) { return g_last_cuda_error; }
+
+int trc_cuda_selftest_wait_timeout(uint64_t limit_ns, int* completed) {
+    if (completed == nullptr || limit_ns == 0 || limit_ns > 5000000000ull) return TRC_CUDA_EINVAL;
+    int* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e);
+    selftest_wait_kernel<<<1, 32>>>(limit_ns, d);
+    note_launch();
+    e = cudaMemcpy(completed, d, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return e == cudaSuccess ? TRC_CUDA_OK : cuda_fail(e);
+}
 
 int trc_cuda_device_error(int* code, int reset) {
     int v = 0;

@@ -21,6 +21,7 @@ enum : int {
     TRC_DEVERR_WAIT_ACCFREE = 5,  // MMA issuer gave up waiting for a drained accumulator
     TRC_DEVERR_WAIT_DRAIN   = 6,  // exit-time drain of in-flight copies gave up
     TRC_DEVERR_WAIT_BULK    = 7,  // dequant gave up waiting for a bulk copy
+    TRC_DEVERR_SELFTEST     = 8,  // trc_cuda_selftest_wait_timeout: the wait ran out as intended
 };
 
 constexpr uint64_t TRC_WAIT_LIMIT_NS = 2000000000ull;  // 2 s
@@ -150,6 +151,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 // Cluster-wide barrier of all threads of every CTA of the cluster.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The bounded wait with an explicit limit (the kernels use TRC_WAIT_LIMIT_NS through mbar_wait).
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int code, uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t spin = 0;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 255u) == 0 && globaltimer() - t0 > limit_ns) {
+            set_device_error(code);
+            return false;
+        }
+    }
 }
 
 // Wait that ignores errors raised elsewhere (used to drain in-flight copies before exit).

@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_rt_ipc_close": (I, [P]),
         "trc_cuda_rt_can_access_peer": (I, [I, I, ctypes.POINTER(I)]),
         "trc_cuda_unary": (I, [I, VP, VP, ctypes.c_float, P]),
+        "trc_cuda_selftest_wait_timeout": (I, [ctypes.c_uint64, ctypes.POINTER(I)]),
         "trc_cuda_sum_rows": (I, [VP, VP, I, P]),
         "trc_cuda_opt_step_adamw": (I, [P, P, P, P, I64, P, P]),
         "trc_cuda_opt_step_sgd": (I, [P, P, P, I64, P, P]),
@@ -511,6 +512,13 @@ def device_error(reset: bool = True) -> int:
     code = ctypes.c_int(0)
     _check(lib().trc_cuda_device_error(ctypes.byref(code), 1 if reset else 0), "trc_cuda_device_error")
     return code.value
+
+
+def selftest_wait_timeout(limit_ns: int) -> bool:
+    """Runs the bounded-wait self-test; True when the wait ran out (the kernel returned on its own)."""
+    done = ctypes.c_int(-1)
+    _check(lib().trc_cuda_selftest_wait_timeout(limit_ns, ctypes.byref(done)), "trc_cuda_selftest_wait_timeout")
+    return done.value == 0
 
 
 def launch_count() -> int:
