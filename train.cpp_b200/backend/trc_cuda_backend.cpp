@@ -760,3 +760,14 @@ bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* con
 extern "C" int trc_cuda_backend_register(void) { return traincpp::cuda_register_devices(); }
 
 extern "C" void* trc_cuda_backend_device(int ordinal) { return traincpp::cuda_device(ordinal); }
+
+extern "C" int64_t trc_cuda_backend_gguf_shard_plan(const char* path, int rank, int world, int64_t* indices,
+                                                    int64_t capacity) {
+    if (path == nullptr || world <= 0 || rank < 0 || rank >= world || capacity < 0) return -1;
+    traincpp::GgufFile* f = traincpp::gguf_open(path, false);
+    if (f == nullptr) return -1;
+    const std::vector<int64_t> mine = traincpp::gguf_shard_tensors(f, rank, world);
+    traincpp::gguf_close(f);
+    for (size_t i = 0; i < mine.size() && static_cast<int64_t>(i) < capacity; ++i) indices[i] = mine[i];
+    return static_cast<int64_t>(mine.size());
+}

@@ -57,4 +57,8 @@ extern "C" {
 // C entry points of the backend library, for hosts that do not link C++ (ctypes, cgo, ...).
 int trc_cuda_backend_register(void);
 void* trc_cuda_backend_device(int ordinal);
+// gguf_shard_tensors of the file at `path` (read without its data segment): writes up to `capacity`
+// tensor indices of rank `rank` and returns how many the rank has, or -1 on a bad argument / file.
+// Needs no GPU.
+int64_t trc_cuda_backend_gguf_shard_plan(const char* path, int rank, int world, int64_t* indices, int64_t capacity);
 }
