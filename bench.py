@@ -283,6 +283,31 @@ def make_blocks(seed_base: int) -> dict:
     return {t: synth.random_blocks(t, N_BLOCKS, seed=seed_base + t) for t in FORMATS}
 
 
+def mixed_traffic_ceiling(tc, torch) -> dict:
+    """What HBM delivers for the dequant's traffic mix on this GPU, measured live: a streaming kernel
+    of the library that reads 1 byte per R written (R = 5 and 6 bracket the cfg2 ratio of 5.43), with
+    the dequant's access shape (512 contiguous bytes per warp store) and none of its arithmetic."""
+    stream = torch.cuda.current_stream()
+    out = torch.empty(1 << 28, dtype=torch.float32, device="cuda")  # 1 GiB written per launch
+    res = {}
+    for ratio in (5, 6):
+        n16 = (out.numel() * 4 // 16 // ratio) // 32 * 32
+        src = torch.ones(n16 * 4, dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            tc.stream_probe(src, out, ratio)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(20):
+            tc.stream_probe(src, out, ratio)
+        e.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(e) / 20
+        res[f"read1_write{ratio}_GBps"] = round(n16 * 16 * (1 + ratio) / (ms * 1e-3) / 1e9, 1)
+        del src
+    del out
+    return res
+
+
 # ------------------------------------------------------------------ the reference arm
 def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
@@ -404,6 +429,8 @@ def run_ours(args) -> None:
                                   "GBps": round(algorithmic_bytes(t, N_BLOCKS) / (per_launch_ms[t] * 1e-3) / 1e9, 1)}
                   for t in FORMATS}
     traffic = profile_value("dequant_cfg2_ncu.txt", "dram_bytes_per_launch_mean")
+    ceiling = mixed_traffic_ceiling(tc, torch)
+    ceiling_best = max(ceiling.values())
 
     # ---- end to end through the public API with host buffers: H2D packed bytes (pinned) +
     # dequant (trc_cuda_load_quant) + D2H readback of the first block of each result
@@ -456,7 +483,9 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                          "peak_source": peaks["source"], "kernel": "dequant_kernel (one launch per step, 5 tensors)",
-                         "per_format_single_tensor_launches": per_format},
+                         "per_format_single_tensor_launches": per_format,
+                         "mixed_traffic_ceiling": ceiling,
+                         "frac_of_mixed_traffic_ceiling": round(achieved / ceiling_best, 4)},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "gpu_launches": launches,
         }
         if whole is not None:

@@ -307,6 +307,15 @@ int    trc_cuda_sum_sqr_acc(float* acc, const float* a, int64_t n, void* workspa
  * OP_CLIP_SCALE_INPLACE. */
 int trc_cuda_clip_scale_inplace(float* a, int64_t n, const float* norm, float max_norm, float eps, void* stream);
 
+/* ------------------------------------------------------------------ measurement support
+ * The dequant kernel's memory traffic without its arithmetic, to measure what HBM delivers for that
+ * mix: reads n_in16 16-byte units from `in` and writes ratio * n_in16 units to `out` (each warp:
+ * 512 contiguous bytes read, ratio x 512 contiguous bytes written, streaming stores). n_in16 must
+ * be a multiple of 32, ratio 1..8, both pointers 16-byte aligned, `out` >= ratio * n_in16 * 16
+ * bytes. bench.py reports the dequant's bandwidth as a fraction of this ceiling next to the copy
+ * peak. */
+int trc_cuda_stream_probe(const void* in, void* out, int64_t n_in16, int ratio, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,3 +38,20 @@ def test_bounded_wait_reports_and_context_survives(tc):
     got = tc.gguf_tensor_to_f32(synth.TYPE_Q4_1, torch.from_numpy(blocks).cuda()).cpu().numpy()
     assert np.array_equal(got.view(np.uint32), oracle.dequant(synth.TYPE_Q4_1, blocks).view(np.uint32))
     assert tc.device_error() == 0
+
+
+def test_stream_probe_writes_what_it_reads(tc):
+    """The measurement-support streaming kernel: each warp's 512 input bytes land R times in order
+    (word x incremented per copy), nothing past the R x input extent is touched."""
+    n16, ratio = 32 * 40, 5
+    src = torch.arange(n16 * 4, dtype=torch.int32, device="cuda")
+    out = torch.full((n16 * 4 * ratio + 64,), -7, dtype=torch.int32, device="cuda")
+    tc.stream_probe(src.view(torch.float32), out.view(torch.float32), ratio)
+    torch.cuda.synchronize()
+    s = src.view(-1, 32, 4).cpu().numpy()        # [warp, lane, 4 words]
+    o = out[: n16 * 4 * ratio].view(-1, ratio, 32, 4).cpu().numpy()
+    for j in range(ratio):
+        want = s.copy()
+        want[:, :, 0] += j + 1
+        assert np.array_equal(o[:, j], want)
+    assert bool((out[n16 * 4 * ratio:] == -7).all())

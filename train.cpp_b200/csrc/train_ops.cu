@@ -270,3 +270,51 @@ int trc_cuda_clip_scale_inplace(float* a, int64_t n, const float* norm, float ma
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ measurement support
+namespace trc {
+namespace {
+
+// The dequant kernel's traffic shape without its arithmetic: every warp reads 512 contiguous bytes
+// and writes `ratio` x 512 contiguous bytes with 16-byte streaming stores.
+template <int R>
+__global__ void stream_probe_kernel(const uint4* in, uint4* out, int64_t n_in16) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wstep = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; (w + 1) * 32 <= n_in16;
+         w += wstep) {
+        uint4 v = __ldcs(in + w * 32 + lane);
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            v.x += 1u;
+            __stcs(out + (w * 32) * R + j * 32 + lane, v);
+        }
+    }
+}
+
+}  // namespace
+}  // namespace trc
+
+extern "C" int trc_cuda_stream_probe(const void* in, void* out, int64_t n_in16, int ratio, void* stream) {
+    using namespace trc;
+    if (in == nullptr || out == nullptr || n_in16 <= 0 || (n_in16 % 32) != 0 || ratio < 1 || ratio > 8)
+        return TRC_CUDA_EINVAL;
+    if ((reinterpret_cast<uint64_t>(in) & 15u) != 0 || (reinterpret_cast<uint64_t>(out) & 15u) != 0) return TRC_CUDA_EINVAL;
+    const int sms = std::max(1, sm_count_current());
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(n_in16 / 32 * 32 / 256 + 1, int64_t(sms) * 16));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint4* pi = static_cast<const uint4*>(in);
+    uint4* po = static_cast<uint4*>(out);
+    switch (ratio) {
+        case 1: stream_probe_kernel<1><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 2: stream_probe_kernel<2><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 3: stream_probe_kernel<3><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 4: stream_probe_kernel<4><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 5: stream_probe_kernel<5><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 6: stream_probe_kernel<6><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        case 7: stream_probe_kernel<7><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+        default: stream_probe_kernel<8><<<grid, 256, 0, s>>>(pi, po, n_in16); break;
+    }
+    note_launch();
+    return check_launch();
+}
