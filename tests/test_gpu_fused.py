@@ -49,6 +49,23 @@ def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed, one_cta):
     assert tc.device_error() == 0
 
 
+@pytest.mark.parametrize("one_cta", [False, True], ids=["pair", "one_cta"])
+def test_fused_split_k_fills_the_last_wave(tc, one_cta):
+    """The fused kernel split in K: 80 pair tiles (160 single tiles) on 148 SMs run as two parts
+    each, so the split warps' look-ahead of the packed words crosses units of both parts."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q4_1, 1024, 2560, 2048
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=81)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    x = np.random.default_rng(82).standard_normal((n, w_ne0)).astype(np.float32)
+    want = oracle.mul_mat(Wf, x)
+    out = torch.full((n, w_ne1), float("nan"), device="cuda")
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), out=out, one_cta=one_cta).cpu().numpy()
+    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), one_cta=one_cta).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(got, want.reshape(got.shape)) <= 1e-5
+    assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))  # deterministic
+
+
 def test_fused_config_shape_slice(tc):
     """The fused Linear workload's weight (Q5_0, 4096 x 14336) against a token slice."""
     qtype, w_ne0, w_ne1 = synth.TYPE_Q5_0, 4096, 14336

@@ -251,6 +251,26 @@ def test_split_k_few_tiles(tc, k, m, n, one):
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))  # deterministic
 
 
+@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
+def test_split_k_fills_the_last_wave(tc, one):
+    """More tiles than the grid, just past a multiple of it (80 pair tiles, or 160 single tiles, on
+    148 SMs): the product is split in two so the last wave is not left mostly idle, and each CTA
+    runs several units of both parts."""
+    k, m, n = 1024, 2560, 2048
+    rng = np.random.default_rng(80)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    want = oracle.mul_mat(a, b)
+    A, B = dev(a), dev(b)
+    out = tc.ggml_empty(tc.mul_mat_out_ne(A, B))
+    out.fill_(float("nan"))
+    got = tc.mul_mat(A, B, out=out, one_cta=one).cpu().numpy()
+    again = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(got, want) <= TOL, normwise(got, want)
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+
+
 def test_split_k_plane_reduction_one_plane_group(tc):
     """The GQA dA product at one ne[3] plane per rank (the 8-GPU shape, reduced in size): M = 128
     after the orientation swap, few tiles, K = 2048 x 4 source planes."""

@@ -46,6 +46,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <type_traits>
 #include <mutex>
 
 #include "trc_internal.h"
@@ -497,80 +498,114 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < QPT; ++i) qoff[i] = (t + NT * i) < A_QUADS ? quad_offset<QTRANS>(t + NT * i) : 0;
             const int row_off = BM * static_cast<int>(rank);
-            // look-ahead cursor: the (tile, k-block) whose packed words are loaded next
-            int64_t ltile = tile0;
-            int lkb = 0;
-            const uint8_t* lbase[QPT];  // packed-row pointers of ltile
-            auto set_base = [&]() {
-                const int m0 = ltile < p.total_tiles ? tile_coord<CG>(p, ltile).m0 + row_off : 0;
-#pragma unroll
-                for (int i = 0; i < QPT; ++i)
-                    lbase[i] = (ltile < p.total_tiles && t + NT * i < A_QUADS)
-                                   ? quad_tile_base<QTYPE, QTRANS>(p, m0, t + NT * i) : nullptr;
-            };
-            // loads the cursor's words into w and advances the cursor; bit i of the result: quad i
-            // lies inside the matrix (else it is decoded as zeros)
-            auto load_next = [&](QuadWords (&w)[QPT]) -> uint32_t {
-                uint32_t valid = 0;
-                if (ltile < p.total_tiles) {
-#pragma unroll
-                    for (int i = 0; i < QPT; ++i) {
-                        int j0 = 0;
-                        const uint8_t* blk = quad_block<QTYPE, QTRANS>(p, lbase[i], lkb * BK, t + NT * i, j0);
-                        if (blk != nullptr) {
-                            load_quad_words<QTYPE>(blk, j0, w[i]);
-                            valid |= 1u << i;
+            // The loop is instantiated twice: with split-K (a unit is a tile's k-blocks [kv0, kv1))
+            // and without (a unit is a whole tile). These warps run at the register cap, and the
+            // unsplit loop keeps the unsplit kernel's lean schedule.
+            auto run = [&](auto split_tag) {
+                constexpr bool SPLIT = decltype(split_tag)::value;
+                // look-ahead cursor: the (unit, k-block) whose packed words are loaded next
+                int64_t lunit = tile0;
+                int lkb = 0, lkv1 = p.k_blocks;
+                const uint8_t* lbase[QPT];  // packed-row pointers of lunit's tile
+                auto set_unit = [&]() {
+                    const bool live = lunit < p.total_units;
+                    int m0 = 0;
+                    if (live) {
+                        if constexpr (SPLIT) {
+                            const UnitSpan us = unit_span(p, lunit);
+                            lkb  = us.kv0;
+                            lkv1 = us.kv1;
+                            m0   = tile_coord<CG>(p, us.tile).m0 + row_off;
+                        } else {
+                            m0 = tile_coord<CG>(p, lunit).m0 + row_off;
                         }
                     }
+#pragma unroll
+                    for (int i = 0; i < QPT; ++i)
+                        lbase[i] = (live && t + NT * i < A_QUADS) ? quad_tile_base<QTYPE, QTRANS>(p, m0, t + NT * i)
+                                                                 : nullptr;
+                };
+                // loads the cursor's words into w and advances the cursor; bit i of the result: quad
+                // i lies inside the matrix (else it is decoded as zeros)
+                auto load_next = [&](QuadWords (&w)[QPT]) -> uint32_t {
+                    uint32_t valid = 0;
+                    if (lunit < p.total_units) {
+#pragma unroll
+                        for (int i = 0; i < QPT; ++i) {
+                            int j0 = 0;
+                            const uint8_t* blk = quad_block<QTYPE, QTRANS>(p, lbase[i], lkb * BK, t + NT * i, j0);
+                            if (blk != nullptr) {
+                                load_quad_words<QTYPE>(blk, j0, w[i]);
+                                valid |= 1u << i;
+                            }
+                        }
+                    }
+                    if (++lkb == (SPLIT ? lkv1 : p.k_blocks)) {
+                        if constexpr (!SPLIT) lkb = 0;
+                        lunit += tile_step;
+                        set_unit();
+                    }
+                    return valid;
+                };
+                set_unit();
+                QuadWords w0[QPT], w1[QPT];
+                uint32_t v0 = load_next(w0);
+                uint32_t v1 = load_next(w1);
+                int64_t unit = tile0;
+                int kb = 0, kv1 = p.k_blocks;
+                if constexpr (SPLIT) {
+                    if (unit < p.total_units) {
+                        const UnitSpan us = unit_span(p, unit);
+                        kb  = us.kv0;
+                        kv1 = us.kv1;
+                    }
                 }
-                if (++lkb == p.k_blocks) {
-                    lkb = 0;
-                    ltile += tile_step;
-                    set_base();
+                uint32_t it = 0;
+                while (unit < p.total_units) {
+                    QuadWords w2[QPT];
+                    const uint32_t v2 = load_next(w2);
+                    const int s = it % G::STAGES;
+                    uint8_t* st = smem + s * G::STAGE_BYTES;
+                    if (it >= G::STAGES &&
+                        !mbar_wait_scoped<PAIR>(&bars->empty[s], ((it / G::STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY))
+                        break;
+#pragma unroll
+                    for (int i = 0; i < QPT; ++i) {
+                        if (t + NT * i >= A_QUADS) continue;
+                        float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        if ((v0 >> i) & 1u) decode_quad_words_cvt<QTYPE>(w0[i], quad_j0<QTRANS>(kb, t + NT * i), w);
+                        store_quad_head_tail(st, qoff[i], w);
+                    }
+                    if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
+                    if (!p.b_pretail)
+                        for (int i = nA + t; i < nAll; i += NT) split_one<G>(st, i, nA);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) arrive_split(s);
+#pragma unroll
+                    for (int i = 0; i < QPT; ++i) {
+                        w0[i] = w1[i];
+                        w1[i] = w2[i];
+                    }
+                    v0 = v1;
+                    v1 = v2;
+                    if (++kb == (SPLIT ? kv1 : p.k_blocks)) {
+                        unit += tile_step;
+                        if constexpr (SPLIT) {
+                            if (unit < p.total_units) {
+                                const UnitSpan us = unit_span(p, unit);
+                                kb  = us.kv0;
+                                kv1 = us.kv1;
+                            }
+                        } else {
+                            kb = 0;
+                        }
+                    }
+                    ++it;
                 }
-                return valid;
             };
-            set_base();
-            QuadWords w0[QPT], w1[QPT];
-            uint32_t v0 = load_next(w0);
-            uint32_t v1 = load_next(w1);
-            int64_t tile = tile0;
-            int kb = 0;
-            uint32_t it = 0;
-            while (tile < p.total_tiles) {
-                QuadWords w2[QPT];
-                const uint32_t v2 = load_next(w2);
-                const int s = it % G::STAGES;
-                uint8_t* st = smem + s * G::STAGE_BYTES;
-                if (it >= G::STAGES &&
-                    !mbar_wait_scoped<PAIR>(&bars->empty[s], ((it / G::STAGES) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY))
-                    break;
-#pragma unroll
-                for (int i = 0; i < QPT; ++i) {
-                    if (t + NT * i >= A_QUADS) continue;
-                    float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if ((v0 >> i) & 1u) decode_quad_words_cvt<QTYPE>(w0[i], quad_j0<QTRANS>(kb, t + NT * i), w);
-                    store_quad_head_tail(st, qoff[i], w);
-                }
-                if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;
-                if (!p.b_pretail)
-                    for (int i = nA + t; i < nAll; i += NT) split_one<G>(st, i, nA);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) arrive_split(s);
-#pragma unroll
-                for (int i = 0; i < QPT; ++i) {
-                    w0[i] = w1[i];
-                    w1[i] = w2[i];
-                }
-                v0 = v1;
-                v1 = v2;
-                if (++kb == p.k_blocks) {
-                    kb = 0;
-                    tile += tile_step;
-                }
-                ++it;
-            }
+            if (p.splits > 1) run(std::true_type{});
+            else run(std::false_type{});
         } else {
             // F32 kernel: all split warps split the A and B tiles.
             const int i_step = SPLIT_WARPS * 32;
@@ -1007,6 +1042,31 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
 
 // CTA pairs when the tile grid has more than one 128-row tile (a single row tile would leave the
 // second CTA of every pair without rows).
+// Split-K in two when it shortens the schedule: the persistent grid runs the units in waves of
+// one unit per CTA (or CTA pair), and a tile count just above a multiple of the grid leaves most of
+// the last wave idle (256 tiles on 74 pairs: 4 waves for 3.46 waves of work). Halving every tile's
+// reduction doubles the units at half the length each; it is taken when that cuts the waves' total
+// length by at least 5 %. Each part reduce-adds into a zeroed D. Two parts only and no ACCUMULATE,
+// so the result does not depend on which part lands first (0 + a + b = 0 + b + a).
+template <int CG>
+int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, cudaStream_t stream) {
+    p.splits = 1;
+    p.kv_per_split = p.kv_blocks;
+    p.total_units = p.total_tiles;
+    const int sms = sm_count_current();
+    const int64_t slots = CG == 2 ? sms / 2 : sms;
+    if (accumulate || !p.tma_store || slots <= 0 || p.kv_blocks < 2 * CHUNK_KB) return TRC_CUDA_OK;
+    const int64_t waves1 = (p.total_tiles + slots - 1) / slots;
+    const int64_t waves2 = (2 * p.total_tiles + slots - 1) / slots;
+    size_t dense_bytes = 0;
+    if (waves2 * 20 >= waves1 * 38 || !dense_extent(d, dense_bytes)) return TRC_CUDA_OK;
+    p.splits = 2;
+    p.kv_per_split = ((p.kv_blocks + 1) / 2 + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB;
+    p.total_units = p.total_tiles * 2;
+    const cudaError_t e = cudaMemsetAsync(d.data, 0, dense_bytes, stream);
+    return e == cudaSuccess ? TRC_CUDA_OK : cuda_fail(e);
+}
+
 bool use_pair(int64_t M, bool allow_pair) { return allow_pair && M > BM; }
 
 }  // namespace
@@ -1088,22 +1148,8 @@ int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const 
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, planes2, planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
 
-    // Split-K when the tiles fill at most half the SMs (or SM pairs) and the reduction is long:
-    // two CTAs per tile, each reduce-adding its partial sum into a zeroed D. Two parts only and no
-    // ACCUMULATE, so the result does not depend on which part lands first (0 + a + b = 0 + b + a).
-    p.splits = 1;
-    p.kv_per_split = p.kv_blocks;
-    const int sms = sm_count_current();
-    const int64_t capacity = CG == 2 ? sms / 2 : sms;
-    size_t dense_bytes = 0;
-    if (!accumulate && p.tma_store && sms > 0 && p.total_tiles * 2 <= capacity && p.kv_blocks >= 2 * CHUNK_KB &&
-        dense_extent(d, dense_bytes)) {
-        p.splits = 2;
-        p.kv_per_split = ((p.kv_blocks + 1) / 2 + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB;
-        const cudaError_t e = cudaMemsetAsync(d.data, 0, dense_bytes, stream);
-        if (e != cudaSuccess) return cuda_fail(e);
-    }
-    p.total_units = p.total_tiles * p.splits;
+    const int st = plan_split<CG>(d, accumulate, p, stream);
+    if (st != TRC_CUDA_OK) return st;
     return launch_tc<0, 0, CG>(tmA, tmB, tmB, tmD, p, stream);
 }
 
@@ -1156,9 +1202,8 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
-    p.splits = 1;
-    p.kv_per_split = p.kv_blocks;
-    p.total_units = p.total_tiles;
+    const int sst = plan_split<CG>(d, accumulate, p, stream);
+    if (sst != TRC_CUDA_OK) return sst;
     Pretail pt;
     if (want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
     const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
