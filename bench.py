@@ -374,18 +374,26 @@ def run_ours(args) -> None:
     step = tc.DequantBatch([(t, d_blocks[t], d_out[t]) for t in FORMATS])
 
     def per_format_launch_us(reps: int) -> dict:
-        """Per-format launch times (one tensor per launch), CUDA events on the launching stream."""
+        """Per-format launch times (one tensor per launch), CUDA events on the launching stream
+        around each launch. A 256 MB read before every launch evicts L2, so the 25-48 MB of packed
+        input come from HBM, not from the previous launch's L2 lines. (A read, not a write: a write
+        would leave L2 full of dirty lines, whose write-back the timed launch would pay for.)"""
         out = {}
+        scrub = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
         for t in FORMATS:
             for _ in range(2):
                 tc.gguf_tensor_to_f32(t, d_blocks[t], out=d_out[t])
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
+            pairs = []
             for _ in range(reps):
+                scrub.sum()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
                 tc.gguf_tensor_to_f32(t, d_blocks[t], out=d_out[t])
-            b.record(stream)
+                b.record(stream)
+                pairs.append((a, b))
             torch.cuda.synchronize()
-            out[t] = a.elapsed_time(b) / reps
+            out[t] = sum(a.elapsed_time(b) for a, b in pairs) / reps
+        del scrub
         return out
 
     # correctness guard for the measured configuration (first tensor of each format, a slice)

@@ -78,7 +78,9 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
         const int lb = warp * 32 + step * 4 + (lane >> 3);
         if (lb < nblk) {
             float w[4];
-            decode_quad<TYPE>(buf + lb * kBB, c, w);
+            QuadWords r;
+            load_quad_words<TYPE>(buf + lb * kBB, 4 * c, r);
+            decode_quad_words<TYPE>(r, 4 * c, w);
             float* o = J.out + (b0 + lb) * 32 + 4 * c;
             const float4 v = make_float4(w[0], w[1], w[2], w[3]);
             if (vec_ok) {

@@ -204,38 +204,6 @@ __device__ __forceinline__ void split_one(uint8_t* st, int i, int nA) {
 // A-tile offsets (the same in both geometries), used by the fused decode.
 constexpr int OFF_A_RAW = 0, OFF_A_TAIL = BM * BK * 4;
 
-// decode_quad_words in few instructions, with the same results: the fp16 fields go through the
-// hardware converter (cvt.f32.f16, exact for every finite half), the four integer codes are
-// gathered into the four bytes of one word (Q5: the high bits spread to bit 4 of each byte by one
-// multiply), and each byte becomes the float 2^23 + code with one byte permute; subtracting
-// 2^23 + offset (8 / 16 / 128 for Q4_0 / Q5_0 / Q8_0, whose int8 byte is stored with its sign bit
-// flipped) gives the weight's integer q exactly. q * d is then the reference's product (exact), and
-// q * d + m one fused multiply-add (the product is exact, so it rounds once, like the reference).
-template <int TYPE>
-__device__ __forceinline__ void decode_quad_words_cvt(const QuadWords& r, int j0, float (&w)[4]) {
-    const float    d = __half2float(__ushort_as_half(static_cast<unsigned short>(r.d)));
-    const uint32_t q = r.q0 | (r.q1 << 16);
-    uint32_t codes;
-    if constexpr (TYPE == 8) {
-        codes = q ^ 0x80808080u;
-    } else {
-        codes = (j0 >= 16 ? (q >> 4) : q) & 0x0F0F0F0Fu;
-        if constexpr (TYPE == 6 || TYPE == 7) {
-            const uint32_t hb = (r.qh >> (j0 & 15)) & 0xFu;       // high bits of weights j0 .. j0+3
-            codes |= ((hb * 0x00204081u) & 0x01010101u) << 4;     // bit e -> bit 4 of byte e
-        }
-    }
-    constexpr float kBias = 8388608.0f + (TYPE == 2 ? 8.0f : TYPE == 6 ? 16.0f : TYPE == 8 ? 128.0f : 0.0f);
-    float m = 0.0f;
-    if constexpr (TYPE == 3 || TYPE == 7) m = __half2float(__ushort_as_half(static_cast<unsigned short>(r.m)));
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        // 0x4B0000cc: byte 0 = code e, bytes 1-2 = 0, byte 3 = 0x4B (the exponent of 2^23)
-        const float qf = __fsub_rn(__uint_as_float(__byte_perm(codes, 0x4B000000u, 0x7440u + e)), kBias);
-        if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(qf, d, m);
-        else w[e] = __fmul_rn(qf, d);
-    }
-}
 
 // Fused dequant: a stage's A tile (128 rows x 16 K) is 512 quads of 4 consecutive weights. Quad q
 // of the stage comes from quad_block() (nullptr: out of range, written as zeros) and goes, as head
@@ -573,7 +541,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int i = 0; i < QPT; ++i) {
                         if (t + NT * i >= A_QUADS) continue;
                         float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                        if ((v0 >> i) & 1u) decode_quad_words_cvt<QTYPE>(w0[i], quad_j0<QTRANS>(kb, t + NT * i), w);
+                        if ((v0 >> i) & 1u) decode_quad_words<QTYPE>(w0[i], quad_j0<QTRANS>(kb, t + NT * i), w);
                         store_quad_head_tail(st, qoff[i], w);
                     }
                     if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) break;

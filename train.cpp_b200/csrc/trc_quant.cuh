@@ -14,38 +14,9 @@
 
 #include <cstdint>
 
-namespace trc {
+#include <cuda_fp16.h>
 
-// IEEE-754 binary16 -> binary32 from the format's definition: exact for finite values; a NaN keeps
-// its payload and comes out quiet (what the reference's arithmetic decode gives on x86).
-__host__ __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
-    const uint32_t sign = (h & 0x8000u) << 16;
-    const uint32_t e    = (h >> 10) & 0x1Fu;
-    const uint32_t m    = h & 0x3FFu;
-    uint32_t       out;
-    if (e == 0x1Fu) {
-        out = sign | 0x7F800000u | (m << 13) | (m != 0 ? 0x00400000u : 0u);
-    } else if (e != 0) {
-        out = sign | ((e + 112u) << 23) | (m << 13);
-    } else if (m == 0) {
-        out = sign;
-    } else {
-#ifdef __CUDA_ARCH__
-        const uint32_t s = static_cast<uint32_t>(__clz(m)) - 21u;  // shift that brings bit 10 up
-#else
-        uint32_t s = 0;
-        while (((m << s) & 0x400u) == 0) ++s;
-#endif
-        out = sign | ((113u - s) << 23) | (((m << s) & 0x3FFu) << 13);
-    }
-#ifdef __CUDA_ARCH__
-    return __uint_as_float(out);
-#else
-    float f;
-    __builtin_memcpy(&f, &out, 4);
-    return f;
-#endif
-}
+namespace trc {
 
 template <int TYPE>
 struct QuantTraits;
@@ -60,38 +31,6 @@ template <> struct QuantTraits<8> { static constexpr int kBytes = 34; static con
 // Little-endian reads from a block in shared or global memory that is only 2-byte aligned.
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) { return ld_u16(p) | (ld_u16(p + 2) << 16); }
-
-// Decode weights 4c .. 4c+3 (c in 0..7) of the block at `blk` (2-byte aligned).
-template <int TYPE>
-__device__ __forceinline__ void decode_quad(const uint8_t* blk, int c, float (&w)[4]) {
-    const float d = half_bits_to_float(ld_u16(blk));
-    const int   j0 = 4 * c;
-    if constexpr (TYPE == 8) {
-        const uint32_t q4 = ld_u32_a2(blk + 2 + j0);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int q = static_cast<int>(static_cast<int8_t>((q4 >> (8 * e)) & 0xFFu));
-            w[e] = static_cast<float>(q) * d;
-        }
-    } else {
-        constexpr int kQs   = QuantTraits<TYPE>::kQs;
-        const uint32_t q4    = ld_u32_a2(blk + kQs + 4 * (c & 3));  // qs[4(c&3)] .. +3
-        const int      shift = (c >> 2) * 4;                          // low nibbles for j < 16
-        uint32_t       qh    = 0;
-        if constexpr (TYPE == 6) qh = ld_u32_a2(blk + 2);
-        if constexpr (TYPE == 7) qh = ld_u32_a2(blk + 4);
-        float m = 0.0f;
-        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(ld_u16(blk + 2));
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int q = static_cast<int>((q4 >> (8 * e + shift)) & 0xFu);
-            if constexpr (TYPE == 6 || TYPE == 7) q |= static_cast<int>(((qh >> (j0 + e)) & 1u) << 4);
-            if constexpr (TYPE == 2) w[e] = static_cast<float>(q - 8) * d;
-            if constexpr (TYPE == 6) w[e] = static_cast<float>(q - 16) * d;
-            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(q), d, m);
-        }
-    }
-}
 
 // Raw 16-bit words a quad (weights j0..j0+3, j0 a multiple of 4) needs: the scale d, the minimum m
 // (_1 formats), the 16-bit word of qh holding bits j0..j0+3 (Q5 formats) and the two words holding
@@ -118,25 +57,39 @@ __device__ __forceinline__ void load_quad_words(const uint8_t* blk, int j0, Quad
     }
 }
 
+// Decode weights j0 .. j0+3 from their raw words, exactly as the reference's dequantizers do:
+// - the four codes are gathered into the four bytes of one word (Q5: the high bit of weight e is
+//   moved to bit 4 of byte e by one multiply, whose partial products fall in disjoint bits; Q8_0:
+//   the sign bit is flipped, so the byte is the int8 value + 128);
+// - one byte permute per weight builds the float 2^23 + code, and subtracting 2^23 + the format's
+//   offset gives the quant value q exactly;
+// - the scale d and minimum m go through the hardware half -> float conversion, exact for every
+//   finite or infinite half (a NaN stays a NaN);
+// - y = q * d, or fma(q, d, m) for the _1 formats: the reference's q * d + m rounds twice, but
+//   q * d is exact in fp32 (|q| < 2^8, d has 11 significant bits), so one fma is the same value.
 template <int TYPE>
 __device__ __forceinline__ void decode_quad_words(const QuadWords& r, int j0, float (&w)[4]) {
-    const float    d = half_bits_to_float(r.d);
+    const float    d = __half2float(__ushort_as_half(static_cast<unsigned short>(r.d)));
     const uint32_t q = r.q0 | (r.q1 << 16);
+    uint32_t codes;
     if constexpr (TYPE == 8) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = static_cast<float>(static_cast<int>(static_cast<int8_t>((q >> (8 * e)) & 0xFFu))) * d;
+        codes = q ^ 0x80808080u;
     } else {
-        const int shift = j0 >= 16 ? 4 : 0;
-        float m = 0.0f;
-        if constexpr (TYPE == 3 || TYPE == 7) m = half_bits_to_float(r.m);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int v = static_cast<int>((q >> (8 * e + shift)) & 0xFu);
-            if constexpr (TYPE == 6 || TYPE == 7) v |= static_cast<int>(((r.qh >> ((j0 & 15) + e)) & 1u) << 4);
-            if constexpr (TYPE == 2) w[e] = static_cast<float>(v - 8) * d;
-            if constexpr (TYPE == 6) w[e] = static_cast<float>(v - 16) * d;
-            if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(static_cast<float>(v), d, m);
+        codes = (j0 >= 16 ? (q >> 4) : q) & 0x0F0F0F0Fu;
+        if constexpr (TYPE == 6 || TYPE == 7) {
+            const uint32_t hb = (r.qh >> (j0 & 15)) & 0xFu;       // high bits of weights j0 .. j0+3
+            codes |= ((hb * 0x00204081u) & 0x01010101u) << 4;     // bit e -> bit 4 of byte e
         }
+    }
+    constexpr float kBias = 8388608.0f + (TYPE == 2 ? 8.0f : TYPE == 6 ? 16.0f : TYPE == 8 ? 128.0f : 0.0f);
+    float m = 0.0f;
+    if constexpr (TYPE == 3 || TYPE == 7) m = __half2float(__ushort_as_half(static_cast<unsigned short>(r.m)));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        // 0x4B0000cc: byte 0 = code e, bytes 1-2 = 0, byte 3 = 0x4B (the exponent of 2^23)
+        const float qf = __fsub_rn(__uint_as_float(__byte_perm(codes, 0x4B000000u, 0x7440u + e)), kBias);
+        if constexpr (TYPE == 3 || TYPE == 7) w[e] = __fmaf_rn(qf, d, m);
+        else w[e] = __fmul_rn(qf, d);
     }
 }
 
