@@ -66,6 +66,25 @@ def test_fused_split_k_fills_the_last_wave(tc, one_cta):
     assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))  # deterministic
 
 
+def test_fused_transposed_split_k_four_parts(tc):
+    """dX's kind of product, transpose(W) . dY, on 75 pair tiles: split in four parts (two into D,
+    two into a workspace added afterwards), deterministic and within the bar."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q5_0, 3840, 1024, 1280   # A = T(W): M 3840, K 1024
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=83)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    dy = (np.random.default_rng(84).standard_normal((n, w_ne1)) * 1e-2).astype(np.float32)
+    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)
+    torch.cuda.synchronize()
+    n0 = tc.launch_count()
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True)
+    assert tc.launch_count() - n0 == 3  # B's tails, the GEMM and the workspace add
+    got = got.cpu().numpy()
+    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(got, want.reshape(got.shape)) <= 1e-5
+    assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))
+
+
 def test_fused_config_shape_slice(tc):
     """The fused Linear workload's weight (Q5_0, 4096 x 14336) against a token slice."""
     qtype, w_ne0, w_ne1 = synth.TYPE_Q5_0, 4096, 14336

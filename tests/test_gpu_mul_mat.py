@@ -252,6 +252,30 @@ def test_split_k_few_tiles(tc, k, m, n, one):
 
 
 @pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
+def test_split_k_four_parts(tc, one):
+    """75 pair tiles on 74 pairs (or 150 tiles on 148 SMs): two waves unsplit, 1.5 with two parts,
+    1.25 with four. Parts 0 and 1 reduce into D, parts 2 and 3 into a workspace that one more
+    kernel adds into D, so the result does not depend on the order the parts land in."""
+    k, m, n = 1024, (3840 if not one else 1280), (1280 if not one else 3840)
+    rng = np.random.default_rng(75)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    want = oracle.mul_mat(a, b)
+    A, B = dev(a), dev(b)
+    out = tc.ggml_empty(tc.mul_mat_out_ne(A, B))
+    out.fill_(float("nan"))
+    torch.cuda.synchronize()
+    n0 = tc.launch_count()
+    got = tc.mul_mat(A, B, out=out, one_cta=one)
+    assert tc.launch_count() - n0 == 2  # the GEMM and the workspace add
+    got = got.cpu().numpy()
+    again = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
+    assert tc.device_error() == 0
+    assert normwise(got, want) <= TOL, normwise(got, want)
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+
+
+@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
 def test_split_k_fills_the_last_wave(tc, one):
     """More tiles than the grid, just past a multiple of it (80 pair tiles, or 160 single tiles, on
     148 SMs): the product is split in two so the last wave is not left mostly idle, and each CTA

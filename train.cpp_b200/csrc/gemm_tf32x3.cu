@@ -287,7 +287,7 @@ template <int QTYPE, int QTRANS, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmD,
-                       const __grid_constant__ TcParams p) {
+                       const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TcParams p) {
     using G = Geo<CG>;
     constexpr bool PAIR = CG == 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -685,7 +685,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     named_barrier_sync(team_bar, 128);
                     if (team_leader) {
                         const uint32_t src = smem_u32(stage_buf);
-                        if (p.accumulate || p.splits > 1) tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        // parts 2 and 3 of a four-part split-K product go to the workspace
+                        if (unit >= 2 * p.total_tiles)
+                            tma_reduce_add_4d(&tmW, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                        else if (p.accumulate || p.splits > 1)
+                            tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
                         else tma_store_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
                         bulk_commit_group();
                     }
@@ -941,8 +945,7 @@ bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
 // Persistent launch: one CTA per SM (CG = 1) or one CTA pair per two SMs (CG = 2, a cluster of 2).
 template <int QTYPE, int QTRANS, int CG>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBt, const CUtensorMap& tmD,
-              const TcParams& p,
-              cudaStream_t stream) {
+              const CUtensorMap& tmW, const TcParams& p, cudaStream_t stream) {
     using G = Geo<CG>;
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
@@ -986,7 +989,7 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
     }
     if constexpr (CG == 1) {
         const int64_t grid = std::min<int64_t>(p.total_units, sms);
-        kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmBt, tmD, p);
+        kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmBt, tmD, tmW, p);
     } else {
         const int64_t clusters = std::min<int64_t>(p.total_units, std::max(1, pairs));
         cudaLaunchConfig_t cfg = {};
@@ -1001,40 +1004,111 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmBt, tmD, p);
+        e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmBt, tmD, tmW, p);
         if (e != cudaSuccess) return cuda_fail(e);
     }
     note_launch();
     return check_launch();
 }
 
-// CTA pairs when the tile grid has more than one 128-row tile (a single row tile would leave the
-// second CTA of every pair without rows).
-// Split-K in two when it shortens the schedule: the persistent grid runs the units in waves of
-// one unit per CTA (or CTA pair), and a tile count just above a multiple of the grid leaves most of
-// the last wave idle (256 tiles on 74 pairs: 4 waves for 3.46 waves of work). Halving every tile's
-// reduction doubles the units at half the length each; it is taken when that cuts the waves' total
-// length by at least 5 %. Each part reduce-adds into a zeroed D. Two parts only and no ACCUMULATE,
-// so the result does not depend on which part lands first (0 + a + b = 0 + b + a).
+// D (+)= W over a dense byte range: the last step of a four-part split-K product.
+__global__ void ws_add_kernel(float* __restrict__ d, const float* __restrict__ w, int64_t n) {
+    const int64_t n4 = n / 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 a = reinterpret_cast<float4*>(d)[i];
+        const float4 b = reinterpret_cast<const float4*>(w)[i];
+        a.x = __fadd_rn(a.x, b.x);
+        a.y = __fadd_rn(a.y, b.y);
+        a.z = __fadd_rn(a.z, b.z);
+        a.w = __fadd_rn(a.w, b.w);
+        reinterpret_cast<float4*>(d)[i] = a;
+    }
+    for (int64_t i = 4 * n4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        d[i] = __fadd_rn(d[i], w[i]);
+}
+
+// Split-K plan of one product. With four parts, parts 2 and 3 reduce into `ws`, a zeroed buffer of
+// D's byte layout from the device's memory pool, through the tensor map tmW.
+struct SplitPlan {
+    void*       ws    = nullptr;
+    size_t      bytes = 0;
+    CUtensorMap tmW;
+};
+
+// Split K when it shortens the schedule. The persistent grid runs the units in waves of one unit
+// per CTA (or CTA pair), and a tile count just above a multiple of the grid leaves most of the last
+// wave idle: 256 tiles on 74 pairs take 4 waves for 3.46 waves of work. Cutting every tile's
+// reduction into s parts gives s times the units at 1/s the length each. The plan takes 2 parts,
+// then 4, each only when it shortens the waves' total length by at least 5 %.
+// The result never depends on the order in which parts land:
+// - two parts reduce-add into a D zeroed here: 0 + a + b = 0 + b + a;
+// - with four, parts 0 and 1 go to D and parts 2 and 3 to the workspace, and finish_split() adds
+//   the two afterwards: (a + b) + (c + d).
+// No ACCUMULATE, since D + a + b would depend on the order.
 template <int CG>
-int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, cudaStream_t stream) {
+int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& sp, cudaStream_t stream) {
     p.splits = 1;
     p.kv_per_split = p.kv_blocks;
     p.total_units = p.total_tiles;
     const int sms = sm_count_current();
     const int64_t slots = CG == 2 ? sms / 2 : sms;
-    if (accumulate || !p.tma_store || slots <= 0 || p.kv_blocks < 2 * CHUNK_KB) return TRC_CUDA_OK;
-    const int64_t waves1 = (p.total_tiles + slots - 1) / slots;
-    const int64_t waves2 = (2 * p.total_tiles + slots - 1) / slots;
     size_t dense_bytes = 0;
-    if (waves2 * 20 >= waves1 * 38 || !dense_extent(d, dense_bytes)) return TRC_CUDA_OK;
-    p.splits = 2;
-    p.kv_per_split = ((p.kv_blocks + 1) / 2 + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB;
-    p.total_units = p.total_tiles * 2;
+    if (accumulate || !p.tma_store || slots <= 0 || p.kv_blocks < 2 * CHUNK_KB || !dense_extent(d, dense_bytes))
+        return TRC_CUDA_OK;
+    // the schedule's length in tile-lengths, and each part's k-blocks (no part may be empty)
+    auto length = [&](int s) { return double((s * p.total_tiles + slots - 1) / slots) / s; };
+    auto per_part = [&](int s) { return ((p.kv_blocks + s - 1) / s + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB; };
+    int parts = 1;
+    double best = length(1);
+    if (length(2) <= 0.95 * best) {
+        parts = 2;
+        best = length(2);
+    }
+    if (p.kv_blocks >= 4 * CHUNK_KB && 3 * per_part(4) < p.kv_blocks && length(4) <= 0.95 * best) {
+        retain_pool_once();
+        if (cudaMallocAsync(&sp.ws, dense_bytes, stream) != cudaSuccess) {
+            cudaGetLastError();
+            sp.ws = nullptr;
+        } else if (!encode_output(sp.ws, p.M, p.N, p.planes2, p.planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, sp.tmW) ||
+                   cudaMemsetAsync(sp.ws, 0, dense_bytes, stream) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFreeAsync(sp.ws, stream);
+            sp.ws = nullptr;
+        } else {
+            sp.bytes = dense_bytes;
+            parts = 4;
+        }
+    }
+    if (parts == 1) return TRC_CUDA_OK;
+    p.splits = parts;
+    p.kv_per_split = per_part(parts);
+    p.total_units = p.total_tiles * parts;
     const cudaError_t e = cudaMemsetAsync(d.data, 0, dense_bytes, stream);
     return e == cudaSuccess ? TRC_CUDA_OK : cuda_fail(e);
 }
 
+// After the GEMM of a four-part plan: D += workspace, then the workspace goes back to the pool.
+// Runs (and frees) also when the GEMM failed, with `run_add` false.
+int finish_split(SplitPlan& sp, void* d, bool run_add, cudaStream_t stream) {
+    if (sp.ws == nullptr) return TRC_CUDA_OK;
+    int st = TRC_CUDA_OK;
+    if (run_add) {
+        const int64_t n = static_cast<int64_t>(sp.bytes / sizeof(float));
+        const int sms = std::max(1, sm_count_current());
+        const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, int64_t(sms) * 8));
+        ws_add_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(static_cast<float*>(d),
+                                                                       static_cast<const float*>(sp.ws), n);
+        note_launch();
+        st = check_launch();
+    }
+    cudaFreeAsync(sp.ws, stream);
+    sp.ws = nullptr;
+    return st;
+}
+
+// CTA pairs when the tile grid has more than one 128-row tile (a single row tile would leave the
+// second CTA of every pair without rows).
 bool use_pair(int64_t M, bool allow_pair) { return allow_pair && M > BM; }
 
 }  // namespace
@@ -1116,9 +1190,11 @@ int mul_mat_tc_impl(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const 
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, planes2, planes3, p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
 
-    const int st = plan_split<CG>(d, accumulate, p, stream);
-    if (st != TRC_CUDA_OK) return st;
-    return launch_tc<0, 0, CG>(tmA, tmB, tmB, tmD, p, stream);
+    SplitPlan sp;
+    int st = plan_split<CG>(d, accumulate, p, sp, stream);
+    if (st == TRC_CUDA_OK) st = launch_tc<0, 0, CG>(tmA, tmB, tmB, tmD, sp.ws ? sp.tmW : tmD, p, stream);
+    const int fin = finish_split(sp, d.data, st == TRC_CUDA_OK, stream);
+    return st != TRC_CUDA_OK ? st : fin;
 }
 
 template <int CG>
@@ -1170,8 +1246,13 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
-    const int sst = plan_split<CG>(d, accumulate, p, stream);
-    if (sst != TRC_CUDA_OK) return sst;
+    SplitPlan sp;
+    const int sst = plan_split<CG>(d, accumulate, p, sp, stream);
+    if (sst != TRC_CUDA_OK) {
+        finish_split(sp, d.data, false, stream);
+        return sst;
+    }
+    const CUtensorMap& tmW = sp.ws ? sp.tmW : tmD;
     Pretail pt;
     if (want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
     const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
@@ -1179,8 +1260,8 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     int st = TRC_CUDA_EUNSUPPORTED;
 #define TRC_Q_CASE(T)                                                                                 \
     case T:                                                                                           \
-        st = a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmBt, tmD, p, stream)                       \
-                          : launch_tc<T, 0, CG>(tmA, tmB, tmBt, tmD, p, stream);                      \
+        st = a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmBt, tmD, tmW, p, stream)                  \
+                          : launch_tc<T, 0, CG>(tmA, tmB, tmBt, tmD, tmW, p, stream);                 \
         break;
     switch (type) {
         TRC_Q_CASE(2)
@@ -1192,7 +1273,8 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     }
 #undef TRC_Q_CASE
     if (pt.buf != nullptr) cudaFreeAsync(pt.buf, stream);
-    return st;
+    const int fin = finish_split(sp, d.data, st == TRC_CUDA_OK, stream);
+    return st != TRC_CUDA_OK ? st : fin;
 }
 
 }  // namespace
