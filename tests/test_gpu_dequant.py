@@ -147,6 +147,23 @@ def test_load_from_pinned_host(tc):
     assert bits_equal(dst.cpu().numpy(), oracle.dequant(t, blocks))
 
 
+def test_pipelined_upload_large_tensors_share_staging(tc):
+    """Uploads of 16 MB or more cross PCIe in chunks on a second stream while the caller's stream
+    dequantizes the chunks already landed. Two large tensors through ONE staging buffer, back to
+    back: the second upload may not overwrite staging before the first dequant has read it."""
+    jobs = [(synth.TYPE_Q8_0, 4096 * 11008 // 32, 31), (synth.TYPE_Q4_1, 4096 * 11008 // 32 + 77, 32)]
+    host = [torch.from_numpy(synth.random_blocks(t, n, seed=sd)).pin_memory() for t, n, sd in jobs]
+    staging = torch.empty(max(h.numel() for h in host), dtype=torch.uint8, device="cuda")
+    outs = [torch.full((n * 32,), float("nan"), device="cuda") for _, n, _ in jobs]
+    for _ in range(2):
+        for (t, _, _), h, o in zip(jobs, host, outs):
+            tc.gguf_load_tensor(t, h, o, staging)
+    torch.cuda.synchronize()
+    assert tc.device_error() == 0
+    for (t, n, _), h, o in zip(jobs, host, outs):
+        assert bits_equal(o.cpu().numpy(), oracle.dequant(t, h.numpy(), n))
+
+
 def test_rejections(tc):
     blocks = dev(synth.random_blocks(synth.TYPE_Q4_0, 4, seed=1))
     with pytest.raises(tc.TrcCudaError):

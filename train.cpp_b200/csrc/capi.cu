@@ -3,8 +3,10 @@
 // dispatch between the tensor-core and SIMT mul_mat kernels.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "trc_internal.h"
 #include "trc_ptx.cuh"
@@ -51,6 +53,64 @@ int sm_count_current() {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
     if (dev >= 0 && dev < 64) cache[dev] = n;
     return n;
+}
+
+namespace {
+
+// The copy stream and the two events of the chunked host upload, one set per device, created on
+// first use (and kept for the process).
+struct UploadCtx {
+    std::mutex   mu;
+    cudaStream_t copy    = nullptr;
+    cudaEvent_t  start   = nullptr;  // recorded on the caller's stream: staging is free from here
+    cudaEvent_t  landed  = nullptr;  // recorded on the copy stream after each chunk
+    bool         ready   = false;
+};
+UploadCtx g_upload[64];
+
+// Packed bytes per chunk of a pipelined upload, and the smallest upload that is pipelined at all.
+constexpr size_t kUploadChunkBytes = size_t(8) << 20;
+constexpr int64_t kRunBlocks       = 256;  // chunks start on whole runs of the dequant kernel
+
+}  // namespace
+
+// trc_cuda_load_quant with the host copy cut into chunks on a second stream: chunk c + 1 crosses
+// PCIe while the caller's stream dequantizes chunk c, so the upload of a large tensor costs its
+// copy time plus one chunk's dequant instead of copy + dequant. The first copy waits for the
+// caller's earlier work (the staging buffer may still be read by a previous dequant), and every
+// dequant waits for its own chunk.
+int load_quant_pipelined(int type, const uint8_t* host, int64_t n_blocks, uint8_t* staging, float* out,
+                         cudaStream_t s) {
+    const size_t bb = trc_cuda_block_bytes(type);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= 64) return TRC_CUDA_EUNSUPPORTED;
+    UploadCtx& u = g_upload[dev];
+    std::lock_guard<std::mutex> lock(u.mu);
+    if (!u.ready) {
+        if ((e = cudaStreamCreateWithFlags(&u.copy, cudaStreamNonBlocking)) != cudaSuccess) return cuda_fail(e);
+        if ((e = cudaEventCreateWithFlags(&u.start, cudaEventDisableTiming)) != cudaSuccess) return cuda_fail(e);
+        if ((e = cudaEventCreateWithFlags(&u.landed, cudaEventDisableTiming)) != cudaSuccess) return cuda_fail(e);
+        u.ready = true;
+    }
+    const int64_t total_bytes = n_blocks * static_cast<int64_t>(bb);
+    const int64_t n_chunks    = (total_bytes + static_cast<int64_t>(kUploadChunkBytes) - 1) / kUploadChunkBytes;
+    int64_t chunk = (n_blocks + n_chunks - 1) / n_chunks;
+    chunk = (chunk + kRunBlocks - 1) / kRunBlocks * kRunBlocks;
+    if ((e = cudaEventRecord(u.start, s)) != cudaSuccess) return cuda_fail(e);
+    if ((e = cudaStreamWaitEvent(u.copy, u.start, 0)) != cudaSuccess) return cuda_fail(e);
+    for (int64_t b0 = 0; b0 < n_blocks; b0 += chunk) {
+        const int64_t nb = std::min(chunk, n_blocks - b0);
+        const size_t off = static_cast<size_t>(b0) * bb;
+        e = cudaMemcpyAsync(staging + off, host + off, static_cast<size_t>(nb) * bb, cudaMemcpyHostToDevice, u.copy);
+        if (e != cudaSuccess) return cuda_fail(e);
+        if ((e = cudaEventRecord(u.landed, u.copy)) != cudaSuccess) return cuda_fail(e);
+        if ((e = cudaStreamWaitEvent(s, u.landed, 0)) != cudaSuccess) return cuda_fail(e);
+        const int st = trc_cuda_dequant(type, staging + off, nb, out + b0 * 32, s);
+        if (st != TRC_CUDA_OK) return st;
+    }
+    return TRC_CUDA_OK;
 }
 
 }  // namespace trc
@@ -145,6 +205,9 @@ int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, voi
     if (host_blocks == nullptr || staging == nullptr || out == nullptr) return TRC_CUDA_EINVAL;
     if ((reinterpret_cast<uint64_t>(staging) & 15u) != 0) return TRC_CUDA_EINVAL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (static_cast<size_t>(n_blocks) * bb >= 2 * kUploadChunkBytes)
+        return load_quant_pipelined(type, static_cast<const uint8_t*>(host_blocks), n_blocks,
+                                    static_cast<uint8_t*>(staging), out, s);
     const cudaError_t e =
         cudaMemcpyAsync(staging, host_blocks, static_cast<size_t>(n_blocks) * bb, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return cuda_fail(e);
