@@ -378,23 +378,22 @@ def run_ours(args) -> None:
         around each launch. A 256 MB read before every launch evicts L2, so the 25-48 MB of packed
         input come from HBM, not from the previous launch's L2 lines. (A read, not a write: a write
         would leave L2 full of dirty lines, whose write-back the timed launch would pay for.)"""
-        out = {}
         scrub = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
         for t in FORMATS:
             for _ in range(2):
                 tc.gguf_tensor_to_f32(t, d_blocks[t], out=d_out[t])
-            pairs = []
-            for _ in range(reps):
+        pairs = {t: [] for t in FORMATS}
+        for _ in range(reps):  # formats interleaved, so no format is timed only first or last
+            for t in FORMATS:
                 scrub.sum()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
                 tc.gguf_tensor_to_f32(t, d_blocks[t], out=d_out[t])
                 b.record(stream)
-                pairs.append((a, b))
-            torch.cuda.synchronize()
-            out[t] = sum(a.elapsed_time(b) for a, b in pairs) / reps
+                pairs[t].append((a, b))
+        torch.cuda.synchronize()
         del scrub
-        return out
+        return {t: sum(a.elapsed_time(b) for a, b in pairs[t]) / reps for t in FORMATS}
 
     # correctness guard for the measured configuration (first tensor of each format, a slice)
     step()
