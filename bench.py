@@ -464,6 +464,26 @@ def run_ours(args) -> None:
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": readback.numel() * 4,
            "ms_per_step": round(e2e_ms, 4), "api": "trc_cuda_load_quant (host packed -> device F32)"}
 
+    # The bound of e2e: the same packed bytes as plain pinned host -> device copies, nothing else.
+    def h2d_only():
+        for t in FORMATS:
+            staging[t][: pinned[t].numel()].copy_(pinned[t], non_blocking=True)
+
+    h2d_only()
+    torch.cuda.synchronize()
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for _ in range(args.steps):
+        h2d_only()
+    c1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    h2d_ms = max_over_ranks(c0.elapsed_time(c1)) / args.steps
+    e2e["h2d_GBps"] = round(h2d / (e2e_ms * 1e-3) / 1e9, 2)
+    e2e["h2d_copy_only_GBps"] = round(h2d / (h2d_ms * 1e-3) / 1e9, 2)
+    e2e["frac_of_h2d_copy"] = round(h2d_ms / e2e_ms, 4)
+
     # ---- secondary: the whole-model dequant (cfg3) and the mul_mat workloads (tensor cores)
     secondary = whole = None
     if not args.no_secondary:
