@@ -490,7 +490,12 @@ def run_ours(args) -> None:
         whole = run_whole_model(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
         if world > 1:
             whole["all_gather"] = run_gather(tc, torch, rank, world, barrier, max_over_ranks, args)
-        secondary = run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
+        # the GEMM workloads' own clock record: dense tensor-core work can run under the power cap
+        with ClockSampler(local) as gclk:
+            gclk.mark_start()
+            secondary = run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args)
+            gclk.mark_stop()
+        secondary["clocks"] = gclk.summary()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
