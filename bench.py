@@ -214,9 +214,10 @@ def write_cfg2_gguf(path: Path, blocks: dict, chunks: int = 1) -> list[tuple[str
     return names
 
 
-def reference_dequant_rate(blocks: dict, threads: int, reps: int, kind_hint: str = "reference") -> dict:
+def reference_dequant_rate(blocks: dict, threads: int, reps: int, warmup: int = 1) -> dict:
     """Times train.cpp's gguf_tensor_to_f32 (host dequant) over the cfg2 workload; one thread per
-    chunk, `threads` at a time. Falls back to the oracle restatement if oracle/_ref is absent."""
+    chunk, `threads` at a time; `warmup` untimed passes first. Falls back to the oracle
+    restatement if oracle/_ref is absent."""
     import oracle
 
     chunks = -(-threads // len(FORMATS)) if threads > len(FORMATS) else 1  # >= one GGUF tensor per thread
@@ -267,7 +268,8 @@ def reference_dequant_rate(blocks: dict, threads: int, reps: int, kind_hint: str
                 th.join()
             return time.perf_counter() - t0
 
-        run_once()  # warm (page in)
+        for _ in range(max(1, warmup)):  # untimed (the first also pages the file in)
+            run_once()
         times = [run_once() for _ in range(reps)]
         if use_ref:
             oracle.ref_lib().ref_gguf_close(handle)
@@ -318,7 +320,7 @@ def run_reference_arm(args) -> None:
     # each step is one pass over the workload; warmup passes run untimed
     import oracle  # noqa: F401
 
-    res = reference_dequant_rate(blocks, threads, reps=max(1, args.steps))
+    res = reference_dequant_rate(blocks, threads, reps=max(1, args.steps), warmup=args.warmup)
     line = {
         "metric": METRIC, "impl": "reference", "value": round(res["value"], 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -326,7 +328,7 @@ def run_reference_arm(args) -> None:
         "vs_baseline": None, "dtype": "u8->f32", "data": "synthetic (seeded PCG64 blocks per the configs)",
         "config": {"workload": "dequant sweep: Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, one 4096x11008 tensor each",
                    "step_bytes": STEP_BYTES, "device": "host CPU"},
-        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {"value": round(res["value"], 3), **{k: res[k] for k in ("unit", "cores", "kind", "sample")}},
         "e2e": {"value": round(res["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
