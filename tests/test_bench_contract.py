@@ -11,6 +11,8 @@ import subprocess
 import sys
 from pathlib import Path
 
+import pytest
+
 ROOT = Path(__file__).resolve().parents[1]
 
 
@@ -66,3 +68,30 @@ def test_reference_arm_under_torchrun_prints_once():
     lines = json_lines(r.stdout)
     assert len(lines) == 1  # rank 0 only
     check_line(lines[0], n_gpus=2, steps=1, warmup=3)
+
+
+@pytest.mark.gpu
+def test_our_arm_line():
+    """Our arm on one GPU (headline only): the base contract's keys, the roofline and cpu_baseline
+    objects, an e2e with the host bytes counted, the clock record, and one library launch per
+    timed step."""
+    r = run([sys.executable, "bench.py", "--no-secondary", "--steps", "3", "--warmup", "3"], timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = json_lines(r.stdout)
+    assert len(lines) == 1
+    d = lines[0]
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "roofline", "cpu_baseline", "e2e", "clocks",
+              "gpu_launches"):
+        assert k in d, k
+    assert d["n_gpus"] == 1 and d["steps"] == 3 and d["warmup"] == 3 and d["value"] > 0
+    rf = d["roofline"]
+    assert rf["bound"] == "hbm" and rf["unit"] == "GB/s" and rf["peak"] > 0
+    assert abs(rf["frac"] - rf["achieved"] / rf["peak"]) < 1e-3
+    cb = d["cpu_baseline"]
+    assert cb["value"] > 0 and cb["cores"] >= 1 and cb["kind"] in ("reference", "port")
+    e2e = d["e2e"]
+    assert e2e["value"] > 0 and e2e["h2d_bytes_per_step"] > 0 and e2e["d2h_bytes_per_step"] > 0
+    assert e2e["value"] != d["value"]
+    assert d["clocks"]["sm_max_mhz"]
+    assert d["gpu_launches"] == d["steps"]  # one batched dequant launch per step
