@@ -320,6 +320,11 @@ int trc_cuda_clip_scale_inplace(float* a, int64_t n, const float* norm, float ma
  * peak. */
 int trc_cuda_stream_probe(const void* in, void* out, int64_t n_in16, int ratio, void* stream);
 
+/* trc_cuda_stream_probe with the dequant kernel's store path: the copies are staged in shared memory
+ * and written by bulk copies (cp.async.bulk), 3 CTAs per SM. Same output layout; n_in16 must be a
+ * multiple of 256. */
+int trc_cuda_stream_probe_bulk(const void* in, void* out, int64_t n_in16, int ratio, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

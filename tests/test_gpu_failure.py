@@ -40,13 +40,15 @@ def test_bounded_wait_reports_and_context_survives(tc):
     assert tc.device_error() == 0
 
 
-def test_stream_probe_writes_what_it_reads(tc):
-    """The measurement-support streaming kernel: each warp's 512 input bytes land R times in order
-    (word x incremented per copy), nothing past the R x input extent is touched."""
-    n16, ratio = 32 * 40, 5
+@pytest.mark.parametrize("bulk", [False, True], ids=["st_global", "bulk_store"])
+def test_stream_probe_writes_what_it_reads(tc, bulk):
+    """The measurement-support streaming kernels: each warp's 512 input bytes land R times in order
+    (word x incremented per copy), nothing past the R x input extent is touched; the bulk-store
+    variant writes the same layout."""
+    n16, ratio = 256 * 40, 5
     src = torch.arange(n16 * 4, dtype=torch.int32, device="cuda")
     out = torch.full((n16 * 4 * ratio + 64,), -7, dtype=torch.int32, device="cuda")
-    tc.stream_probe(src.view(torch.float32), out.view(torch.float32), ratio)
+    tc.stream_probe(src.view(torch.float32), out.view(torch.float32), ratio, bulk=bulk)
     torch.cuda.synchronize()
     s = src.view(-1, 32, 4).cpu().numpy()        # [warp, lane, 4 words]
     o = out[: n16 * 4 * ratio].view(-1, ratio, 32, 4).cpu().numpy()

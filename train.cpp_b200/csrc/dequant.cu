@@ -4,19 +4,22 @@
 // 320-417 of train.cpp). HBM-bound: per 32 weights it reads 18..34 packed bytes and writes 128.
 //
 // Layout and schedule
-//   * A "run" is 256 consecutive blocks of one tensor (4.5-8.5 KiB packed, 32 KiB of F32 out).
+//   * A "run" is 128 consecutive blocks of one tensor (2.25-4.25 KiB packed, 16 KiB of F32 out).
 //   * Persistent CTAs of 256 threads walk the runs of all jobs of a launch (one launch can cover a
 //     whole model shard). Each CTA double-buffers its runs in shared memory: while it decodes run r
 //     it already has the bulk copy (cp.async.bulk, TMA engine) of its next run in flight.
-//   * Decode: warp w owns blocks 32w..32w+31 of the run. In each of 8 steps a lane decodes 4
-//     weights (a quad) of one of 4 blocks and the warp stores 4 x 128 B = 512 contiguous bytes
-//     with 16-byte streaming (.cs) vector stores, so every store instruction is fully coalesced.
-//   * Measured on B200 (4096 x 11008 tensors of all five formats): 4.98 TB/s of algorithmic
-//     traffic when the five tensors go through one launch (trc_cuda_dequant_many), 76 % of the
-//     6.55 TB/s copy peak; write-only fill reaches 7.45 TB/s, copy 6.46 TB/s. A shared-memory +
-//     bulk-store output path and smaller runs were measured and were not faster.
+//   * Decode: warp w owns blocks 16w..16w+15 of the run. In each of 4 steps a lane decodes 4
+//     weights (a quad) of one of 4 blocks, and the warp writes 4 x 128 B = 512 contiguous bytes.
+//   * Output: the decoded run goes to one of two F32 buffers in shared memory, and one bulk copy
+//     (cp.async.bulk global <- shared) writes it to HBM while the CTA decodes the next run. On
+//     B200 this writes the dequant's 1:5.4 read:write mix at 5.98 TB/s of algorithmic traffic
+//     (five 4096 x 11008 tensors of all formats in one launch), 91 % of the 6.55 TB/s copy peak,
+//     against 5.55 TB/s with 16-byte streaming st.global stores from registers.
+//   * The peer variant (all-gather fused into the dequant) keeps the register stores: it writes
+//     every quad to the local buffer and to each peer's buffer over NVLink.
 //   * A run whose packed bytes are not 16-byte aligned / sized (a tensor's ragged tail, or an
-//     unaligned tensor) is staged by ordinary loads instead of the bulk copy.
+//     unaligned tensor) is staged by ordinary loads instead of the bulk copy, and a run whose output
+//     is not 16-byte aligned is written from shared memory with ordinary stores.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -32,11 +35,15 @@ namespace trc {
 namespace {
 
 constexpr int kThreads   = 256;
-constexpr int kRun       = 256;       // blocks per run
+constexpr int kRun       = 128;       // blocks per run
 constexpr int kMaxBlk    = 34;        // largest block (Q8_0)
 constexpr int kMaxJobs   = 256;       // jobs per launch (kernel parameter of ~10 KiB)
 constexpr int kBufBytes  = kRun * kMaxBlk;
 constexpr int kMaxPeers  = 8;         // copies of each output written to other GPUs' buffers
+// CTAs per SM of the bulk-store kernel (5 would fit). Measured on B200, five-tensor step: 3 per SM
+// 5.98 TB/s, 4 per SM 5.77, 5 per SM 5.57; a plain streaming probe with the same bulk stores
+// peaked at 3 per SM as well.
+constexpr int kBulkCtasPerSm = 3;
 
 struct DqJob {
     const uint8_t* src;
@@ -66,6 +73,28 @@ __device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
 // PEERS: every quad is also stored at the same offset of each peer GPU's buffer (peer-mapped
 // addresses, plain stores over NVLink), which fuses the all-gather of a sharded tensor into its
 // dequantization.
+// Decodes a staged run into the CTA's output buffer in shared memory (F32, the run's layout), from
+// where one bulk copy writes it to HBM. Warp w owns blocks (kRun/8)w .. (kRun/8)(w+1)-1; in each step a
+// lane decodes 4 weights of one of 4 blocks, so a warp writes 512 contiguous bytes (no bank
+// conflicts).
+template <int TYPE>
+__device__ __forceinline__ void decode_run_smem(const uint8_t* buf, float* obuf, int nblk) {
+    constexpr int kBB = QuantTraits<TYPE>::kBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = lane & 7;
+#pragma unroll 2
+    for (int step = 0; step < kRun / 32; ++step) {
+        const int lb = warp * (kRun / 8) + step * 4 + (lane >> 3);
+        if (lb < nblk) {
+            float w[4];
+            QuadWords r;
+            load_quad_words<TYPE>(buf + lb * kBB, 4 * c, r);
+            decode_quad_words<TYPE>(r, 4 * c, w);
+            *reinterpret_cast<float4*>(obuf + lb * 32 + 4 * c) = make_float4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
 template <int TYPE, bool PEERS>
 __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, int64_t b0, int nblk,
                                            const DqBatch& batch) {
@@ -74,8 +103,8 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
     const int c = lane & 7;
     const bool vec_ok = (reinterpret_cast<uint64_t>(J.out) & 15u) == 0;
 #pragma unroll 2
-    for (int step = 0; step < 8; ++step) {
-        const int lb = warp * 32 + step * 4 + (lane >> 3);
+    for (int step = 0; step < kRun / 32; ++step) {
+        const int lb = warp * (kRun / 8) + step * 4 + (lane >> 3);
         if (lb < nblk) {
             float w[4];
             QuadWords r;
@@ -108,6 +137,8 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
 template <bool PEERS>
 __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DqBatch batch) {
     __shared__ __align__(128) uint8_t buf[2][kBufBytes];
+    // decoded runs, written to HBM by bulk copies (two, so one can drain while the next fills)
+    __shared__ __align__(128) float obuf[PEERS ? 1 : 2][PEERS ? 4 : kRun * 32];
     __shared__ __align__(8) uint64_t bar[2];
 
     if (threadIdx.x == 0) {
@@ -179,15 +210,49 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
             __syncthreads();
         }
 
-        switch (J.type) {
-            case 2: decode_run<2, PEERS>(buf[slot], J, b0, nblk, batch); break;
-            case 3: decode_run<3, PEERS>(buf[slot], J, b0, nblk, batch); break;
-            case 6: decode_run<6, PEERS>(buf[slot], J, b0, nblk, batch); break;
-            case 7: decode_run<7, PEERS>(buf[slot], J, b0, nblk, batch); break;
-            case 8: decode_run<8, PEERS>(buf[slot], J, b0, nblk, batch); break;
-            default: break;
+        if constexpr (PEERS) {
+            switch (J.type) {
+                case 2: decode_run<2, true>(buf[slot], J, b0, nblk, batch); break;
+                case 3: decode_run<3, true>(buf[slot], J, b0, nblk, batch); break;
+                case 6: decode_run<6, true>(buf[slot], J, b0, nblk, batch); break;
+                case 7: decode_run<7, true>(buf[slot], J, b0, nblk, batch); break;
+                case 8: decode_run<8, true>(buf[slot], J, b0, nblk, batch); break;
+                default: break;
+            }
+        } else {
+            // At this point at most one bulk store is still reading shared memory: the previous
+            // run's, from the other buffer (each run ends by waiting for all older ones).
+            float* ob = obuf[slot];
+            switch (J.type) {
+                case 2: decode_run_smem<2>(buf[slot], ob, nblk); break;
+                case 3: decode_run_smem<3>(buf[slot], ob, nblk); break;
+                case 6: decode_run_smem<6>(buf[slot], ob, nblk); break;
+                case 7: decode_run_smem<7>(buf[slot], ob, nblk); break;
+                case 8: decode_run_smem<8>(buf[slot], ob, nblk); break;
+                default: break;
+            }
+            float* dst = J.out + b0 * 32;
+            if ((reinterpret_cast<uint64_t>(dst) & 15u) == 0) {
+                fence_proxy_async_smem();  // the generic-proxy writes become visible to the bulk copy
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    bulk_store(dst, smem_u32(ob), static_cast<uint32_t>(nblk) * 128u);
+                    bulk_commit_group();
+                    bulk_wait_group_read<1>();  // the previous run's copy has read the other buffer
+                }
+            } else {
+                __syncthreads();  // an unaligned output: plain stores
+                for (int i = threadIdx.x; i < nblk * 32; i += kThreads) dst[i] = ob[i];
+                // no copy was issued: let every earlier one finish reading, so that none is
+                // pending when the next run fills a buffer
+                if (threadIdx.x == 0) bulk_wait_group_read<0>();
+            }
         }
         __syncthreads();
+    }
+    // Every bulk store has completed before the grid counts as complete.
+    if constexpr (!PEERS) {
+        if (threadIdx.x == 0) bulk_wait_group_all();
     }
     // Never leave the CTA with a bulk copy still writing into its shared memory.
     for (int s = 0; s < 2; ++s) {
@@ -272,7 +337,8 @@ int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void*
         }
         if (batch.n_jobs == 0) continue;
         batch.total_runs = runs;
-        const int per_sm = n_peers > 0 ? resident_ctas<true>() : resident_ctas<false>();
+        int per_sm = n_peers > 0 ? resident_ctas<true>() : resident_ctas<false>();
+        if (n_peers == 0) per_sm = std::min(per_sm, kBulkCtasPerSm);
         if (per_sm <= 0) return TRC_CUDA_ECUDA;
         const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * per_sm);
         if (n_peers > 0) dequant_kernel<true><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);

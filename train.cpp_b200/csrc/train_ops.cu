@@ -16,6 +16,7 @@
 #include <cstdint>
 
 #include "trc_internal.h"
+#include "trc_ptx.cuh"
 
 namespace trc {
 
@@ -292,8 +293,76 @@ __global__ void stream_probe_kernel(const uint4* in, uint4* out, int64_t n_in16)
     }
 }
 
+// The same traffic and output layout with the writes staged in shared memory and written by bulk
+// copies, the dequant kernel's store path: each CTA reads 256 x 16 bytes, places its R copies in one
+// of two shared buffers and stores the buffer with one cp.async.bulk while it fills the other.
+template <int R>
+__global__ void __launch_bounds__(256) stream_probe_bulk_kernel(const uint4* in, uint4* out, int64_t n_in16) {
+    extern __shared__ __align__(128) uint4 sbuf[];  // 2 x R x 256
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int64_t chunks = n_in16 / 256;
+    int b = 0;
+    for (int64_t c = blockIdx.x; c < chunks; c += gridDim.x, b ^= 1) {
+        uint4* buf = sbuf + b * R * 256;
+        uint4 v = __ldcs(in + c * 256 + threadIdx.x);
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            v.x += 1u;
+            buf[wp * 32 * R + j * 32 + lane] = v;
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store(out + c * 256 * R, smem_u32(buf), static_cast<uint32_t>(R * 256 * 16));
+            bulk_commit_group();
+            bulk_wait_group_read<1>();  // the other buffer's copy has been read: it may be refilled
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) bulk_wait_group_all();
+}
+
+template <int R>
+int launch_probe_bulk(const uint4* in, uint4* out, int64_t n_in16, cudaStream_t s) {
+    const int smem = 2 * R * 256 * 16;
+    static bool configured[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TRC_CUDA_ECUDA;
+    if (!configured[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(stream_probe_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(e);
+        configured[dev] = true;
+    }
+    const int sms = std::max(1, sm_count_current());
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(n_in16 / 256, int64_t(sms) * 3));
+    stream_probe_bulk_kernel<R><<<grid, 256, smem, s>>>(in, out, n_in16);
+    note_launch();
+    return check_launch();
+}
+
 }  // namespace
 }  // namespace trc
+
+extern "C" int trc_cuda_stream_probe_bulk(const void* in, void* out, int64_t n_in16, int ratio, void* stream) {
+    using namespace trc;
+    if (in == nullptr || out == nullptr || n_in16 <= 0 || (n_in16 % 256) != 0 || ratio < 1 || ratio > 8)
+        return TRC_CUDA_EINVAL;
+    if ((reinterpret_cast<uint64_t>(in) & 15u) != 0 || (reinterpret_cast<uint64_t>(out) & 15u) != 0) return TRC_CUDA_EINVAL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint4* pi = static_cast<const uint4*>(in);
+    uint4* po = static_cast<uint4*>(out);
+    switch (ratio) {
+        case 1: return launch_probe_bulk<1>(pi, po, n_in16, s);
+        case 2: return launch_probe_bulk<2>(pi, po, n_in16, s);
+        case 3: return launch_probe_bulk<3>(pi, po, n_in16, s);
+        case 4: return launch_probe_bulk<4>(pi, po, n_in16, s);
+        case 5: return launch_probe_bulk<5>(pi, po, n_in16, s);
+        case 6: return launch_probe_bulk<6>(pi, po, n_in16, s);
+        case 7: return launch_probe_bulk<7>(pi, po, n_in16, s);
+        default: return launch_probe_bulk<8>(pi, po, n_in16, s);
+    }
+}
 
 extern "C" int trc_cuda_stream_probe(const void* in, void* out, int64_t n_in16, int ratio, void* stream) {
     using namespace trc;

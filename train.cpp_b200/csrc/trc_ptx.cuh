@@ -223,6 +223,13 @@ __device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t sme
         : "memory");
 }
 
+// Bulk copy (TMA engine) of `bytes` (a multiple of 16) from shared memory to 16-byte aligned global
+// memory; its completion is tracked by bulk groups (bulk_commit_group / bulk_wait_group_*).
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_src), "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N committed bulk groups still read their shared-memory source.

@@ -100,6 +100,7 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_unary": (I, [I, VP, VP, ctypes.c_float, P]),
         "trc_cuda_selftest_wait_timeout": (I, [ctypes.c_uint64, ctypes.POINTER(I)]),
         "trc_cuda_stream_probe": (I, [P, P, I64, I, P]),
+        "trc_cuda_stream_probe_bulk": (I, [P, P, I64, I, P]),
         "trc_cuda_sum_rows": (I, [VP, VP, I, P]),
         "trc_cuda_opt_step_adamw": (I, [P, P, P, P, I64, P, P]),
         "trc_cuda_opt_step_sgd": (I, [P, P, P, I64, P, P]),
@@ -515,13 +516,14 @@ def device_error(reset: bool = True) -> int:
     return code.value
 
 
-def stream_probe(src: torch.Tensor, dst: torch.Tensor, ratio: int, stream=None) -> None:
-    """Streams src (read once) into ratio x its bytes of dst: the dequant's traffic mix, no math."""
-    n16 = (src.numel() * src.element_size()) // 16 // 32 * 32
+def stream_probe(src: torch.Tensor, dst: torch.Tensor, ratio: int, stream=None, bulk: bool = False) -> None:
+    """Streams src (read once) into ratio x its bytes of dst: the dequant's traffic mix, no math.
+    bulk=True writes through shared memory and bulk copies, the dequant kernel's store path."""
+    n16 = (src.numel() * src.element_size()) // 16 // (256 if bulk else 32) * (256 if bulk else 32)
     if dst.numel() * dst.element_size() < ratio * n16 * 16:
         raise TrcCudaError("stream_probe: destination too small")
-    _check(lib().trc_cuda_stream_probe(src.data_ptr(), dst.data_ptr(), n16, ratio, _stream(stream)),
-           "trc_cuda_stream_probe")
+    fn = lib().trc_cuda_stream_probe_bulk if bulk else lib().trc_cuda_stream_probe
+    _check(fn(src.data_ptr(), dst.data_ptr(), n16, ratio, _stream(stream)), "trc_cuda_stream_probe")
 
 
 def selftest_wait_timeout(limit_ns: int) -> bool:
