@@ -93,6 +93,27 @@ def test_unaligned_buffers(tc, qtype):
     assert bits_equal(out.cpu().numpy(), oracle.dequant(qtype, blocks))
 
 
+def test_batch_alternating_output_alignment(tc):
+    """Twenty jobs of 64 runs each (128 blocks per run) in one launch, outputs alternately 16-byte
+    aligned (written by bulk copies from shared memory) and 4 bytes off (plain stores): every CTA
+    handles several runs, so a plain-store run sits between bulk-copy runs that reuse the CTA's
+    two output buffers."""
+    jobs, want = [], []
+    for j in range(20):
+        t = TYPES[j % len(TYPES)]
+        n = 64 * 128 - (j % 3) * 37                       # ragged last run in some jobs
+        blocks = synth.random_blocks(t, n, seed=500 + j)
+        base = torch.full((n * 32 + 4,), float("nan"), device="cuda")
+        out = base[1:1 + n * 32] if j % 2 else base[: n * 32]
+        jobs.append((t, dev(blocks), out))
+        want.append(oracle.dequant(t, blocks))
+    tc.dequantize_many(jobs)
+    torch.cuda.synchronize()
+    assert tc.device_error() == 0
+    for (t, _, out), w in zip(jobs, want):
+        assert bits_equal(out.cpu().numpy(), w), t
+
+
 def test_batched_jobs_whole_model_slice(tc):
     """trc_cuda_dequant_many over a mixed set of tensors (the whole-model workload's formats and
     row shapes, at reduced row counts) in one launch."""
