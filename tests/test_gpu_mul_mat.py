@@ -119,6 +119,25 @@ def test_transposed_output_view(tc):
     assert normwise(out.cpu().numpy(), want) <= TOL
 
 
+@pytest.mark.parametrize("simt", [False, True], ids=["tcgen05", "simt"])
+@pytest.mark.parametrize("k,m,n,b2,b3", [(128, 512, 512, 4, 2), (512, 2048, 2048, 4, 2)], ids=["default", "full"])
+def test_stress_matmul_batch_known_answer(tc, simt, k, m, n, b2, b3):
+    """The reference's batch-matmul stress case (tests/test_stress.cpp:415-480, both tiers): A has
+    2 x 2 planes filled with 1, 2, 4, 8, B is 0.25 everywhere, so D[.., i2, i3] is exactly
+    k * a[i2 % 2 + 2 (i3 % 2)] * 0.25. The reference checks 3 points per plane within 1e-3; every
+    element is checked for equality here (the operands have no TF32 tails)."""
+    av = torch.tensor([1.0, 2.0, 4.0, 8.0], device="cuda")
+    A = av.view(2, 2, 1, 1).expand(2, 2, m, k).contiguous()   # torch (i3, i2, m, k): plane i2 + 2 i3
+    B = torch.full((b3, b2, n, k), 0.25, device="cuda")
+    D = tc.mul_mat(A, B, simt=simt)
+    assert tuple(D.shape) == (b3, b2, n, m)
+    i2 = torch.arange(b2, device="cuda").view(1, b2)
+    i3 = torch.arange(b3, device="cuda").view(b3, 1)
+    want = (k * av[(i2 % 2) + (i3 % 2) * 2] * 0.25).view(b3, b2, 1, 1).expand(b3, b2, n, m)
+    assert torch.equal(D, want)
+    assert tc.device_error() == 0
+
+
 @pytest.mark.parametrize("k,m,n", [(4096, 4096, 64), (128, 2048, 96), (2048, 640, 72), (14336, 256, 16)])
 def test_config_shaped_slices(tc, k, m, n):
     """Slices of the Linear / GQA / backward GEMMs at their true K, against the oracle."""
