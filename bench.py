@@ -806,8 +806,12 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
     dX = torch.empty((N, K), device="cuda")
     dW = torch.zeros((M, K), device="cuda")
     flops = 2.0 * K * M * N
+    # mul_mat_q's default at 2048 tokens: W dequantized into scratch, then the F32 kernel (the
+    # dequant is inside the timed call); the fused dequant-in-prologue kernel is timed beside it
     t_fwd = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y))
     t_dx = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX))
+    t_fwd_fused = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, fused=True))
+    t_dx_fused = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, fused=True))
     # dW for an F32 LoRA-style copy: dW^T = mul_mat(T(dY), T(X)) accumulated into the grad buffer
     t_dw = timed(lambda: tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True))
     step_ms = t_fwd + t_dx + t_dw
@@ -817,6 +821,8 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         "step_tflops": round(world * 3 * flops / step_ms / 1e9, 2),
         "frac_of_3xtf32_peak": round(3 * flops / step_ms / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
         "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
+        "path": "mul_mat_q from packed W: dequant into pooled scratch + F32 tcgen05 kernel (N >= 1024), timed together",
+        "fused_kernel": {"fwd_tflops": round(flops / t_fwd_fused / 1e9, 2), "dx_tflops": round(flops / t_dx_fused / 1e9, 2)},
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         out["linear_q5_0"]["cpu_reference"] = linear_cpu_rates(tc, torch, wq, K, M, X, dY)

@@ -110,3 +110,4 @@ def test_mul_mat_flag_values_match_header():
     assert int(flags["TRC_CUDA_MM_ACCUMULATE"]) == trc_cuda.MM_ACCUMULATE
     assert int(flags["TRC_CUDA_MM_SIMT"]) == trc_cuda.MM_SIMT
     assert int(flags["TRC_CUDA_MM_ONE_CTA"]) == trc_cuda.MM_ONE_CTA
+    assert int(flags["TRC_CUDA_MM_FUSED"]) == trc_cuda.MM_FUSED

@@ -40,7 +40,7 @@ def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed, one_cta):
     x = np.random.default_rng(qtype).standard_normal((n, K)).astype(np.float32)
     want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, x)
     got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed,
-                       one_cta=one_cta).cpu().numpy()
+                       one_cta=one_cta, fused=True).cpu().numpy()
     assert got.shape == want.shape
     assert normwise(got, want) <= 1e-5
     Wd = tc.gguf_tensor_to_f32(qtype, dev(blocks)).reshape(w_ne1, w_ne0)
@@ -59,8 +59,8 @@ def test_fused_split_k_fills_the_last_wave(tc, one_cta):
     x = np.random.default_rng(82).standard_normal((n, w_ne0)).astype(np.float32)
     want = oracle.mul_mat(Wf, x)
     out = torch.full((n, w_ne1), float("nan"), device="cuda")
-    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), out=out, one_cta=one_cta).cpu().numpy()
-    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), one_cta=one_cta).cpu().numpy()
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), out=out, one_cta=one_cta, fused=True).cpu().numpy()
+    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), one_cta=one_cta, fused=True).cpu().numpy()
     assert tc.device_error() == 0
     assert normwise(got, want.reshape(got.shape)) <= 1e-5
     assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))  # deterministic
@@ -76,13 +76,50 @@ def test_fused_transposed_split_k_four_parts(tc):
     want = oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)
     torch.cuda.synchronize()
     n0 = tc.launch_count()
-    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True)
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True)
     assert tc.launch_count() - n0 == 3  # B's tails, the GEMM and the workspace add
     got = got.cpu().numpy()
-    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True).cpu().numpy()
+    again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True).cpu().numpy()
     assert tc.device_error() == 0
     assert normwise(got, want.reshape(got.shape)) <= 1e-5
     assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))
+
+
+@pytest.mark.parametrize("transposed", [False, True], ids=["W", "WT"])
+def test_two_step_equals_fused_kernel(tc, transposed):
+    """From 1024 columns on, mul_mat_q dequantizes W into scratch and runs the F32 kernel. W is
+    bit-exact and both take the same tile and split-K plan, so the result equals the fused
+    kernel's bit for bit; both are within the bar of the reference."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q4_1, 512, 1024, 1024
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=90)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    K = w_ne1 if transposed else w_ne0
+    x = np.random.default_rng(91).standard_normal((n, K)).astype(np.float32)
+    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, x)
+    torch.cuda.synchronize()
+    n0 = tc.launch_count()
+    two = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed)
+    torch.cuda.synchronize()
+    launched = tc.launch_count() - n0
+    fused = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed, fused=True)
+    assert tc.device_error() == 0
+    two, fused = two.cpu().numpy(), fused.cpu().numpy()
+    assert launched >= 2  # the dequant, then the F32 GEMM (no B-tail pass)
+    assert np.array_equal(two.view(np.uint32), fused.view(np.uint32))
+    assert normwise(two, want.reshape(two.shape)) <= 1e-5
+
+
+def test_simt_two_step_is_bit_exact_with_reference(tc):
+    """mul_mat_q with simt=True: bit-exact dequant, then the SIMT kernel's reference summation, so
+    the whole product is the reference's to the bit (also below 1024 columns)."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q5_1, 256, 96, 40
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=92)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    x = np.random.default_rng(93).standard_normal((n, w_ne0)).astype(np.float32)
+    want = oracle.mul_mat(Wf, x)
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), simt=True).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.reshape(got.shape).view(np.uint32))
+    assert tc.device_error() == 0
 
 
 def test_fused_config_shape_slice(tc):
@@ -91,10 +128,10 @@ def test_fused_config_shape_slice(tc):
     blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=3)
     Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
     x = np.random.default_rng(0).standard_normal((48, w_ne0)).astype(np.float32)
-    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x)).cpu().numpy()
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), fused=True).cpu().numpy()
     assert normwise(got, oracle.mul_mat(Wf, x)) <= 1e-5
     dy = (np.random.default_rng(1).standard_normal((16, w_ne1)) * 1e-2).astype(np.float32)
-    got_t = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True).cpu().numpy()
+    got_t = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True).cpu().numpy()
     assert normwise(got_t, oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)) <= 1e-5
 
 
@@ -111,7 +148,7 @@ def test_cfg1_cpu_runnable_config_in_full(tc):
     x = synth.normal((n, ne0), seed=2025)
     want = oracle.mul_mat(Wf, x)
     two_step = tc.mul_mat(dev(Wf), dev(x)).cpu().numpy()
-    fused = tc.mul_mat_q(qtype, dev(blocks), ne0, ne1, dev(x)).cpu().numpy()
+    fused = tc.mul_mat_q(qtype, dev(blocks), ne0, ne1, dev(x), fused=True).cpu().numpy()
     assert normwise(two_step, want) <= 1e-5
     assert normwise(fused, want) <= 1e-5
     assert tc.device_error() == 0

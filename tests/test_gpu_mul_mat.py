@@ -364,8 +364,9 @@ def test_pretail_bit_identical_fused(tc, transposed, b_mn, one, n):
     k = w_ne1 if transposed else w_ne0
     xn = np.random.default_rng(3).standard_normal((n, k)).astype(np.float32)
     x = dev(np.ascontiguousarray(xn.T)).t() if b_mn else dev(xn)  # same values, contiguous along n
-    got = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one).cpu().numpy()
-    base = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one,
+    got = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one,
+                       fused=True).cpu().numpy()
+    base = tc.mul_mat_q(synth.TYPE_Q5_0, blocks, w_ne0, w_ne1, x, transposed=transposed, one_cta=one, fused=True,
                         no_pretail=True).cpu().numpy()
     assert tc.device_error() == 0
     assert np.array_equal(got.view(np.uint32), base.view(np.uint32))

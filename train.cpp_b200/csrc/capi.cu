@@ -68,6 +68,11 @@ struct UploadCtx {
 };
 UploadCtx g_upload[64];
 
+// From this many columns of b on, trc_cuda_mul_mat_q dequantizes W into scratch and runs the F32
+// kernel: the dequant pass costs about 88 / N of the GEMM, while the fused kernel's in-loop decode
+// costs it 12-20 % at N = 2048 on B200.
+constexpr int64_t kTwoStepMinColumns = 1024;
+
 // Packed bytes per chunk of a pipelined upload, and the smallest upload that is pipelined at all.
 constexpr size_t kUploadChunkBytes = size_t(8) << 20;
 constexpr int64_t kRunBlocks       = 256;  // chunks start on whole runs of the dequant kernel
@@ -111,6 +116,34 @@ int load_quant_pipelined(int type, const uint8_t* host, int64_t n_blocks, uint8_
         if (st != TRC_CUDA_OK) return st;
     }
     return TRC_CUDA_OK;
+}
+
+// trc_cuda_mul_mat_q in two steps: W dequantized into pooled, stream-ordered scratch, then
+// trc_cuda_mul_mat on a view of it (transposed for a_transposed). TRC_CUDA_EUNSUPPORTED, with
+// nothing launched, when the scratch cannot be allocated.
+int mul_mat_q_two_step(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
+                       const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags, cudaStream_t s) {
+    const int64_t n = w_ne0 * w_ne1;
+    retain_pool_once();
+    void* wf = nullptr;
+    if (cudaMallocAsync(&wf, static_cast<size_t>(n) * sizeof(float), s) != cudaSuccess) {
+        cudaGetLastError();
+        return TRC_CUDA_EUNSUPPORTED;
+    }
+    int st = trc_cuda_dequant(type, w_blocks, n / 32, static_cast<float*>(wf), s);
+    if (st == TRC_CUDA_OK) {
+        trc_cuda_view a;
+        a.data = wf;
+        a.ne[0] = a_transposed ? w_ne1 : w_ne0;
+        a.ne[1] = a_transposed ? w_ne0 : w_ne1;
+        a.ne[2] = a.ne[3] = 1;
+        a.nb[0] = a_transposed ? 4 * w_ne0 : 4;
+        a.nb[1] = a_transposed ? 4 : 4 * w_ne0;
+        a.nb[2] = a.nb[3] = 4 * n;
+        st = trc_cuda_mul_mat(&a, &b, &d, flags & ~(TRC_CUDA_MM_FUSED | TRC_CUDA_MM_NO_PRETAIL), s);
+    }
+    cudaFreeAsync(wf, s);
+    return st;
 }
 
 }  // namespace trc
@@ -282,7 +315,13 @@ int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_
     if (b->ne[0] != K || d->ne[0] != M || d->ne[1] != b->ne[1] || d->ne[2] != b->ne[2] || d->ne[3] != b->ne[3])
         return TRC_CUDA_EINVAL;
     if (nelements(*d) == 0) return TRC_CUDA_OK;
-    return mul_mat_q_tc(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, flags, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool fused = (flags & TRC_CUDA_MM_FUSED) != 0;
+    if (!fused && ((flags & TRC_CUDA_MM_SIMT) != 0 || b->ne[1] >= kTwoStepMinColumns)) {
+        const int st = mul_mat_q_two_step(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, flags, s);
+        if (st != TRC_CUDA_EUNSUPPORTED) return st;  // else: no scratch memory, the fused kernel runs
+    }
+    return mul_mat_q_tc(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, flags, s);
 }
 
 }  // extern "C"

@@ -57,6 +57,26 @@
 
 namespace trc {
 
+
+// Scratch buffers (B's tails, split-K workspaces, dequantized weights) come from the device's
+// default memory pool; freed blocks stay in the pool (release threshold raised once per device, a
+// setting of this process only) so that steady-state calls do not map memory again.
+void retain_pool_once() {
+    static std::mutex mu;
+    static uint64_t   done = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done & (uint64_t(1) << dev)) return;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t threshold = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    }
+    cudaGetLastError();
+    done |= uint64_t(1) << dev;
+}
+
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 16;   // D tile of one CTA: BM rows (TMEM lanes) x BN columns
@@ -885,24 +905,6 @@ struct Pretail {
     CUtensorMap map;
 };
 
-// The tails come from the device's default memory pool; freed blocks stay in the pool (release
-// threshold raised once per device, a setting of this process only) so that steady-state calls do
-// not map memory again.
-void retain_pool_once() {
-    static std::mutex mu;
-    static uint64_t   done = 0;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
-    std::lock_guard<std::mutex> lock(mu);
-    if (done & (uint64_t(1) << dev)) return;
-    cudaMemPool_t pool;
-    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-        uint64_t threshold = UINT64_MAX;
-        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
-    }
-    cudaGetLastError();
-    done |= uint64_t(1) << dev;
-}
 
 bool make_pretail(const trc_cuda_view& B, int box_rows, bool b_mn, bool b_tma5, cudaStream_t stream, Pretail& out) {
     retain_pool_once();

@@ -55,6 +55,9 @@ int check_launch();
 
 int sm_count_current();
 
+// Keeps memory freed to the device's default pool (cudaFreeAsync) in the pool for reuse.
+void retain_pool_once();
+
 // Per-library entry points implemented in the individual .cu files.
 int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream);
 int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base, void* const* peer_bases,
