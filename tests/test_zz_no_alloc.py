@@ -33,7 +33,10 @@ def _free_device_bytes(tc) -> int:
 
 
 def test_static_loader_matches_staged_loader_twice(tc):
-    cases = [(synth.TYPE_Q5_0, 4096 * 1024), (synth.TYPE_Q8_0, 4096 * 512 + 32 * 7)]
+    # the last case is above the 16 MB from which trc_cuda_load_quant splits its upload across a
+    # second stream; the static loader always makes one copy on the caller's stream
+    cases = [(synth.TYPE_Q5_0, 4096 * 1024), (synth.TYPE_Q8_0, 4096 * 512 + 32 * 7),
+             (synth.TYPE_Q8_0, 4096 * 5000)]
     for i, (qtype, n) in enumerate(cases):
         host = torch.from_numpy(synth.random_blocks(qtype, n // 32, seed=900 + i)).pin_memory()
         staging = torch.empty(host.numel(), dtype=torch.uint8, device="cuda")

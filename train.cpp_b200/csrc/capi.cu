@@ -146,6 +146,17 @@ int mul_mat_q_two_step(int type, const void* w_blocks, int64_t w_ne0, int64_t w_
     return st;
 }
 
+// The upload as one copy and one dequant, both on the caller's stream: no stream, event or memory
+// of the library's own is created (the allocation-free loader relies on this).
+int load_quant_direct(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
+                      cudaStream_t s) {
+    const size_t bb = trc_cuda_block_bytes(type);
+    const cudaError_t e =
+        cudaMemcpyAsync(staging, host_blocks, static_cast<size_t>(n_blocks) * bb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return trc_cuda_dequant(type, staging, n_blocks, out, s);
+}
+
 }  // namespace trc
 
 using namespace trc;
@@ -241,10 +252,7 @@ int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, voi
     if (static_cast<size_t>(n_blocks) * bb >= 2 * kUploadChunkBytes)
         return load_quant_pipelined(type, static_cast<const uint8_t*>(host_blocks), n_blocks,
                                     static_cast<uint8_t*>(staging), out, s);
-    const cudaError_t e =
-        cudaMemcpyAsync(staging, host_blocks, static_cast<size_t>(n_blocks) * bb, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_fail(e);
-    return trc_cuda_dequant(type, staging, n_blocks, out, stream);
+    return load_quant_direct(type, host_blocks, n_blocks, staging, out, s);
 }
 
 // Shape rules of the mul_mat constructor (src/ops/trc_ops.cpp:366-385).

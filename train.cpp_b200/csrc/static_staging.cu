@@ -51,5 +51,7 @@ extern "C" int trc_cuda_load_quant_static(int type, const void* host_blocks, int
     void* staging = nullptr;
     const int st = static_staging_address(&staging);
     if (st != TRC_CUDA_OK) return st;
-    return trc_cuda_load_quant(type, host_blocks, n_blocks, staging, out, stream);
+    // One copy and one dequant on the caller's stream, whatever the size: the chunked upload of
+    // trc_cuda_load_quant would create a copy stream and events of the library's own.
+    return trc::load_quant_direct(type, host_blocks, n_blocks, staging, out, static_cast<cudaStream_t>(stream));
 }

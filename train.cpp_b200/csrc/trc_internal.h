@@ -58,6 +58,11 @@ int sm_count_current();
 // Keeps memory freed to the device's default pool (cudaFreeAsync) in the pool for reuse.
 void retain_pool_once();
 
+// trc_cuda_load_quant's single-copy path (arguments already checked): one host-to-device copy into
+// `staging` and one dequant, both on stream s; creates no stream, event or allocation.
+int load_quant_direct(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
+                      cudaStream_t s);
+
 // Per-library entry points implemented in the individual .cu files.
 int dequant_jobs(const trc_cuda_dequant_job* jobs, int n_jobs, cudaStream_t stream);
 int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void* local_base, void* const* peer_bases,
