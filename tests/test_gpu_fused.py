@@ -109,6 +109,26 @@ def test_two_step_equals_fused_kernel(tc, transposed):
     assert normwise(two, want.reshape(two.shape)) <= 1e-5
 
 
+def test_two_step_accumulate_equals_fused_kernel(tc):
+    """ACCUMULATE through both implementations (no split-K with ACCUMULATE, so the same plan):
+    D += W^T dY on top of the same starting D, bit for bit, and within the bar of the reference."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q8_0, 768, 512, 1024      # A = T(W): M 768, K 512
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=94)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    dy = (np.random.default_rng(95).standard_normal((n, w_ne1)) * 1e-2).astype(np.float32)
+    d0 = np.random.default_rng(96).standard_normal((n, w_ne0)).astype(np.float32)
+    outs = []
+    for fused in (False, True):
+        out = dev(d0)
+        tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, out=out, accumulate=True,
+                     fused=fused)
+        outs.append(out.cpu().numpy())
+    assert tc.device_error() == 0
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    want = d0 + oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy).reshape(d0.shape)
+    assert normwise(outs[0], want) <= 1e-5
+
+
 def test_simt_two_step_is_bit_exact_with_reference(tc):
     """mul_mat_q with simt=True: bit-exact dequant, then the SIMT kernel's reference summation, so
     the whole product is the reference's to the bit (also below 1024 columns)."""
