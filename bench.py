@@ -815,6 +815,7 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
     # dW for an F32 LoRA-style copy: dW^T = mul_mat(T(dY), T(X)) accumulated into the grad buffer
     t_dw = timed(lambda: tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True))
     step_ms = t_fwd + t_dx + t_dw
+    check_linear_slices(tc, torch, wq, K, M, X, dY, world)
     out["linear_q5_0"] = {
         "fwd_tflops": round(flops / t_fwd / 1e9, 2), "dx_tflops": round(flops / t_dx / 1e9, 2),
         "dw_tflops": round(flops / t_dw / 1e9, 2), "step_ms": round(step_ms, 4),
@@ -846,6 +847,7 @@ def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> 
     # dA = repeat_back(T(mul_mat(T(G), T(B)))): one plane-reducing GEMM writing T(dA)
     t_a = timed(lambda: tc.mul_mat_repeat_back(G.transpose(-1, -2), B.transpose(-1, -2), dA.transpose(-1, -2)))
     t_b = timed(lambda: tc.mul_mat(A.transpose(-1, -2), G, out=dB))
+    check_gqa_planes(tc, torch, A, B, G, D, dA, dB, world)
     out["gqa_bcast"] = {
         "fwd_tflops": round(world * gflop / t_f / 1e9, 2), "da_tflops": round(world * gflop / t_a / 1e9, 2),
         "db_tflops": round(world * gflop / t_b / 1e9, 2), "step_ms": round(t_f + t_a + t_b, 4),
@@ -858,6 +860,57 @@ def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> 
     out["peak_3xtf32_tflops"] = round(tf32x3_peak, 1) if tf32x3_peak else None
     out["peak_note"] = "TF32 dense taken as half the measured bf16 burst rate; 3 passes"
     return out
+
+
+def _normwise(got: np.ndarray, want: np.ndarray) -> float:
+    return float(np.max(np.abs(got.astype(np.float64) - want)) / np.max(np.abs(want)))
+
+
+def check_linear_slices(tc, torch, wq, K, M, X, dY, world: int) -> None:
+    """Correctness guard for the timed Linear step, outside the timed region: every product the
+    step times, run once more into fresh outputs, on 16 token (or output) columns against the oracle
+    (the reference's summation order), normwise <= 1e-5."""
+    import oracle
+
+    threads = max(1, (os.cpu_count() or 1) // world)
+    N = X.shape[0]
+    Wn = oracle.dequant(synth.TYPE_Q5_0, wq.cpu().numpy()).reshape(M, K)
+    j = np.arange(7, N, N // 16)[:16]
+    Xj, dYj = X[j].cpu().numpy(), dY[j].cpu().numpy()
+    want_y = oracle.mul_mat(Wn, Xj, n_threads=threads)[0, 0]
+    want_dx = oracle.mul_mat(np.ascontiguousarray(Wn.T), dYj, n_threads=threads)[0, 0]
+    for fused in (False, True):
+        Y = tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, fused=fused)
+        dX = tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, fused=fused)
+        e_y, e_dx = _normwise(Y[j].cpu().numpy(), want_y), _normwise(dX[j].cpu().numpy(), want_dx)
+        assert e_y <= 1e-5 and e_dx <= 1e-5, f"Linear step parity (fused={fused}): fwd {e_y:.2e}, dX {e_dx:.2e}"
+    dW = torch.zeros((M, K), device="cuda")
+    tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True)
+    k = np.arange(3, K, K // 16)[:16]
+    want_dw = oracle.mul_mat(np.ascontiguousarray(dY.cpu().numpy().T), np.ascontiguousarray(X.cpu().numpy().T[k]),
+                             n_threads=threads)[0, 0]
+    e_dw = _normwise(dW[:, k].t().cpu().numpy(), want_dw)
+    assert e_dw <= 1e-5, f"Linear step parity: dW {e_dw:.2e}"
+    assert tc.device_error() == 0
+
+
+def check_gqa_planes(tc, torch, A, B, G, D, dA, dB, world: int) -> None:
+    """Correctness guard for the timed GQA step (outputs of its last timed launches): one (i2, i3)
+    plane of the forward and of dB, and one reduced plane of dA, against the oracle."""
+    import oracle
+
+    threads = max(1, (os.cpu_count() or 1) // world)
+    torch.cuda.synchronize()
+    i3, i2, ga = A.shape[0] - 1, 13, 5
+    a, b, g = A[i3, i2 % 8].cpu().numpy(), B[i3, i2].cpu().numpy(), G[i3, i2].cpu().numpy()
+    e_f = _normwise(D[i3, i2].cpu().numpy(), oracle.mul_mat(a, b, n_threads=threads)[0, 0])
+    e_b = _normwise(dB[i3, i2].cpu().numpy(), oracle.mul_mat(np.ascontiguousarray(a.T), g, n_threads=threads)[0, 0])
+    want_da = sum(oracle.mul_mat(np.ascontiguousarray(G[i3, p].cpu().numpy().T),
+                                 np.ascontiguousarray(B[i3, p].cpu().numpy().T), n_threads=threads)[0, 0]
+                  for p in range(ga, 32, 8))
+    e_a = _normwise(np.ascontiguousarray(dA[i3, ga].t().cpu().numpy()), want_da)
+    assert max(e_f, e_a, e_b) <= 1e-5, f"GQA step parity: fwd {e_f:.2e}, dA {e_a:.2e}, dB {e_b:.2e}"
+    assert tc.device_error() == 0
 
 
 def _ref_gflops(a_base, a_trans, b_base, b_trans, flops: float) -> float | None:

@@ -145,13 +145,18 @@ int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, voi
  * that must not grow device memory (a process whose device memory is owned by another allocator or
  * has a fixed budget, or a loader running while other work owns the allocator). It needs no
  * caller staging buffer: the packed blocks are staged in a fixed array inside the library, a
- * file-scope static __device__ array of TRC_CUDA_STATIC_STAGING_BYTES (64 MiB) that every GPU
- * which loads the library holds until the process exits. The call itself allocates nothing and
- * calls no allocating routine.
+ * file-scope static __device__ array of TRC_CUDA_STATIC_STAGING_BYTES (64 MiB). The call itself
+ * allocates nothing and calls no allocating routine.
+ *   - When the memory is taken: the array is part of the library's device code, which CUDA loads
+ *     on a device at the library's first kernel launch or symbol lookup there (lazy module loading,
+ *     the default since CUDA 12.2), or at process start under CUDA_MODULE_LOADING=EAGER. From then
+ *     on that GPU holds the 64 MiB until the process exits. A caller with a fixed budget makes one
+ *     call per device before fixing it; a call with n_blocks = 0 is enough (it loads the module
+ *     and copies nothing). Make that first call before any stream capture begins.
  *   - Tensors whose packed bytes exceed TRC_CUDA_STATIC_STAGING_BYTES are rejected with
  *     TRC_CUDA_ETOOBIG before any device work.
- *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) for
- *     that device; make that first call before any stream capture begins.
+ *   - Every call looks up the array's address on the current device (cudaGetSymbolAddress, a host
+ *     lookup once the module is loaded), so a device reset that re-creates the context is safe.
  *   - All calls share the one array per device and it keeps the last call's bytes; each call
  *     overwrites the bytes it uses before reading them, so nothing needs clearing. Calls whose
  *     copies or kernels overlap on the GPU (different streams without ordering) race on the array.

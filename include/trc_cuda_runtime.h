@@ -29,6 +29,9 @@ const char* trc_cuda_rt_error_string(int cuda_error);
 int trc_cuda_rt_malloc(void** ptr, size_t bytes);        /* device memory of the current device */
 int trc_cuda_rt_free(void* ptr);
 int trc_cuda_rt_malloc_host(void** ptr, size_t bytes);   /* pinned host memory */
+/* Number of successful trc_cuda_rt_malloc_host calls in this process (page-locking is a system
+ * call; loaders that reuse their pinned staging keep this constant across repeated loads). */
+uint64_t trc_cuda_rt_host_alloc_count(void);
 int trc_cuda_rt_free_host(void* ptr);
 
 /* kind: 0 host->device, 1 device->host, 2 device->device. Synchronous. */

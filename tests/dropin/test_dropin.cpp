@@ -7,10 +7,11 @@
 // backend conformance suite compares its Vulkan device with the CPU
 // (tests/test_backend_conformance.cpp:43-128 of train.cpp).
 //
-// usage: test_dropin [all|alloc_fail|shard] [path/to/quantized.gguf]
+// usage: test_dropin [all|alloc_fail|shard|packed|checkpoint] [path] [tokens]
 // Exit status 0 when every case passes.
 #include "traincpp/traincpp.h"
 #include "trc_cuda_backend.h"
+#include "trc_cuda_runtime.h"
 
 #include <cmath>
 #include <cstdio>
@@ -392,6 +393,30 @@ void gguf_warm_start(Device* cpu, Device* cuda, const char* path) {
         buffer_free(buf);
         context_free(ctx);
     }
+    // repeated single-tensor loads reuse the device's pinned staging: no page-locking per tensor
+    {
+        Context* ctx = context_new(1 << 20);
+        std::vector<Tensor*> ws;
+        for (int64_t i = 0; i < gguf_tensor_count(f); ++i)
+            ws.push_back(gguf_new_tensor(ctx, f, gguf_tensor_info(f, i)->name, TYPE_F32));
+        Buffer* buf = buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
+        size_t largest = 0;
+        for (int64_t i = 0; i < gguf_tensor_count(f); ++i) largest = std::max(largest, gguf_tensor_info(f, i)->nbytes);
+        int64_t big = 0;
+        for (int64_t i = 0; i < gguf_tensor_count(f); ++i)
+            if (gguf_tensor_info(f, i)->nbytes == largest) big = i;
+        cuda_gguf_load_tensor(f, path, gguf_tensor_info(f, big)->name, ws[(size_t) big]);  // sizes the staging
+        const uint64_t pins = trc_cuda_rt_host_alloc_count();
+        bool ok = true;
+        for (int rep = 0; rep < 3; ++rep)
+            for (int64_t i = 0; i < gguf_tensor_count(f); ++i)
+                ok = ok && cuda_gguf_load_tensor(f, path, gguf_tensor_info(f, i)->name, ws[(size_t) i]);
+        if (!ok || trc_cuda_rt_host_alloc_count() != pins) fail("repeated cuda_gguf_load_tensor pinned host memory again");
+        else std::printf("    [ OK ] %-34s %lld loads, no new pinned allocation\n", "single-tensor loader staging reuse",
+                         (long long) (3 * gguf_tensor_count(f)));
+        buffer_free(buf);
+        context_free(ctx);
+    }
     // the warm-started weight feeds nn::Linear (linear_init_weight, src/nn/trc_nn.cpp:209-220)
     const GgufTensorInfo* info = gguf_tensor_info(f, 0);
     std::vector<float> outs[2];
@@ -472,6 +497,243 @@ void gguf_sharded_load(Device* cuda, const char* path, int world) {
     gguf_close(full);
 }
 
+// Frozen quantized weights on the packed-weight buffer type (CUDA<i>_Q): nn::Linear's forward and
+// the gradient of its input through train.cpp's own autograd, with W's packed GGUF blocks decoded
+// inside the GEMM. Compared with (a) the same graph on the CUDA device with W as an ordinary F32
+// tensor (dequantized on load): bit for bit, since the dequant-in-prologue GEMM and the F32 GEMM
+// take the same tile and split-K plan on bit-identical weights; (b) the CPU device with the
+// reference loader: normwise 1e-5. Device memory: the packed weight takes its blocks' bytes, not
+// its F32 bytes.
+struct PackedRun {
+    std::vector<float> y, dx, w_head;
+    size_t             weight_bytes = 0;  // device memory the loaded weight took
+};
+
+size_t device_free(Device* d) { return d->props().memory_free; }
+
+PackedRun packed_linear(Device* dev, int mode, const GgufFile* meta, const GgufFile* full, const char* path,
+                        const char* name, int64_t tokens) {
+    // mode 0: packed buffer on the CUDA device; 1: F32 weight on the CUDA device; 2: CPU device
+    PackedRun r;
+    Context* wctx = context_new(1 << 16);
+    Tensor*  W    = gguf_new_tensor(wctx, meta, name, TYPE_F32);
+    const size_t free0 = mode < 2 ? device_free(dev) : 0;
+    Buffer* wbuf = buffer_alloc_ctx_tensors(wctx, mode == 0 ? cuda_packed_buffer_type(0) : dev->default_buffer_type());
+    const bool loaded = mode < 2 ? cuda_gguf_load_tensor(meta, path, name, W) : gguf_load_tensor(full, name, W);
+    if (!loaded) fail(std::string("loading ") + name);
+    if (mode < 2) r.weight_bytes = free0 - device_free(dev);
+    Context* ctx = context_new(1 << 22);
+    Graph*   g   = graph_new(ctx);
+    Linear   lin;
+    linear_init_weight(ctx, &lin, W, nullptr);
+    tensor_clear_param(W);  // frozen: no gradient for the quantized weight
+    Tensor* X = new_tensor_2d(ctx, TYPE_F32, W->ne[0], tokens);
+    tensor_set_param(X);
+    Tensor* y = linear_forward(ctx, &lin, X);
+    Tensor* G = new_tensor_2d(ctx, TYPE_F32, y->ne[0], y->ne[1]);
+    Tensor* loss = sum(ctx, mul(ctx, y, G));
+    tensor_set_loss(loss);
+    graph_build_forward_expand(ctx, g, loss);
+    graph_build_backward_expand(g);
+    if (const Tensor* bad = graph_first_unsupported(g, dev)) fail(std::string("preflight: ") + op_name(bad->op));
+    Buffer* buf = buffer_alloc_ctx_tensors(ctx, dev->default_buffer_type());
+    const auto xv = gauss((size_t) tensor_nelements(X), 31), gv = gauss((size_t) tensor_nelements(G), 32, 1e-2f);
+    tensor_set(X, xv.data(), 0, xv.size() * 4);
+    tensor_set(G, gv.data(), 0, gv.size() * 4);
+    graph_reset(g);
+    dev->graph_compute(g);
+    r.y.resize((size_t) tensor_nelements(y));
+    tensor_get(y, r.y.data(), 0, r.y.size() * 4);
+    Tensor* gx = graph_get_grad_acc(g, X);
+    r.dx.resize((size_t) tensor_nelements(gx));
+    tensor_get(gx, r.dx.data(), 0, r.dx.size() * 4);
+    r.w_head.resize((size_t) std::min<int64_t>(tensor_nelements(W), 4096 + 37));
+    tensor_get(W, r.w_head.data(), 0, r.w_head.size() * 4);  // on the packed buffer: dequantized on read
+    buffer_free(buf);
+    graph_free(g);
+    context_free(ctx);
+    buffer_free(wbuf);
+    context_free(wctx);
+    return r;
+}
+
+void packed_weights(Device* cpu, Device* cuda, const char* path, int64_t tokens) {
+    std::printf("  frozen quantized weights on %s (%s, %lld tokens)\n", cuda_packed_buffer_type(0)->name(), path,
+                (long long) tokens);
+    GgufFile* meta = gguf_open(path, false);
+    GgufFile* full = gguf_open(path, true);
+    if (meta == nullptr || full == nullptr) {
+        fail("gguf_open failed");
+        return;
+    }
+    auto same_bits = [](const std::vector<float>& a, const std::vector<float>& b) {
+        return a.size() == b.size() && std::memcmp(a.data(), b.data(), a.size() * 4) == 0;
+    };
+    for (int64_t i = 0; i < gguf_tensor_count(meta); ++i) {
+        const GgufTensorInfo* info = gguf_tensor_info(meta, i);
+        const PackedRun pk = packed_linear(cuda, 0, meta, full, path, info->name, tokens);
+        const PackedRun f32 = packed_linear(cuda, 1, meta, full, path, info->name, tokens);
+        const std::string n = std::string(info->name) + " (" + type_name(info->type) + ")";
+        if (!same_bits(pk.y, f32.y) || !same_bits(pk.dx, f32.dx)) fail(n + ": packed path differs from the F32 device path");
+        else std::printf("    [ OK ] %-34s y and dX bit-identical to the F32 device path\n", n.c_str());
+        // the CPU device (single-threaded reference kernels) on the weights small enough for it
+        const int64_t cpu_tokens = std::min<int64_t>(tokens, 64);
+        if (gguf_tensor_nelements(meta, i) <= (int64_t(1) << 23)) {
+            const PackedRun pk_small = cpu_tokens == tokens ? pk : packed_linear(cuda, 0, meta, full, path, info->name, cpu_tokens);
+            const PackedRun ref = packed_linear(cpu, 2, meta, full, path, info->name, cpu_tokens);
+            if (!same_bits(pk_small.w_head, ref.w_head))
+                fail(n + ": tensor_get of the packed weight differs from the reference loader");
+            compare((n + " y vs CPU").c_str(), pk_small.y, ref.y);
+            compare((n + " dX vs CPU").c_str(), pk_small.dx, ref.dx);
+        }
+        const size_t f32_bytes = (size_t) gguf_tensor_nelements(meta, i) * 4;
+        std::printf("    device memory of the loaded weight: packed %zu B, F32 %zu B (file %zu B packed)\n",
+                    pk.weight_bytes, f32.weight_bytes, (size_t) info->nbytes);
+        // the packed weight holds its blocks (rounded to the allocator's granularity), never F32 bytes
+        if (f32_bytes >= (size_t(64) << 20) && !(pk.weight_bytes < info->nbytes + (size_t(4) << 20) && f32.weight_bytes >= f32_bytes))
+            fail(n + ": the packed weight took more device memory than its blocks");
+    }
+    // what the device refuses on a packed weight: any op other than mul_mat reading it
+    {
+        const GgufTensorInfo* info = gguf_tensor_info(meta, 0);
+        Context* wctx = context_new(1 << 16);
+        Tensor*  W    = gguf_new_tensor(wctx, meta, info->name, TYPE_F32);
+        Buffer*  wbuf = buffer_alloc_ctx_tensors(wctx, cuda_packed_buffer_type(0));
+        cuda_gguf_load_tensor(meta, path, info->name, W);
+        Context* ctx = context_new(1 << 20);
+        Graph*   g   = graph_new(ctx);
+        Tensor*  s   = sum(ctx, sqr(ctx, W));
+        graph_build_forward_expand(ctx, g, s);
+        const Tensor* bad = graph_first_unsupported(g, cuda);
+        if (bad == nullptr || bad->op != OP_SQR) fail("preflight accepted sqr of a packed weight");
+        else std::printf("    [ OK ] %-34s preflight reports %s\n", "non-mul_mat reader of a packed W", op_name(bad->op));
+        Graph* g2 = graph_new(ctx);
+        Tensor* c = cont(ctx, transpose(ctx, W));
+        graph_build_forward_expand(ctx, g2, c);
+        const Tensor* bad2 = graph_first_unsupported(g2, cuda);
+        if (bad2 == nullptr || bad2->op != OP_CONT) fail("preflight accepted cont of a packed weight");
+        graph_free(g2);
+        graph_free(g);
+        context_free(ctx);
+        buffer_free(wbuf);
+        context_free(wctx);
+    }
+    gguf_close(meta);
+    gguf_close(full);
+}
+
+// checkpoint_save / checkpoint_load (src/io/trc_checkpoint.cpp) of a model trained on the CUDA device:
+// the reference's own functions, unchanged, over the CUDA buffers (tensor_get / set_tensor). The
+// file written from the device is loaded onto a fresh CUDA model and onto a fresh CPU model; every
+// parameter and AdamW state tensor must come back bit-identical on both, the optimizer step and
+// learning rate restored, and one more step on each device must agree.
+struct CkptModel {
+    Context*   ctx = nullptr;
+    Graph*     g = nullptr;
+    Buffer*    buf = nullptr;
+    Optimizer* opt = nullptr;
+    Tensor*    W = nullptr;
+    Tensor*    b = nullptr;
+};
+
+CkptModel ckpt_model(Device* dev) {
+    constexpr int64_t IN = 128, OUT = 96, BATCH = 40;
+    CkptModel m;
+    m.ctx = context_new((size_t) 1 << 24);
+    m.g   = graph_new(m.ctx);
+    m.W   = new_tensor_2d(m.ctx, TYPE_F32, IN, OUT);
+    m.b   = new_tensor_2d(m.ctx, TYPE_F32, OUT, 1);
+    tensor_set_name(m.W, "lin.weight");
+    tensor_set_name(m.b, "lin.bias");
+    Tensor* x = new_tensor_2d(m.ctx, TYPE_F32, IN, BATCH);
+    Tensor* y = new_tensor_2d(m.ctx, TYPE_F32, OUT, BATCH);
+    tensor_set_param(m.W);
+    tensor_set_param(m.b);
+    Tensor* loss = scale(m.ctx, sum(m.ctx, sqr(m.ctx, sub(m.ctx, add(m.ctx, mul_mat(m.ctx, m.W, x), m.b), y))),
+                         1.0f / (float) (OUT * BATCH));
+    tensor_set_loss(loss);
+    graph_build_forward_expand(m.ctx, m.g, loss);
+    graph_build_backward_expand(m.g);
+    m.buf = buffer_alloc_ctx_tensors(m.ctx, dev->default_buffer_type());
+    const auto vw = gauss((size_t) (IN * OUT), 41, 0.05f), vb = gauss((size_t) OUT, 42, 0.1f);
+    const auto vx = gauss((size_t) (IN * BATCH), 43), vy = gauss((size_t) (OUT * BATCH), 44);
+    tensor_set(m.W, vw.data(), 0, vw.size() * 4);
+    tensor_set(m.b, vb.data(), 0, vb.size() * 4);
+    tensor_set(x, vx.data(), 0, vx.size() * 4);
+    tensor_set(y, vy.data(), 0, vy.size() * 4);
+    Tensor* params[2] = {m.W, m.b};
+    AdamwOptions o;
+    o.lr = 1e-2f;
+    m.opt = optim_adamw_new(m.ctx, params, 2, o);
+    optim_alloc_state(m.opt);
+    return m;
+}
+
+void ckpt_step(Device* dev, CkptModel& m) {
+    graph_reset(m.g);
+    dev->graph_compute(m.g);
+    optim_step(m.opt);
+}
+
+std::vector<std::vector<float>> ckpt_tensors(const CkptModel& m) {
+    std::vector<std::vector<float>> out;
+    std::vector<Tensor*> ts = {m.W, m.b};
+    for (int64_t i = 0; i < optim_state_count(m.opt); ++i) ts.push_back(optim_state(m.opt, i));
+    for (Tensor* t : ts) {
+        std::vector<float> v((size_t) tensor_nelements(t));
+        tensor_get(t, v.data(), 0, v.size() * 4);
+        out.push_back(std::move(v));
+    }
+    return out;
+}
+
+void ckpt_free(CkptModel& m) {
+    optim_free(m.opt);
+    buffer_free(m.buf);
+    graph_free(m.g);
+    context_free(m.ctx);
+}
+
+void checkpoint_roundtrip(Device* cpu, Device* cuda, const char* path) {
+    std::printf("  checkpoint_save / checkpoint_load on the CUDA device (%s)\n", path);
+    CkptModel src = ckpt_model(cuda);
+    for (int s = 0; s < 3; ++s) ckpt_step(cuda, src);
+    CheckpointItems items;
+    items.optimizer = src.opt;
+    if (!checkpoint_save(path, items, "dropin")) {
+        fail("checkpoint_save from the CUDA device");
+        return;
+    }
+    const auto saved = ckpt_tensors(src);
+    CkptModel on_cuda = ckpt_model(cuda), on_cpu = ckpt_model(cpu);
+    CheckpointItems a, b;
+    a.optimizer = on_cuda.opt;
+    b.optimizer = on_cpu.opt;
+    if (!checkpoint_load(path, a) || !checkpoint_load(path, b)) {
+        fail("checkpoint_load");
+        return;
+    }
+    const auto got_cuda = ckpt_tensors(on_cuda), got_cpu = ckpt_tensors(on_cpu);
+    bool same = got_cuda.size() == saved.size() && got_cpu.size() == saved.size();
+    for (size_t i = 0; same && i < saved.size(); ++i)
+        same = std::memcmp(got_cuda[i].data(), saved[i].data(), saved[i].size() * 4) == 0 &&
+               std::memcmp(got_cpu[i].data(), saved[i].data(), saved[i].size() * 4) == 0;
+    if (!same) fail("checkpoint tensors differ between the saved model, the CUDA load and the CPU load");
+    else std::printf("    [ OK ] %-34s %zu tensors bit-identical (CUDA load = CPU load = saved)\n", "checkpoint round trip",
+                     saved.size());
+    if (optim_step_count(on_cuda.opt) != optim_step_count(src.opt) || optim_step_count(on_cpu.opt) != optim_step_count(src.opt) ||
+        optim_get_lr(on_cuda.opt) != optim_get_lr(src.opt))
+        fail("optimizer step / learning rate not restored");
+    ckpt_step(cuda, on_cuda);
+    ckpt_step(cpu, on_cpu);
+    const auto next_cuda = ckpt_tensors(on_cuda), next_cpu = ckpt_tensors(on_cpu);
+    compare("step after resume: W (CUDA vs CPU)", next_cuda[0], next_cpu[0], false, 5e-5);
+    compare("step after resume: b (CUDA vs CPU)", next_cuda[1], next_cpu[1], false, 5e-5);
+    ckpt_free(src);
+    ckpt_free(on_cuda);
+    ckpt_free(on_cpu);
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -493,6 +755,16 @@ int main(int argc, char** argv) {
         buffer_alloc_ctx_tensors(ctx, cuda->default_buffer_type());
         std::printf("allocation unexpectedly succeeded\n");
         return 0;
+    }
+    if (mode == "packed" && argc > 2) {
+        packed_weights(cpu, cuda, argv[2], argc > 3 ? std::atoll(argv[3]) : 64);
+        std::printf("%s: %d failure(s)\n", g_failures == 0 ? "PASS" : "FAIL", g_failures);
+        return g_failures == 0 ? 0 : 1;
+    }
+    if (mode == "checkpoint" && argc > 2) {
+        checkpoint_roundtrip(cpu, cuda, argv[2]);
+        std::printf("%s: %d failure(s)\n", g_failures == 0 ? "PASS" : "FAIL", g_failures);
+        return g_failures == 0 ? 0 : 1;
     }
     if (mode == "shard" && argc > 2) {
         for (int world : {1, 2, 3}) gguf_sharded_load(cuda, argv[2], world);

@@ -111,3 +111,20 @@ def test_mul_mat_flag_values_match_header():
     assert int(flags["TRC_CUDA_MM_SIMT"]) == trc_cuda.MM_SIMT
     assert int(flags["TRC_CUDA_MM_ONE_CTA"]) == trc_cuda.MM_ONE_CTA
     assert int(flags["TRC_CUDA_MM_FUSED"]) == trc_cuda.MM_FUSED
+
+
+def test_loader_wrappers_reject_bad_destinations_on_host():
+    """The loaders write 32 floats per block at dst.data_ptr(): a host tensor, another dtype or a
+    device tensor passed as the host source is refused before any library call."""
+    import numpy as np
+    import torch
+
+    host = np.zeros(18 * 2, dtype=np.uint8)
+    for load in (lambda d: trc_cuda.gguf_load_tensor(2, host, d, torch.empty(36, dtype=torch.uint8)),
+                 lambda d: trc_cuda.gguf_load_tensor_static(2, host, d)):
+        with pytest.raises(trc_cuda.TrcCudaError, match="float32"):
+            load(torch.empty(64, dtype=torch.float16))
+        with pytest.raises(trc_cuda.TrcCudaError, match="CUDA"):
+            load(torch.empty(64, dtype=torch.float32))       # host memory, not device memory
+    with pytest.raises(trc_cuda.TrcCudaError, match="contiguous"):
+        trc_cuda.gguf_load_tensor_static(2, np.zeros((4, 18), dtype=np.uint8)[:, :9], torch.empty(64))

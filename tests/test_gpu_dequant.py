@@ -195,3 +195,22 @@ def test_rejections(tc):
     assert tc.lib().trc_cuda_dequant(10, blocks.data_ptr(), 1, out.data_ptr(), None) == -2
     assert tc.lib().trc_cuda_dequant(2, blocks.data_ptr(), -1, out.data_ptr(), None) == -1
     assert tc.lib().trc_cuda_dequant(2, blocks.data_ptr(), 0, out.data_ptr(), None) == 0
+
+
+def test_loader_wrappers_reject_bad_device_destinations(tc):
+    """A half/bf16 destination would be written past its end, a ragged or strided one partly:
+    the loader wrappers refuse them (and a device tensor passed as the host source)."""
+    host = torch.from_numpy(synth.random_blocks(synth.TYPE_Q4_0, 2, seed=3))
+    staging = torch.empty(64, dtype=torch.uint8, device="cuda")
+    bad = [torch.empty(64, dtype=torch.float16, device="cuda"), torch.empty(64, dtype=torch.bfloat16, device="cuda"),
+           torch.empty(48, device="cuda"), torch.empty(128, device="cuda")[::2]]
+    for dst in bad:
+        with pytest.raises(tc.TrcCudaError):
+            tc.gguf_load_tensor(synth.TYPE_Q4_0, host, dst, staging)
+        with pytest.raises(tc.TrcCudaError):
+            tc.gguf_load_tensor_static(synth.TYPE_Q4_0, host, dst)
+    with pytest.raises(tc.TrcCudaError, match="host memory"):
+        tc.gguf_load_tensor_static(synth.TYPE_Q4_0, host.cuda(), torch.empty(64, device="cuda"))
+    with pytest.raises(tc.TrcCudaError):
+        tc.gguf_tensor_to_f32(synth.TYPE_Q4_0, dev(host.numpy()), out=torch.empty(64, dtype=torch.float16, device="cuda"))
+    assert tc.device_error() == 0

@@ -155,6 +155,111 @@ trc_cuda_view view_of(const Tensor* t) {
     return v;
 }
 
+// ---------------------------------------------------------------- packed-weight buffers
+// A frozen quantized weight is an F32 graph tensor whose bytes are never backed: the buffer keeps
+// the packed GGUF blocks loaded into it, and Tensor::extra of the weight points at their
+// descriptor. Only mul_mat(W, x) and mul_mat(transpose(W), g) read it on the device (through the
+// dequant-in-prologue GEMM); tensor_get dequantizes.
+struct PackedWeight {
+    const Buffer* owner = nullptr;  // the buffer that holds the blocks
+    Type          type = TYPE_F32;  // Q4_0 .. Q8_0
+    int64_t       ne0 = 0, ne1 = 0; // the F32 tensor's extents (2-D)
+    void*         blocks = nullptr; // device memory: ne0 * ne1 / 32 blocks
+    size_t        bytes = 0;
+    size_t        capacity = 0;     // bytes allocated at `blocks`
+};
+
+class CudaPackedBufferType : public BufferType {
+public:
+    CudaPackedBufferType(CudaDevice* dev, int ordinal) : dev_(dev), ordinal_(ordinal) {
+        std::snprintf(name_, sizeof(name_), "CUDA%d_Q", ordinal);
+    }
+    Device* device() const override;
+    const char* name() const override { return name_; }
+    size_t alignment() const override { return 256; }
+    Buffer* alloc_buffer(size_t size) override;  // bookkeeping only: the blocks arrive with each load
+    CudaDevice* cuda_device() const { return dev_; }
+    int ordinal() const { return ordinal_; }
+
+private:
+    CudaDevice* dev_;
+    int         ordinal_;
+    char        name_[16];
+};
+
+Tensor* view_root(Tensor* t) {
+    while (t->view_src != nullptr) t = t->view_src;
+    return t;
+}
+const Tensor* view_root(const Tensor* t) {
+    while (t->view_src != nullptr) t = t->view_src;
+    return t;
+}
+
+class CudaPackedBuffer : public Buffer {
+public:
+    CudaPackedBuffer(CudaPackedBufferType* buft, size_t size) : buft_(buft), size_(size) {}
+    ~CudaPackedBuffer() override {
+        int prev = 0;
+        trc_cuda_rt_get_device(&prev);
+        trc_cuda_rt_set_device(buft_->ordinal());
+        for (auto& kv : weights_) trc_cuda_rt_free(kv.second->blocks);
+        trc_cuda_rt_set_device(prev);
+    }
+    BufferType* buffer_type() const override { return buft_; }
+    size_t size() const override { return size_; }
+    void* base() override { return nullptr; }
+    bool is_host() const override { return false; }
+
+    void set_tensor(Tensor* t, size_t, const void*, size_t) override {
+        CB_ABORT("%s: 张量 %s 是冻结的量化权重，只能载入 GGUF 量化块（cuda_gguf_load_tensor / "
+                 "cuda_set_tensor_from_quant）；本后端不做量化", buft_->name(), t->name);
+    }
+    void get_tensor(const Tensor* t, size_t offset, void* data, size_t size) const override;
+    void clear() override;
+
+    // Makes `bytes` of packed blocks (HOST memory) the data of root tensor t; false + log on a
+    // mismatch. Synchronous.
+    bool store(Tensor* t, Type type, const void* host, size_t bytes);
+
+    const PackedWeight* weight_of(const Tensor* root) const {
+        const auto it = weights_.find(root);
+        if (it == weights_.end() || root->extra != it->second.get()) return nullptr;
+        return it->second.get();
+    }
+
+private:
+    CudaPackedBufferType* buft_;
+    size_t                size_;
+    std::unordered_map<const Tensor*, std::unique_ptr<PackedWeight>> weights_;
+};
+
+CudaPackedBuffer* packed_buffer_of(const Tensor* t) {
+    if (t == nullptr) return nullptr;
+    const Tensor* r = view_root(t);
+    return r->buffer == nullptr ? nullptr : dynamic_cast<CudaPackedBuffer*>(r->buffer);
+}
+
+// How a graph operand refers to a packed weight: not at all, as W itself, as transpose(W) (the
+// two forms the GEMM reads), or through a view the GEMM cannot take.
+enum class PackedUse { none, plain, transposed, unsupported };
+
+PackedUse packed_use(const Tensor* t, const PackedWeight** w_out) {
+    CudaPackedBuffer* buf = packed_buffer_of(t);
+    if (buf == nullptr) return PackedUse::none;
+    const Tensor* r = view_root(t);
+    const PackedWeight* w = buf->weight_of(r);
+    if (w_out != nullptr) *w_out = w;
+    if (r->ne[2] != 1 || r->ne[3] != 1 || t->ne[2] != 1 || t->ne[3] != 1) return PackedUse::unsupported;
+    if (t->data_offset != r->data_offset && t != r) return PackedUse::unsupported;
+    const int64_t ne0 = r->ne[0], ne1 = r->ne[1];
+    if (t->ne[0] == ne0 && t->ne[1] == ne1 && t->nb[0] == 4 && t->nb[1] == static_cast<size_t>(4 * ne0))
+        return PackedUse::plain;
+    if (t->ne[0] == ne1 && t->ne[1] == ne0 && t->nb[1] == 4 && t->nb[0] == static_cast<size_t>(4 * ne0))
+        return PackedUse::transposed;
+    return PackedUse::unsupported;
+}
+
 bool all_f32(const Tensor* t) {
     if (t->type != TYPE_F32) return false;
     for (int i = 0; i < t->nsrc; ++i)
@@ -164,7 +269,7 @@ bool all_f32(const Tensor* t) {
 
 class CudaDevice : public Device {
 public:
-    explicit CudaDevice(int ordinal) : ordinal_(ordinal), buft_(this, ordinal) {
+    explicit CudaDevice(int ordinal) : ordinal_(ordinal), buft_(this, ordinal), packed_buft_(this, ordinal) {
         char name[256];
         int  major = 0, minor = 0;
         CB_CUDA(trc_cuda_rt_device_info(ordinal, name, sizeof(name), &major, &minor));
@@ -186,6 +291,9 @@ public:
 
     bool supports_op(const Tensor* t) const override {
         if (t == nullptr) return false;
+        const int reads_packed = packed_reads(t);
+        if (reads_packed < 0) return false;
+        if (reads_packed > 0) return t->op == OP_MUL_MAT && all_f32(t);  // the dequant-in-prologue GEMM
         switch (t->op) {
             case OP_NONE:
             case OP_RESHAPE:
@@ -269,6 +377,7 @@ public:
 
     int          ordinal() const { return ordinal_; }
     void*        stream() const { return stream_; }
+    BufferType*  packed_buffer_type() { return &packed_buft_; }
 
     // Device scratch, grown on demand (sum partials, GGUF staging). Stream-ordered use only.
     void* scratch(size_t bytes) {
@@ -283,6 +392,21 @@ public:
         return scratch_;
     }
 
+    // Pinned host staging for the single-tensor GGUF loader, grown on demand and kept for the
+    // device's lifetime (page-locking is a system call; a warm start loads hundreds of tensors).
+    // The caller synchronizes the stream before the next use.
+    void* pinned(size_t bytes) {
+        if (bytes > pinned_bytes_) {
+            CB_CUDA(trc_cuda_rt_stream_sync(stream_));
+            if (pinned_ != nullptr) CB_CUDA(trc_cuda_rt_free_host(pinned_));
+            pinned_ = nullptr;
+            pinned_bytes_ = 0;
+            CB_CUDA(trc_cuda_rt_malloc_host(&pinned_, bytes));
+            pinned_bytes_ = bytes;
+        }
+        return pinned_;
+    }
+
 private:
     void refresh_memory() {
         size_t free_b = 0, total_b = 0;
@@ -293,6 +417,32 @@ private:
             props_.memory_total = total_b;
         }
         trc_cuda_rt_set_device(prev);
+    }
+
+    // Whether node t reads a packed weight: 0 no; 1 as the first operand of a mul_mat in one of the
+    // two forms the dequant-in-prologue GEMM takes (W, or transpose(W)) with an ordinary second
+    // operand; -1 in any other way (no kernel of this device reads it so), or t itself lives on a
+    // packed buffer. Views of a packed weight compute nothing and count as 0.
+    static int packed_reads(const Tensor* t) {
+        switch (t->op) {
+            case OP_NONE:
+            case OP_RESHAPE:
+            case OP_VIEW:
+            case OP_PERMUTE:
+            case OP_TRANSPOSE:
+                return 0;
+            default:
+                break;
+        }
+        if (packed_buffer_of(t) != nullptr) return -1;
+        int found = 0;
+        for (int i = 0; i < t->nsrc; ++i) {
+            const PackedUse u = packed_use(t->src[i], nullptr);
+            if (u == PackedUse::none) continue;
+            if (t->op != OP_MUL_MAT || i != 0 || u == PackedUse::unsupported) return -1;
+            found = 1;
+        }
+        return found;
     }
 
     // ---------------------------------------------------------------- graph-level fusion
@@ -366,6 +516,14 @@ private:
     // ---------------------------------------------------------------- per-node execution
     void compute_node(Tensor* t) {
         if (skipped_.count(t) != 0) return;
+        const int reads_packed = packed_reads(t);
+        if (reads_packed < 0)
+            CB_ABORT("CUDA: 算子 %s（张量 %s）不能读取冻结的量化权重：只有 mul_mat(W, x) 与 "
+                     "mul_mat(transpose(W), g) 支持；请先用 graph_first_unsupported 预检", op_name(t->op), t->name);
+        if (reads_packed > 0) {
+            compute_packed_mul_mat(t);
+            return;
+        }
         switch (t->op) {
             case OP_NONE:
             case OP_RESHAPE:
@@ -509,6 +667,52 @@ private:
         }
     }
 
+    // mul_mat whose first operand is a packed weight W or transpose(W): the dequant-in-prologue GEMM
+    // (trc_cuda_mul_mat_q with TRC_CUDA_MM_FUSED), which decodes W's blocks inside the GEMM and
+    // writes no F32 copy of W. The graph-level fusion into grad_acc (dX of a parameter input)
+    // applies as for any mul_mat. Views the tensor-core kernel cannot address fall back to the
+    // dequant + SIMT kernel (W dequantized into stream-ordered scratch for that one product).
+    void compute_packed_mul_mat(Tensor* t) {
+        const PackedWeight* w = nullptr;
+        const PackedUse u = packed_use(t->src[0], &w);
+        if (w == nullptr)
+            CB_ABORT("CUDA: 冻结的量化权重 %s 尚未载入（cuda_gguf_load_tensor / cuda_set_tensor_from_quant）",
+                     view_root(t->src[0])->name);
+        const trc_cuda_view b = view_of(t->src[1]);
+        trc_cuda_view d;
+        uint32_t flags = mm_flags();
+        const auto it = fused_gemm_.find(t);
+        if (it == fused_gemm_.end()) {
+            d = view_of(t);
+        } else {
+            const Fused& f = it->second;
+            if (f.reduce) CB_ABORT("CUDA: 量化权重不会作为广播操作数（张量 %s）", t->name);
+            d = view_of(f.target);
+            if (f.transposed) {
+                std::swap(d.ne[0], d.ne[1]);
+                std::swap(d.nb[0], d.nb[1]);
+            }
+            if (f.accumulate) flags |= TRC_CUDA_MM_ACCUMULATE;
+        }
+        if ((flags & TRC_CUDA_MM_SIMT) == 0 && !packed_two_step()) flags |= TRC_CUDA_MM_FUSED;
+        const int tr = u == PackedUse::transposed ? 1 : 0;
+        int st = trc_cuda_mul_mat_q(static_cast<int>(w->type), w->blocks, w->ne0, w->ne1, tr, &b, &d, flags, stream_);
+        if (st == TRC_CUDA_EUNSUPPORTED)  // a view TMA cannot address: dequant + the SIMT kernel
+            st = trc_cuda_mul_mat_q(static_cast<int>(w->type), w->blocks, w->ne0, w->ne1, tr, &b, &d,
+                                    (flags & ~static_cast<uint32_t>(TRC_CUDA_MM_FUSED)) | TRC_CUDA_MM_SIMT, stream_);
+        CB_TRC(st, "trc_cuda_mul_mat_q (packed weight)");
+    }
+
+    // TRC_CUDA_PACKED_TWO_STEP=1: packed weights may take mul_mat_q's two-step path (W dequantized
+    // into scratch for one product) from 1024 columns on; by default no F32 copy of W is written.
+    static bool packed_two_step() {
+        static const bool on = [] {
+            const char* e = std::getenv("TRC_CUDA_PACKED_TWO_STEP");
+            return e != nullptr && *e != '\0' && *e != '0';
+        }();
+        return on;
+    }
+
     // TRC_CUDA_MM_SIMT=1 runs every mul_mat on the SIMT kernel, which sums in the reference's order,
     // so whole training runs can be compared bit for bit with the CPU device.
     static uint32_t mm_flags() {
@@ -521,10 +725,13 @@ private:
 
     int            ordinal_;
     CudaBufferType buft_;
+    CudaPackedBufferType packed_buft_;
     DeviceProps    props_;
     void*          stream_ = nullptr;
     void*          scratch_ = nullptr;
     size_t         scratch_bytes_ = 0;
+    void*          pinned_ = nullptr;
+    size_t         pinned_bytes_ = 0;
 };
 
 Device* CudaBufferType::device() const { return dev_; }
@@ -536,6 +743,78 @@ Buffer* CudaBufferType::alloc_buffer(size_t size) {
     void* p = nullptr;
     if (trc_cuda_rt_malloc(&p, size) != TRC_CUDA_OK) return nullptr;
     return new CudaBuffer(this, ordinal, static_cast<char*>(p), size);
+}
+
+Device* CudaPackedBufferType::device() const { return dev_; }
+
+Buffer* CudaPackedBufferType::alloc_buffer(size_t size) {
+    if (fake_alloc_failure()) return nullptr;
+    return new CudaPackedBuffer(this, size);
+}
+
+bool CudaPackedBuffer::store(Tensor* t, Type type, const void* host, size_t bytes) {
+    const size_t bb = trc_cuda_block_bytes(static_cast<int>(type));
+    if (t->buffer != this || t->view_src != nullptr) CB_ABORT("%s: 张量 %s 不是本 buffer 的根张量", buft_->name(), t->name);
+    if (bb == 0 || t->type != TYPE_F32 || !tensor_is_contiguous(t) || t->ne[2] != 1 || t->ne[3] != 1 ||
+        t->ne[0] % 32 != 0) {
+        std::fprintf(stderr, "[traincpp] %s: 张量 %s 须为二维连续 F32（ne0 为 32 的倍数），数据须为 Q4_0/Q4_1/Q5_0/Q5_1/Q8_0\n",
+                     buft_->name(), t->name);
+        return false;
+    }
+    if (static_cast<size_t>(tensor_nelements(t) / 32) * bb != bytes) {
+        std::fprintf(stderr, "[traincpp] %s: 张量 %s 的量化块字节数不符（%zu）\n", buft_->name(), t->name, bytes);
+        return false;
+    }
+    std::unique_ptr<PackedWeight>& slot = weights_[t];
+    if (!slot) slot = std::make_unique<PackedWeight>();
+    PackedWeight& w = *slot;
+    CB_CUDA(trc_cuda_rt_set_device(buft_->ordinal()));
+    const size_t want = (bytes + 255) / 256 * 256;
+    if (w.capacity < want) {
+        if (w.blocks != nullptr) CB_CUDA(trc_cuda_rt_free(w.blocks));
+        w.blocks = nullptr;
+        w.capacity = 0;
+        const int st = trc_cuda_rt_malloc(&w.blocks, want);
+        if (st != TRC_CUDA_OK) {
+            std::fprintf(stderr, "[traincpp] %s: 量化块显存分配失败（%zu 字节）\n", buft_->name(), want);
+            return false;
+        }
+        w.capacity = want;
+    }
+    CB_CUDA(trc_cuda_rt_memcpy(w.blocks, host, bytes, 0));
+    w.owner = this;
+    w.type = type;
+    w.ne0 = t->ne[0];
+    w.ne1 = t->ne[1];
+    w.bytes = bytes;
+    t->extra = &w;
+    return true;
+}
+
+void CudaPackedBuffer::get_tensor(const Tensor* t, size_t offset, void* data, size_t size) const {
+    const Tensor* r = view_root(t);
+    const PackedWeight* w = weight_of(r);
+    if (w == nullptr) CB_ABORT("%s: 张量 %s 尚未载入量化块", buft_->name(), r->name);
+    // the bytes asked for, as positions in the root's F32 layout (views address the root's bytes)
+    const size_t pos = t->data_offset - r->data_offset + offset;
+    if (pos + size > tensor_nbytes(r)) CB_ABORT("%s::get_tensor: 越界", buft_->name());
+    if (size == 0) return;
+    const int64_t b0 = static_cast<int64_t>(pos / 128), b1 = static_cast<int64_t>((pos + size + 127) / 128);
+    CudaDevice* dev = buft_->cuda_device();
+    CB_CUDA(trc_cuda_rt_set_device(buft_->ordinal()));
+    const size_t bb = trc_cuda_block_bytes(static_cast<int>(w->type));
+    float* tmp = static_cast<float*>(dev->scratch(static_cast<size_t>(b1 - b0) * 128));
+    CB_TRC(trc_cuda_dequant(static_cast<int>(w->type), static_cast<const uint8_t*>(w->blocks) + b0 * bb, b1 - b0, tmp,
+                            dev->stream()),
+           "trc_cuda_dequant (tensor_get of a packed weight)");
+    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
+    CB_CUDA(trc_cuda_rt_memcpy(data, reinterpret_cast<const char*>(tmp) + (pos - static_cast<size_t>(b0) * 128), size, 1));
+}
+
+void CudaPackedBuffer::clear() {
+    CB_CUDA(trc_cuda_rt_set_device(buft_->ordinal()));
+    for (auto& kv : weights_)  // all-zero blocks decode to 0.0f (scale 0)
+        if (kv.second->blocks != nullptr) CB_CUDA(trc_cuda_rt_memset(kv.second->blocks, 0, kv.second->bytes));
 }
 
 std::mutex& registry_mutex() {
@@ -585,6 +864,44 @@ int cuda_register_devices() {
     return registered;
 }
 
+BufferType* cuda_packed_buffer_type(int ordinal) {
+    Device* d = cuda_device(ordinal);
+    return d == nullptr ? nullptr : static_cast<CudaDevice*>(d)->packed_buffer_type();
+}
+
+bool cuda_tensor_is_packed(const Tensor* t) { return packed_buffer_of(t) != nullptr; }
+
+bool cuda_set_tensor_from_quant(Tensor* dst, Type type, const void* packed, size_t bytes) {
+    if (dst == nullptr || (packed == nullptr && bytes != 0)) CB_ABORT("cuda_set_tensor_from_quant: 参数为空");
+    if (CudaPackedBuffer* pb = packed_buffer_of(dst)) {
+        if (dst->view_src != nullptr) {
+            std::fprintf(stderr, "[traincpp] cuda_set_tensor_from_quant: 量化权重 %s 须按根张量载入\n", dst->name);
+            return false;
+        }
+        return pb->store(dst, type, packed, bytes);
+    }
+    CudaBuffer* buf = cuda_buffer_of(dst);
+    const size_t bb = trc_cuda_block_bytes(static_cast<int>(type));
+    if (buf == nullptr || bb == 0 || dst->type != TYPE_F32 || !tensor_is_contiguous(dst) ||
+        tensor_nelements(dst) % 32 != 0 || static_cast<size_t>(tensor_nelements(dst) / 32) * bb != bytes) {
+        std::fprintf(stderr, "[traincpp] cuda_set_tensor_from_quant: 张量 %s 须为 CUDA 上的连续 F32 张量，"
+                     "数据须为与元素数一致的 Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 块\n", dst->name);
+        return false;
+    }
+    if (bytes == 0) return true;
+    CB_CUDA(trc_cuda_rt_set_device(buf->ordinal()));
+    CudaDevice* dev = static_cast<CudaDevice*>(buf->buffer_type()->device());
+    void* staging = dev->scratch((bytes + 15) / 16 * 16);
+    float* out = reinterpret_cast<float*>(buf->device_ptr() + dst->data_offset);
+    CB_TRC(trc_cuda_load_quant(static_cast<int>(type), packed, tensor_nelements(dst) / 32, staging, out, dev->stream()),
+           "trc_cuda_load_quant");
+    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
+    int code = 0;
+    CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
+    if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
+    return true;
+}
+
 bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name, Tensor* dst) {
     if (f == nullptr || path == nullptr || name == nullptr || dst == nullptr)
         CB_ABORT("cuda_gguf_load_tensor: 参数为空");
@@ -595,7 +912,12 @@ bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name
     }
     const GgufTensorInfo* info = gguf_tensor_info(f, ti);
     CudaBuffer* buf = cuda_buffer_of(dst);
-    if (!is_legacy_quant(info->type) || dst->type != TYPE_F32 || buf == nullptr)
+    CudaPackedBuffer* pbuf = packed_buffer_of(dst);
+    if (pbuf != nullptr && !is_legacy_quant(info->type)) {
+        std::fprintf(stderr, "[traincpp] GGUF: 张量 %s 的类型 %s 不能载入量化权重 buffer\n", name, type_name(info->type));
+        return false;
+    }
+    if (pbuf == nullptr && (!is_legacy_quant(info->type) || dst->type != TYPE_F32 || buf == nullptr))
         return gguf_load_tensor(f, name, dst);  // the reference path (also reports its errors)
     // the reference's destination checks (src/io/trc_gguf.cpp:1060-1076)
     if (!tensor_is_contiguous(dst)) {
@@ -613,24 +935,23 @@ bool cuda_gguf_load_tensor(const GgufFile* f, const char* path, const char* name
         std::fprintf(stderr, "[traincpp] GGUF: 无法打开 %s\n", path);
         return false;
     }
-    void* host = nullptr;
-    CB_CUDA(trc_cuda_rt_set_device(buf->ordinal()));
-    CB_CUDA(trc_cuda_rt_malloc_host(&host, bytes));
+    CudaDevice* dev = static_cast<CudaDevice*>(pbuf != nullptr ? pbuf->buffer_type()->device()
+                                                               : buf->buffer_type()->device());
+    CB_CUDA(trc_cuda_rt_set_device(dev->ordinal()));
+    void* host = dev->pinned(bytes);  // reused across calls: no page-locking per tensor
     const long pos = static_cast<long>(gguf_data_offset(f) + info->offset);
     const bool ok = std::fseek(fp, pos, SEEK_SET) == 0 && std::fread(host, 1, bytes, fp) == bytes;
     std::fclose(fp);
     if (!ok) {
-        trc_cuda_rt_free_host(host);
         std::fprintf(stderr, "[traincpp] GGUF: 张量 %s 数据越界\n", name);
         return false;
     }
-    CudaDevice* dev = static_cast<CudaDevice*>(buf->buffer_type()->device());
+    if (pbuf != nullptr) return pbuf->store(dst, info->type, host, bytes);  // the blocks as they are
     void* staging = dev->scratch((bytes + 15) / 16 * 16);
     float* out = reinterpret_cast<float*>(buf->device_ptr() + dst->data_offset);
     CB_TRC(trc_cuda_load_quant(static_cast<int>(info->type), host, n_blocks, staging, out, dev->stream()),
            "trc_cuda_load_quant");
-    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
-    CB_CUDA(trc_cuda_rt_free_host(host));
+    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));  // the pinned and device staging are free again
     int code = 0;
     CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
     if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
@@ -673,6 +994,7 @@ bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* con
     };
     std::vector<Job> jobs;
     std::vector<size_t> fallback;  // tensors the reference loader handles (not quantized / not on CUDA)
+    std::vector<size_t> packed;    // destinations on a packed-weight buffer
     CudaDevice* dev = nullptr;
     for (size_t i = 0; i < count; ++i) {
         const int64_t ti = gguf_find_tensor(f, names[i]);
@@ -682,6 +1004,10 @@ bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* con
         }
         const GgufTensorInfo* info = gguf_tensor_info(f, ti);
         CudaBuffer* buf = cuda_buffer_of(dsts[i]);
+        if (packed_buffer_of(dsts[i]) != nullptr) {  // frozen quantized weight: its blocks as they are
+            packed.push_back(i);
+            continue;
+        }
         if ((!is_legacy_quant(info->type) && info->type != TYPE_F32) || dsts[i]->type != TYPE_F32 || buf == nullptr) {
             fallback.push_back(i);
             continue;
@@ -751,6 +1077,7 @@ bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* con
         CB_TRC(trc_cuda_device_error(&code, 1), "trc_cuda_device_error");
         if (code != 0) CB_ABORT("CUDA: dequant kernel 等待超时（设备错误码 %d）", code);
     }
+    for (const size_t i : packed) ok = ok && cuda_gguf_load_tensor(f, path, names[i], dsts[i]);
     for (const size_t i : fallback) ok = ok && gguf_load_tensor(f, names[i], dsts[i]);
     return ok;
 }

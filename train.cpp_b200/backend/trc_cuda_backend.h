@@ -51,6 +51,38 @@ std::vector<int64_t> gguf_shard_tensors(const GgufFile* f, int rank, int world);
 bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* const* names, Tensor* const* dsts,
                             size_t count, size_t staging_bytes = size_t(64) << 20);
 
+// ---- frozen quantized weights that never exist as F32 in device memory ----------------------
+//
+// A second buffer type of GPU `ordinal`, "CUDA<i>_Q", for frozen weights kept as their packed GGUF
+// blocks. Tensors allocated from it (buffer_alloc_ctx_tensors on a context holding only such
+// weights) stay ordinary F32 graph tensors, so train.cpp's op constructors, autograd and
+// nn::Linear accept them unchanged (mul_mat requires a->type == b->type, src/ops/trc_ops.cpp:368,
+// and quantized types are not allocatable, src/core/trc_types.cpp:104-118). Their F32 bytes are
+// never backed: the buffer holds, per weight, the packed blocks loaded into it, described by
+// Tensor::extra (include/traincpp/trc_tensor.h:62). The CUDA device runs mul_mat(W, x) and
+// mul_mat(transpose(W), g) -- a Linear's forward and its dX -- with the dequant-in-prologue GEMM,
+// which decodes the blocks inside the GEMM and writes no F32 copy of W anywhere. Rules:
+//   - a weight is 2-D (ne[2] = ne[3] = 1), F32-typed, with ne[0] a multiple of 32, and must be
+//     loaded (cuda_gguf_load_tensor, cuda_gguf_load_tensors or cuda_set_tensor_from_quant) before a
+//     graph reads it; the weight is frozen (its blocks change only by another load);
+//   - supports_op answers false for every node that would read a packed weight other than
+//     mul_mat with the weight (or its transpose) as the first operand, so graph_first_unsupported
+//     reports such graphs; tensor_get dequantizes (bit-exact with the reference's host
+//     dequantizers); tensor_set of F32 data is refused (the library does not quantize).
+// With TRC_CUDA_PACKED_TWO_STEP=1, products of 1024 or more columns may dequantize W into
+// stream-ordered scratch for the duration of one GEMM instead (same results, bit for bit).
+BufferType* cuda_packed_buffer_type(int ordinal = 0);
+
+// True when t (or the root of the view t) lives on a packed-weight buffer.
+bool cuda_tensor_is_packed(const Tensor* t);
+
+// The Buffer::set_tensor_from_quant hook of this backend: makes `bytes` of packed GGUF blocks of
+// `type` (HOST memory) the data of the F32 tensor `dst`. On a packed-weight buffer the blocks are
+// stored as they are; on an ordinary CUDA buffer they are uploaded and dequantized on the device
+// (bit-exact with the reference). Returns false (and logs) for a non-legacy type, a size that does
+// not match dst's element count, a non-contiguous dst, or a dst that is not on this backend.
+bool cuda_set_tensor_from_quant(Tensor* dst, Type type, const void* packed, size_t bytes);
+
 }  // namespace traincpp
 
 extern "C" {

@@ -3,6 +3,7 @@
 // CUDA runtime linked into libtrc_cuda.so.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "../../include/trc_cuda_runtime.h"
@@ -68,6 +69,10 @@ int trc_cuda_rt_malloc(void** ptr, size_t bytes) {
 
 int trc_cuda_rt_free(void* ptr) { return rt(cudaFree(ptr)); }
 
+static std::atomic<uint64_t> g_host_allocs{0};
+
+uint64_t trc_cuda_rt_host_alloc_count(void) { return g_host_allocs.load(std::memory_order_relaxed); }
+
 int trc_cuda_rt_malloc_host(void** ptr, size_t bytes) {
     if (ptr == nullptr) return TRC_CUDA_EINVAL;
     const cudaError_t e = cudaMallocHost(ptr, bytes == 0 ? 1 : bytes);
@@ -76,6 +81,7 @@ int trc_cuda_rt_malloc_host(void** ptr, size_t bytes) {
         *ptr = nullptr;
         return TRC_CUDA_ENOMEM;
     }
+    if (e == cudaSuccess) g_host_allocs.fetch_add(1, std::memory_order_relaxed);
     return rt(e);
 }
 

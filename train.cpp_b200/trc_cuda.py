@@ -175,6 +175,21 @@ def block_bytes(qtype: int) -> int:
     return int(lib().trc_cuda_block_bytes(qtype))
 
 
+def _check_f32_dst(dst: torch.Tensor, what: str, n_weights: int | None = None) -> None:
+    """The kernels write 32 floats per block at dst.data_ptr(): dst must be a contiguous float32
+    CUDA tensor of whole blocks (and of n_weights elements when that is given)."""
+    if dst.dtype != torch.float32:
+        raise TrcCudaError(f"{what}: destination must be float32, got {dst.dtype}")
+    if not dst.is_cuda:
+        raise TrcCudaError(f"{what}: destination must be a CUDA tensor (device memory)")
+    if not dst.is_contiguous():
+        raise TrcCudaError(f"{what}: destination must be contiguous")
+    if dst.numel() % QK != 0:
+        raise TrcCudaError(f"{what}: {dst.numel()} weights are not a whole number of 32-weight blocks")
+    if n_weights is not None and dst.numel() < n_weights:
+        raise TrcCudaError(f"{what}: destination holds {dst.numel()} floats, the tensor has {n_weights}")
+
+
 def gguf_tensor_to_f32(qtype: int, blocks: torch.Tensor, n_elems: int | None = None,
                        out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """Device dequantization of packed legacy blocks (uint8 CUDA tensor) to F32, bit-exact with the
@@ -193,6 +208,7 @@ def gguf_tensor_to_f32(qtype: int, blocks: torch.Tensor, n_elems: int | None = N
         raise TrcCudaError("packed buffer is smaller than the tensor")
     if out is None:
         out = torch.empty(n_blocks * QK, dtype=torch.float32, device=blocks.device)
+    _check_f32_dst(out, "gguf_tensor_to_f32", n_blocks * QK)
     _check(lib().trc_cuda_dequant(qtype, blocks.data_ptr(), n_blocks, out.data_ptr(), _stream(stream)),
            "trc_cuda_dequant")
     return out
@@ -317,14 +333,27 @@ def dequantize_to_peers(jobs: Sequence[tuple[int, torch.Tensor, torch.Tensor]], 
                                                 _stream(stream)), "trc_cuda_dequant_many_to_peers")
 
 
+def _host_bytes(host_blocks) -> tuple[int, int]:
+    """Address and size of packed blocks in HOST memory (a contiguous CPU tensor or numpy array)."""
+    if isinstance(host_blocks, torch.Tensor):
+        if host_blocks.is_cuda or not host_blocks.is_contiguous():
+            raise TrcCudaError("packed blocks must be a contiguous tensor in host memory")
+        return host_blocks.data_ptr(), host_blocks.numel() * host_blocks.element_size()
+    if not host_blocks.flags["C_CONTIGUOUS"]:
+        raise TrcCudaError("packed blocks must be a contiguous array")
+    return host_blocks.ctypes.data, host_blocks.nbytes
+
+
 def gguf_load_tensor(qtype: int, host_blocks, dst: torch.Tensor, staging: torch.Tensor, stream=None) -> None:
     """Device-side gguf_load_tensor for a quantized file tensor and an F32 destination: uploads the
     packed HOST bytes (numpy array or CPU tensor, pinned for an asynchronous copy) into `staging`
     and dequantizes into `dst`."""
-    if isinstance(host_blocks, torch.Tensor):
-        ptr, nbytes = host_blocks.data_ptr(), host_blocks.numel() * host_blocks.element_size()
-    else:
-        ptr, nbytes = host_blocks.ctypes.data, host_blocks.nbytes
+    ptr, nbytes = _host_bytes(host_blocks)
+    _check_f32_dst(dst, "gguf_load_tensor")
+    if staging.dtype != torch.uint8 or not staging.is_cuda or not staging.is_contiguous():
+        raise TrcCudaError("gguf_load_tensor: staging must be a contiguous uint8 CUDA tensor")
+    if block_bytes(qtype) == 0:
+        raise TrcCudaError(f"gguf_load_tensor: type {qtype} is not a legacy quantized type")
     n_blocks = dst.numel() // QK
     if nbytes < n_blocks * block_bytes(qtype) or staging.numel() < n_blocks * block_bytes(qtype):
         raise TrcCudaError("host or staging buffer smaller than the tensor")
@@ -340,10 +369,10 @@ def gguf_load_tensor_static(qtype: int, host_blocks, dst: torch.Tensor, stream=N
     """gguf_load_tensor without a staging buffer and without any allocation: the packed bytes are
     staged in the library's fixed 64 MiB device array (for callers that cannot allocate device
     memory). Tensors larger than that are rejected; calls overlapping on the GPU race on the array."""
-    if isinstance(host_blocks, torch.Tensor):
-        ptr, nbytes = host_blocks.data_ptr(), host_blocks.numel() * host_blocks.element_size()
-    else:
-        ptr, nbytes = host_blocks.ctypes.data, host_blocks.nbytes
+    ptr, nbytes = _host_bytes(host_blocks)
+    _check_f32_dst(dst, "gguf_load_tensor_static")
+    if block_bytes(qtype) == 0:
+        raise TrcCudaError(f"gguf_load_tensor_static: type {qtype} is not a legacy quantized type")
     n_blocks = dst.numel() // QK
     if nbytes < n_blocks * block_bytes(qtype):
         raise TrcCudaError("host buffer smaller than the tensor")
@@ -547,10 +576,13 @@ def sm_count() -> int:
 
 
 def exported_symbols() -> list[str]:
-    """Names declared in include/trc_cuda.h (parsed), used by the CPU symbol test."""
-    hdr = PKG.parent / "include" / "trc_cuda.h"
+    """Names of the functions declared in include/trc_cuda.h and include/trc_cuda_runtime.h
+    (parsed), used by the CPU symbol test."""
     import re
-    names = re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b(trc_cuda_\w+)\s*\(", hdr.read_text(), flags=re.M)
+    names: list[str] = []
+    for hdr in ("trc_cuda.h", "trc_cuda_runtime.h"):
+        text = (PKG.parent / "include" / hdr).read_text()
+        names += re.findall(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b(trc_cuda_\w+)\s*\(", text, flags=re.M)
     return sorted(set(names))
 
 
