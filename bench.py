@@ -767,15 +767,50 @@ def run_gather(tc, torch, rank, world, barrier, max_over_ranks, args) -> dict:
             "steps": reps}
 
 
+def tf32_ceiling(tc, torch, barrier, max_over_ranks) -> dict:
+    """The tcgen05 kind::tf32 ceiling measured here (trc_cuda_tf32_mma_probe): the GEMM's MMA stream
+    alone -- three MMAs per K=8 from shared memory into TMEM, no loads, no split, no epilogue -- on
+    CTA pairs (the GEMM's default) and on single CTAs. Best of 5 timed launches of ~5 ms after 2
+    warm-ups, CUDA events on the launching stream, max over ranks."""
+    stream = torch.cuda.current_stream()
+    out = {}
+    for cg, key in ((2, "pair"), (1, "single_cta")):
+        iters = 8000
+        for _ in range(2):
+            tc.tf32_mma_probe(cg, iters)
+        torch.cuda.synchronize()
+        barrier()
+        best = None
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            flops = tc.tf32_mma_probe(cg, iters)
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+        ms = max_over_ranks(best)
+        out[key + "_tf32_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+    assert tc.device_error() == 0
+    out["tf32x3_tflops"] = round(out["pair_tf32_tflops"] / 3, 1)
+    out["note"] = ("tcgen05 kind::tf32 MMA stream of the GEMM's main loop alone (CTA pairs, 256x256x8, "
+                   "3 MMAs per K=8); tf32x3 = pair rate / 3, F32 FLOPs counted once")
+    return out
+
+
 def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, args) -> dict:
     """Fused Linear step (Q5_0 4096x14336, 2048 tokens) per rank, and the GQA batched broadcast
-    forward + backward with ne[3] planes sharded across ranks. TFLOP/s count 2*K*M*N once."""
+    forward + backward with ne[3] planes sharded across ranks. TFLOP/s count 2*K*M*N once. Each
+    fraction is given against two ceilings: half the measured bf16 rate / 3 (derived), and the
+    tcgen05 TF32 MMA rate measured by the probe in the same run / 3."""
     stream = torch.cuda.current_stream()
     gen = torch.Generator(device="cuda").manual_seed(11 + rank)
     reps, warm = max(3, min(args.steps, 10)), max(3, args.warmup)
     tf32x3_peak = None  # derived: TF32 = half the bf16 rate, 3 passes
     if peaks.get("bf16_tflops"):
         tf32x3_peak = peaks["bf16_tflops"] / 2 / 3
+    ceiling = tf32_ceiling(tc, torch, barrier, max_over_ranks)
+    measured_x3 = ceiling["tf32x3_tflops"]
 
     def timed(fn):
         for _ in range(warm):
@@ -797,6 +832,7 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
     K, M, N = 4096, 14336, 2048
     if only == "gqa":
         K = 0
+    out["tf32_mma_ceiling"] = ceiling
     if K == 0:
         return gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out)
     wq = torch.from_numpy(synth.random_blocks(synth.TYPE_Q5_0, K * M // 32, seed=21 + rank)).cuda()
@@ -821,9 +857,11 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         "dw_tflops": round(flops / t_dw / 1e9, 2), "step_ms": round(step_ms, 4),
         "step_tflops": round(world * 3 * flops / step_ms / 1e9, 2),
         "frac_of_3xtf32_peak": round(3 * flops / step_ms / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
+        "frac_of_measured_tf32x3": round(3 * flops / step_ms / 1e9 / measured_x3, 4),
         "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
         "path": "mul_mat_q from packed W: dequant into pooled scratch + F32 tcgen05 kernel (N >= 1024), timed together",
-        "fused_kernel": {"fwd_tflops": round(flops / t_fwd_fused / 1e9, 2), "dx_tflops": round(flops / t_dx_fused / 1e9, 2)},
+        "fused_kernel": {"fwd_tflops": round(flops / t_fwd_fused / 1e9, 2), "dx_tflops": round(flops / t_dx_fused / 1e9, 2),
+                         "frac_of_measured_tf32x3": round(2 * flops / (t_fwd_fused + t_dx_fused) / 1e9 / measured_x3, 4)},
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         out["linear_q5_0"]["cpu_reference"] = linear_cpu_rates(tc, torch, wq, K, M, X, dY)
@@ -834,6 +872,7 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
 
 
 def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> dict:
+    measured_x3 = out["tf32_mma_ceiling"]["tf32x3_tflops"]
     """GQA batched broadcast, planes of ne[3] sharded across ranks."""
     p3 = args.gqa_p3 if getattr(args, "gqa_p3", 0) else max(1, 8 // world)
     A = torch.randn((p3, 8, 2048, 128), generator=gen, device="cuda")
@@ -853,6 +892,7 @@ def gqa_workload(tc, torch, rank, world, timed, gen, tf32x3_peak, args, out) -> 
         "db_tflops": round(world * gflop / t_b / 1e9, 2), "step_ms": round(t_f + t_a + t_b, 4),
         "step_tflops": round(world * 3 * gflop / (t_f + t_a + t_b) / 1e9, 2),
         "frac_of_3xtf32_peak": round(3 * gflop / (t_f + t_a + t_b) / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
+        "frac_of_measured_tf32x3": round(3 * gflop / (t_f + t_a + t_b) / 1e9 / measured_x3, 4),
         "shape": f"A [128,2048,8,{p3}] . B [128,2048,32,{p3}] per rank (ne[3] sharded over {world})",
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -879,17 +919,19 @@ def check_linear_slices(tc, torch, wq, K, M, X, dY, world: int) -> None:
     Xj, dYj = X[j].cpu().numpy(), dY[j].cpu().numpy()
     want_y = oracle.mul_mat(Wn, Xj, n_threads=threads)[0, 0]
     want_dx = oracle.mul_mat(np.ascontiguousarray(Wn.T), dYj, n_threads=threads)[0, 0]
+    Y = torch.empty((N, M), device="cuda")
+    dX = torch.empty((N, K), device="cuda")
     for fused in (False, True):
-        Y = tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, fused=fused)
-        dX = tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, fused=fused)
-        e_y, e_dx = _normwise(Y[j].cpu().numpy(), want_y), _normwise(dX[j].cpu().numpy(), want_dx)
+        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, fused=fused)
+        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, fused=fused)
+        e_y, e_dx = _normwise(Y.cpu().numpy()[j], want_y), _normwise(dX.cpu().numpy()[j], want_dx)
         assert e_y <= 1e-5 and e_dx <= 1e-5, f"Linear step parity (fused={fused}): fwd {e_y:.2e}, dX {e_dx:.2e}"
     dW = torch.zeros((M, K), device="cuda")
     tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True)
     k = np.arange(3, K, K // 16)[:16]
     want_dw = oracle.mul_mat(np.ascontiguousarray(dY.cpu().numpy().T), np.ascontiguousarray(X.cpu().numpy().T[k]),
                              n_threads=threads)[0, 0]
-    e_dw = _normwise(dW[:, k].t().cpu().numpy(), want_dw)
+    e_dw = _normwise(dW.cpu().numpy()[:, k].T, want_dw)
     assert e_dw <= 1e-5, f"Linear step parity: dW {e_dw:.2e}"
     assert tc.device_error() == 0
 

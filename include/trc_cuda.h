@@ -341,6 +341,14 @@ int trc_cuda_stream_probe(const void* in, void* out, int64_t n_in16, int ratio, 
  * multiple of 256. */
 int trc_cuda_stream_probe_bulk(const void* in, void* out, int64_t n_in16, int ratio, void* stream);
 
+/* The tcgen05 kind::tf32 ceiling: one CTA per SM (cta_group = 1, 128 x 256 x 8 MMAs) or one CTA pair
+ * per two SMs (cta_group = 2, 256 x 256 x 8 MMAs) issues `iters` K=16 steps of the 3xTF32 GEMM's
+ * main loop -- three MMAs per K=8 from shared-memory operands into an fp32 TMEM accumulator -- with
+ * no loads, operand split or epilogue. FLOPs per launch (each MMA counted):
+ * iters x 6 x 2 x 128 x 256 x 8 x (number of CTAs). bench.py times it with CUDA events to state
+ * every GEMM as a fraction of what the tensor pipe delivers here. iters in 1 .. 2^22. */
+int trc_cuda_tf32_mma_probe(int cta_group, int iters, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

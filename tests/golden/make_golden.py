@@ -18,6 +18,7 @@ Three fixture files, all small:
 from __future__ import annotations
 
 import struct
+import os
 import sys
 from pathlib import Path
 
@@ -123,4 +124,10 @@ def main(ref_dir: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) > 1:
+        src = Path(sys.argv[1])
+    elif os.environ.get("TRC_REFERENCE_DIR"):
+        src = Path(os.environ["TRC_REFERENCE_DIR"])
+    else:
+        sys.exit("usage: make_golden.py <train.cpp source dir>  (or set TRC_REFERENCE_DIR)")
+    main(src)

@@ -22,7 +22,7 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU_SOURCES = ["capi.cu", "runtime.cu", "dequant.cu", "elementwise.cu", "mul_mat_simt.cu", "gemm_tf32x3.cu",
-              "static_staging.cu", "train_ops.cu"]
+              "static_staging.cu", "train_ops.cu", "probe_tc.cu"]
 
 
 def _run(cmd: list[str], log: Path | None = None) -> None:
@@ -57,8 +57,17 @@ def build_cuda(force: bool = False) -> Path:
 
 
 def reference_dir() -> Path | None:
-    d = Path(os.environ.get("TRC_REFERENCE_DIR", "/root/reference"))
-    return d if (d / "include" / "traincpp" / "trc_backend.h").exists() else None
+    """The train.cpp source tree: $TRC_REFERENCE_DIR, else a checkout named `reference` beside this
+    repository. None (with a note on stderr) when neither holds train.cpp's headers; the parts that
+    compile against them (the C++ backend, the reference's CPU library, the drop-in test program)
+    are then skipped and their prebuilt files, if any, are used."""
+    env = os.environ.get("TRC_REFERENCE_DIR")
+    d = Path(env) if env else ROOT.parent / "reference"
+    if (d / "include" / "traincpp" / "trc_backend.h").exists():
+        return d
+    sys.stderr.write(f"build: no train.cpp source tree at {d} (set TRC_REFERENCE_DIR); "
+                     "skipping the parts built against it\n")
+    return None
 
 
 def build_backend(force: bool = False) -> Path | None:

@@ -101,6 +101,7 @@ def lib() -> ctypes.CDLL:
         "trc_cuda_selftest_wait_timeout": (I, [ctypes.c_uint64, ctypes.POINTER(I)]),
         "trc_cuda_stream_probe": (I, [P, P, I64, I, P]),
         "trc_cuda_stream_probe_bulk": (I, [P, P, I64, I, P]),
+        "trc_cuda_tf32_mma_probe": (I, [I, I, P]),
         "trc_cuda_sum_rows": (I, [VP, VP, I, P]),
         "trc_cuda_opt_step_adamw": (I, [P, P, P, P, I64, P, P]),
         "trc_cuda_opt_step_sgd": (I, [P, P, P, I64, P, P]),
@@ -558,6 +559,14 @@ def stream_probe(src: torch.Tensor, dst: torch.Tensor, ratio: int, stream=None, 
         raise TrcCudaError("stream_probe: destination too small")
     fn = lib().trc_cuda_stream_probe_bulk if bulk else lib().trc_cuda_stream_probe
     _check(fn(src.data_ptr(), dst.data_ptr(), n16, ratio, _stream(stream)), "trc_cuda_stream_probe")
+
+
+def tf32_mma_probe(cta_group: int, iters: int, stream=None) -> float:
+    """Launches the tcgen05 kind::tf32 ceiling probe; returns the FLOPs the launch executes (every
+    MMA counted: divide by 3 for the 3xTF32 rate with F32 FLOPs counted once)."""
+    _check(lib().trc_cuda_tf32_mma_probe(cta_group, iters, _stream(stream)), "trc_cuda_tf32_mma_probe")
+    ctas = sm_count() if cta_group == 1 else 2 * (sm_count() // 2)
+    return float(iters) * 6 * 2 * 128 * 256 * 8 * ctas
 
 
 def selftest_wait_timeout(limit_ns: int) -> bool:
