@@ -67,21 +67,24 @@ def test_fused_split_k_fills_the_last_wave(tc, one_cta):
 
 
 def test_fused_transposed_split_k_four_parts(tc):
-    """dX's kind of product, transpose(W) . dY, on 75 pair tiles: split in four parts (two into D,
-    two into a workspace added afterwards), deterministic and within the bar."""
-    qtype, w_ne0, w_ne1, n = synth.TYPE_Q5_0, 3840, 1024, 1280   # A = T(W): M 3840, K 1024
+    """dX's kind of product, transpose(W) . dY, on 75 pair tiles of 256 k-blocks: split in four parts
+    (two into D, two into a workspace added afterwards), deterministic and within the bar (all of it
+    against float64, 64 columns against the oracle)."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q5_0, 3840, 4096, 1280   # A = T(W): M 3840, K 4096
     blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=83)
     Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
     dy = (np.random.default_rng(84).standard_normal((n, w_ne1)) * 1e-2).astype(np.float32)
-    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2), dy)
     torch.cuda.synchronize()
     n0 = tc.launch_count()
     got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True)
     assert tc.launch_count() - n0 == 3  # B's tails, the GEMM and the workspace add
-    got = got.cpu().numpy()
+    want64 = (dev(dy).double() @ dev(Wf).double()).cpu().numpy()
+    got = got.cpu().numpy().reshape(n, w_ne0)
     again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True).cpu().numpy()
     assert tc.device_error() == 0
-    assert normwise(got, want.reshape(got.shape)) <= 1e-5
+    assert normwise(got, want64) <= 5e-6
+    want = oracle.mul_mat(np.ascontiguousarray(Wf.T), dy[:64])[0, 0]
+    assert normwise(got[:64], want) <= 1e-5
     assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))
 
 
@@ -172,3 +175,30 @@ def test_cfg1_cpu_runnable_config_in_full(tc):
     assert normwise(two_step, want) <= 1e-5
     assert normwise(fused, want) <= 1e-5
     assert tc.device_error() == 0
+
+
+@pytest.mark.parametrize("qtype", [synth.TYPE_Q4_0, synth.TYPE_Q4_1, synth.TYPE_Q5_0, synth.TYPE_Q5_1, synth.TYPE_Q8_0])
+@pytest.mark.parametrize("transposed", [False, True], ids=["W", "WT"])
+def test_fused_tma_staged_and_global_load_paths_agree(tc, qtype, transposed):
+    """On CTA pairs the fused kernel stages each stage's packed bytes by TMA when the packed rows are
+    16-byte aligned; otherwise its split warps load them from global memory. The same blocks at an
+    aligned and at a 2-byte-offset address take the two paths: bit-identical results, ragged M/K
+    (zero-filled rows and columns), within the bar of the reference."""
+    w_ne0, w_ne1, n = 512, 300, 72                      # 16 blocks per row: aligned row pitch for every type
+    bb = synth.BLOCK_BYTES[qtype]
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=120 + qtype)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    K = w_ne1 if transposed else w_ne0
+    x = np.random.default_rng(121).standard_normal((n, K)).astype(np.float32)
+    want = oracle.mul_mat(np.swapaxes(Wf, -1, -2) if transposed else Wf, x)
+    aligned = dev(blocks)
+    raw = torch.zeros(blocks.size + 16, dtype=torch.uint8, device="cuda")
+    raw[2:2 + blocks.size] = aligned
+    shifted = raw[2:2 + blocks.size]                    # 2 bytes off the 16-byte grid
+    assert aligned.data_ptr() % 16 == 0 and shifted.data_ptr() % 16 == 2
+    outs = [tc.mul_mat_q(qtype, wb, w_ne0, w_ne1, dev(x), transposed=transposed, fused=True).cpu().numpy()
+            for wb in (aligned, shifted)]
+    assert tc.device_error() == 0
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert normwise(outs[0], want.reshape(outs[0].shape)) <= 1e-5
+    assert bb in (18, 20, 22, 24, 34)

@@ -95,15 +95,19 @@ constexpr int MAX_STAGES    = 6;
 // A tile and a 256-row B tile. CG = 2 (tcgen05 cta_group::2): a cluster of two CTAs computes a
 // 256 x 256 tile; each CTA stages its own 128 rows of A and 128 of the 256 rows of B, and the
 // leader's MMA reads both CTAs' shared memory, so each SM stages and splits half the B bytes.
-template <int CG>
+// PQ > 0: the fused kernel's stages also hold PQ bytes of the weight's packed blocks, loaded by TMA
+// (the slot follows the tiles; one stage fewer fits).
+template <int CG, int PQ = 0>
 struct Geo {
     static constexpr int BN_CTA      = BN / CG;                     // B rows staged by one CTA
-    static constexpr int STAGES      = CG == 2 ? 6 : 4;
+    static constexpr int STAGES      = CG == 2 ? (PQ ? 5 : 6) : 4;
     static constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
     static constexpr int B_BYTES     = BN_CTA * BK * 4;             // 16 KiB (CG 1) / 8 KiB (CG 2)
-    static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);     // raw + tail
+    static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES) + PQ;  // raw + tail (+ packed A)
     static constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES;
     static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;
+    static constexpr int OFF_PQ      = 2 * (A_BYTES + B_BYTES);
+    static_assert(PQ % 1024 == 0 && (PQ == 0 || CG == 2), "packed slot: 1 KiB multiples, CTA pairs only");
     static constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
     static constexpr int EPI_OFF     = STAGES * STAGE_BYTES;
     static constexpr int SMEM_BYTES  = EPI_OFF + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + 256 /*barriers*/;
@@ -247,6 +251,32 @@ constexpr int OFF_A_RAW = 0, OFF_A_TAIL = BM * BK * 4;
 // quads read adjacent bytes of the packed rows, so a warp's loads touch few cache lines.
 constexpr int A_QUADS = BM * BK / 4;
 
+// TMA staging of the packed weight (CTA pairs): per stage one 2-D box of the packed rows, uint8
+// elements, starting at a 16-byte-aligned column x (the TMA rule for the innermost coordinate) at or
+// below the first needed byte; the needed bytes then start at an even offset o <= 14 into each box
+// row (block sizes are even), and the box is wide enough for o + the needed bytes.
+//   K-major (A = W): 128 W rows x the one block holding the stage's 16 weights of each row.
+//   MN-major (A = transpose(W)): 16 W rows (the stage's K) x the 4 blocks of the tile's 128 columns.
+// Rows or bytes outside the tensor arrive as zeros.
+template <int QTYPE, int QTRANS>
+struct PackedBox {
+    static constexpr int kBB    = QuantTraits<QTYPE>::kBytes;
+    static constexpr int kNeed  = QTRANS ? 4 * kBB : kBB;
+    static constexpr int kW     = (14 + kNeed + 15) / 16 * 16;   // box width in bytes
+    static constexpr int kH     = QTRANS ? BK : BM;              // box rows
+    static constexpr int kBytes = kW * kH;
+    static constexpr int kSlot  = (kBytes + 1023) / 1024 * 1024;
+    static_assert(kW <= 256, "TMA box width");
+};
+template <int QTYPE, int QTRANS, int PT>
+struct PackedSlot {
+    static constexpr int value = 0;
+};
+template <int QTYPE, int QTRANS>
+struct PackedSlot<QTYPE, QTRANS, 1> {
+    static constexpr int value = QTYPE == 0 ? 0 : PackedBox<QTYPE == 0 ? 2 : QTYPE, QTRANS>::kSlot;
+};
+
 // Per tile: the packed-row pointer of quad q (K-major: its W row; MN-major: its K-row offset and
 // block column), nullptr when the quad's rows lie outside the matrix.
 template <int QTYPE, int QTRANS>
@@ -319,12 +349,16 @@ __device__ __forceinline__ void store_quad_head_tail(uint8_t* st, int off, const
 // its own `full` barrier; its split warps then arrive on the leader's `split` barrier, the leader's
 // single thread issues the pair's MMAs and commits them to both CTAs' `empty` / `acc_full`
 // barriers, and both CTAs' epilogue warps arrive on the leader's `acc_empty`.
-template <int QTYPE, int QTRANS, int CG>
+// PT = 1 (fused kernel on CTA pairs): the producer also stages each stage's packed weight bytes by
+// TMA through tmA (a uint8 map of the packed rows), and the split warps decode from shared memory;
+// PT = 0: the split warps load the packed words from global memory themselves.
+template <int QTYPE, int QTRANS, int CG, int PT = 0>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmD,
                        const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TcParams p) {
-    using G = Geo<CG>;
+    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value>;
+    constexpr bool PTMA = QTYPE != 0 && PT != 0;
     constexpr bool PAIR = CG == 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -346,7 +380,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         mbar_init(&bars->mma_done, 1);
         fence_barrier_init();
-        if (QTYPE == 0) prefetch_tmap(&tmA);
+        if (QTYPE == 0 || PTMA) prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
         if (p.b_pretail) prefetch_tmap(&tmBt);
         if (p.tma_store) prefetch_tmap(&tmD);
@@ -382,9 +416,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!mbar_wait_scoped<PAIR>(&bars->empty[s], ph ^ 1u, TRC_DEVERR_WAIT_EMPTY)) { ok = false; break; }
                     const uint32_t st = smem_base + s * G::STAGE_BYTES;
+                    constexpr int pq_tx = PTMA ? PackedBox<QTYPE, QTRANS>::kBytes : 0;
                     mbar_arrive_expect_tx(&bars->full[s], (QTYPE == 0 ? G::RAW_TX_BYTES : G::B_BYTES) +
-                                                              (p.b_pretail ? G::B_BYTES : 0));
+                                                              (p.b_pretail ? G::B_BYTES : 0) + pq_tx);
                     const int k0 = kb * BK;
+                    if constexpr (PTMA) {
+                        // the stage's packed bytes: from the 16-byte boundary at or below the first one
+                        constexpr int bbq = QuantTraits<QTYPE>::kBytes;
+                        const int blk = QTRANS ? (am0 >> 5) : (k0 >> 5);
+                        tma_load_4d(st + G::OFF_PQ, &tmA, &bars->full[s], (blk * bbq) & ~15, QTRANS ? k0 : am0, 0, 0);
+                    }
                     if constexpr (QTYPE == 0) {
                         if (!p.a_mn) {
                             tma_load_4d(st + G::OFF_A_RAW, &tmA, &bars->full[s], k0, am0, a2, a3);
@@ -491,7 +532,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(&bars->split[s], 0));
             else mbar_arrive(&bars->split[s]);
         };
-        if constexpr (QTYPE != 0) {
+        if constexpr (PTMA) {
+            // Fused kernel, packed bytes staged by TMA: once the stage has landed, each thread decodes
+            // its A quads (2 per thread) from the stage's packed box into the head + tail tiles.
+            constexpr int NT = SPLIT_WARPS * 32;
+            constexpr int QPT = A_QUADS / NT;
+            static_assert(A_QUADS % NT == 0, "quads per thread");
+            using PB = PackedBox<QTYPE, QTRANS>;
+            int qoff[QPT];
+#pragma unroll
+            for (int i = 0; i < QPT; ++i) qoff[i] = quad_offset<QTRANS>(t + NT * i);
+            const int row_off = BM * static_cast<int>(rank);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
+                const UnitSpan us = unit_span(p, unit);
+                const int am0 = tile_coord<CG>(p, us.tile).m0 + row_off;
+                for (int kb = us.kv0; kb < us.kv1; ++kb, ++it) {
+                    const int s = it % G::STAGES;
+                    if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * G::STAGE_BYTES;
+                    const int k0 = kb * BK;
+                    const int blk = QTRANS ? (am0 >> 5) : (k0 >> 5);
+                    const uint8_t* box = st + G::OFF_PQ + ((blk * PB::kBB) & 15);
+#pragma unroll
+                    for (int i = 0; i < QPT; ++i) {
+                        const int q = t + NT * i;
+                        float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        // rows outside the matrix are zero-filled by TMA; they are written as +0 here
+                        // exactly as the F32 operand's zero fill reads
+                        const uint8_t* bp;
+                        int j0;
+                        bool valid;
+                        if constexpr (QTRANS == 0) {
+                            bp = box + (q >> 2) * PB::kW;
+                            j0 = (k0 & 16) + 4 * (q & 3);
+                            valid = am0 + (q >> 2) < p.M;
+                        } else {
+                            bp = box + (q >> 5) * PB::kW + ((q & 31) >> 3) * PB::kBB;
+                            j0 = (q & 7) * 4;
+                            valid = k0 + (q >> 5) < p.K && am0 + 32 * ((q & 31) >> 3) < p.M;
+                        }
+                        if (valid) {
+                            QuadWords wd;
+                            load_quad_words<QTYPE>(bp, j0, wd);
+                            decode_quad_words<QTYPE>(wd, j0, w);
+                        }
+                        store_quad_head_tail(st, qoff[i], w);
+                    }
+                    if (!p.b_pretail) split_chunks<G, (nAll - nA + NT - 1) / NT>(st, nA + t, nAll, NT, nA);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) arrive_split(s);
+                }
+            }
+        } else if constexpr (QTYPE != 0) {
             // Fused kernel: the split warps decode the stage's A quads (up to 2 per thread) from
             // the packed blocks into head + tail tiles, then split the TMA-loaded B tile. The packed
             // words are loaded two stages ahead of their decode (a stage takes about one loaded L2
@@ -945,6 +1043,40 @@ bool make_pretail(const trc_cuda_view& B, int box_rows, bool b_mn, bool b_tma5, 
     return true;
 }
 
+// Tensor map of a packed weight for the fused kernel's TMA staging: uint8 elements, the packed
+// rows (row_bytes each, `rows` of them) as a 2-D tensor, the box of PackedBox for the type and
+// orientation. False when TMA cannot address it (base or row pitch not 16-byte multiples).
+bool encode_packed(const void* blocks, int64_t row_bytes, int64_t rows, int type, bool transposed, CUtensorMap& map) {
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr || (reinterpret_cast<uint64_t>(blocks) & 15u) != 0 || row_bytes % 16 != 0 || row_bytes <= 0 ||
+        rows <= 0 || row_bytes * rows >= (int64_t(1) << 40))
+        return false;
+    int w = 0, h = 0;
+    switch (type) {
+#define TRC_PB(T)                                                                                                  \
+    case T:                                                                                                        \
+        w = transposed ? PackedBox<T, 1>::kW : PackedBox<T, 0>::kW;                                                \
+        h = transposed ? PackedBox<T, 1>::kH : PackedBox<T, 0>::kH;                                                \
+        break;
+        TRC_PB(2)
+        TRC_PB(3)
+        TRC_PB(6)
+        TRC_PB(7)
+        TRC_PB(8)
+#undef TRC_PB
+        default: return false;
+    }
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows), 1, 1};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(row_bytes * rows),
+                                   static_cast<cuuint64_t>(row_bytes * rows)};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(w), static_cast<cuuint32_t>(h), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(blocks), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // True when the view's elements fill a gap-free byte range starting at d.data (a permutation of a
 // contiguous tensor); `bytes` receives its size.
 bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
@@ -960,14 +1092,14 @@ bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
 }
 
 // Persistent launch: one CTA per SM (CG = 1) or one CTA pair per two SMs (CG = 2, a cluster of 2).
-template <int QTYPE, int QTRANS, int CG>
+template <int QTYPE, int QTRANS, int CG, int PT = 0>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBt, const CUtensorMap& tmD,
               const CUtensorMap& tmW, const TcParams& p, cudaStream_t stream) {
-    using G = Geo<CG>;
+    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value>;
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
     static int        max_pairs[64] = {};
-    auto kernel = tf32x3_gemm_kernel<QTYPE, QTRANS, CG>;
+    auto kernel = tf32x3_gemm_kernel<QTYPE, QTRANS, CG, PT>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -1056,8 +1188,14 @@ struct SplitPlan {
 // Split K when it shortens the schedule. The persistent grid runs the units in waves of one unit
 // per CTA (or CTA pair), and a tile count just above a multiple of the grid leaves most of the last
 // wave idle: 256 tiles on 74 pairs take 4 waves for 3.46 waves of work. Cutting every tile's
-// reduction into s parts gives s times the units at 1/s the length each. The plan takes 2 parts,
-// then 4, each only when it shortens the waves' total length by at least 5 %.
+// reduction into s parts gives s times the units at 1/s the length each, but every unit also pays a
+// fixed cost (filling and draining the pipeline, storing or reduce-adding its tile, and with four
+// parts the workspace pass). The plan takes the part count s in {1, 2, 4} whose schedule is
+// shortest, costed as waves(s) x (k-blocks per part + kUnitCostKb), and splits only when that is at
+// least 1 % shorter than not splitting. kUnitCostKb = 12 k-blocks is fitted to timings on B200:
+// 4 parts lengthen the GQA dB at one ne[3] plane (256 tiles of 128 k-blocks on 148 SMs) by a
+// quarter although its waves shrink from 2 to 1.75, and shorten the Linear dX (128 tiles of 896
+// k-blocks on 74 pairs) by 7 %.
 // The result never depends on the order in which parts land:
 // - two parts reduce-add into a D zeroed here: 0 + a + b = 0 + b + a;
 // - with four, parts 0 and 1 go to D and parts 2 and 3 to the workspace, and finish_split() adds
@@ -1073,16 +1211,21 @@ int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& 
     size_t dense_bytes = 0;
     if (accumulate || !p.tma_store || slots <= 0 || p.kv_blocks < 2 * CHUNK_KB || !dense_extent(d, dense_bytes))
         return TRC_CUDA_OK;
-    // the schedule's length in tile-lengths, and each part's k-blocks (no part may be empty)
-    auto length = [&](int s) { return double((s * p.total_tiles + slots - 1) / slots) / s; };
+    // each part's k-blocks (no part may be empty), and the schedule's length in k-blocks
+    constexpr int kUnitCostKb = 12;
     auto per_part = [&](int s) { return ((p.kv_blocks + s - 1) / s + CHUNK_KB - 1) / CHUNK_KB * CHUNK_KB; };
+    auto length = [&](int s) {
+        return double((s * p.total_tiles + slots - 1) / slots) * double((s == 1 ? p.kv_blocks : per_part(s)) + kUnitCostKb);
+    };
+    const double unsplit = length(1);
     int parts = 1;
-    double best = length(1);
-    if (length(2) <= 0.95 * best) {
+    double best = unsplit;
+    if (length(2) <= 0.99 * unsplit) {
         parts = 2;
         best = length(2);
     }
-    if (p.kv_blocks >= 4 * CHUNK_KB && 3 * per_part(4) < p.kv_blocks && length(4) <= 0.95 * best) {
+    if (p.kv_blocks >= 4 * CHUNK_KB && 3 * per_part(4) < p.kv_blocks && length(4) <= 0.99 * unsplit &&
+        length(4) < best) {
         retain_pool_once();
         if (cudaMallocAsync(&sp.ws, dense_bytes, stream) != cudaSuccess) {
             cudaGetLastError();
@@ -1274,9 +1417,19 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     if (want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
     const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
 
+    // CTA pairs stage the packed bytes by TMA where the packed rows allow a tensor map (16-byte
+    // aligned base and row pitch); otherwise the split warps load them from global memory.
+    const bool ptma = CG == 2 && encode_packed(w_blocks, p.q_row_bytes, w_ne1, type, a_transposed != 0, tmA);
     int st = TRC_CUDA_EUNSUPPORTED;
 #define TRC_Q_CASE(T)                                                                                 \
     case T:                                                                                           \
+        if constexpr (CG == 2) {                                                                      \
+            if (ptma) {                                                                               \
+                st = a_transposed ? launch_tc<T, 1, 2, 1>(tmA, tmB, tmBt, tmD, tmW, p, stream)        \
+                                  : launch_tc<T, 0, 2, 1>(tmA, tmB, tmBt, tmD, tmW, p, stream);       \
+                break;                                                                                \
+            }                                                                                         \
+        }                                                                                             \
         st = a_transposed ? launch_tc<T, 1, CG>(tmA, tmB, tmBt, tmD, tmW, p, stream)                  \
                           : launch_tc<T, 0, CG>(tmA, tmB, tmBt, tmD, tmW, p, stream);                 \
         break;
