@@ -557,14 +557,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     uint8_t* st = smem + s * G::STAGE_BYTES;
                     const int k0 = kb * BK;
                     const int blk = QTRANS ? (am0 >> 5) : (k0 >> 5);
-                    const uint8_t* box = st + G::OFF_PQ + ((blk * PB::kBB) & 15);
+                    const uint32_t box = smem_u32(st + G::OFF_PQ) + ((blk * PB::kBB) & 15);
 #pragma unroll
                     for (int i = 0; i < QPT; ++i) {
                         const int q = t + NT * i;
                         float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                         // rows outside the matrix are zero-filled by TMA; they are written as +0 here
                         // exactly as the F32 operand's zero fill reads
-                        const uint8_t* bp;
+                        uint32_t bp;
                         int j0;
                         bool valid;
                         if constexpr (QTRANS == 0) {
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                         if (valid) {
                             QuadWords wd;
-                            load_quad_words<QTYPE>(bp, j0, wd);
+                            load_quad_words_smem<QTYPE>(bp, j0, wd);
                             decode_quad_words<QTYPE>(wd, j0, w);
                         }
                         store_quad_head_tail(st, qoff[i], w);

@@ -57,6 +57,31 @@ __device__ __forceinline__ void load_quad_words(const uint8_t* blk, int j0, Quad
     }
 }
 
+// load_quad_words for a block in shared memory, addressed by its shared-window address (explicit
+// ld.shared: a generic pointer into shared memory loses its address space through the kernel's
+// aligned-pointer arithmetic and would be loaded with generic loads).
+__device__ __forceinline__ uint32_t lds_u16(uint32_t saddr) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(saddr));
+    return v;
+}
+
+template <int TYPE>
+__device__ __forceinline__ void load_quad_words_smem(uint32_t blk, int j0, QuadWords& r) {
+    r.d = lds_u16(blk);
+    if constexpr (TYPE == 8) {
+        r.q0 = lds_u16(blk + 2 + 2 * (j0 >> 1));
+        r.q1 = lds_u16(blk + 4 + 2 * (j0 >> 1));
+    } else {
+        constexpr int qs = QuantTraits<TYPE>::kQs;
+        r.q0 = lds_u16(blk + qs + 2 * ((j0 & 15) >> 1));
+        r.q1 = lds_u16(blk + qs + 2 + 2 * ((j0 & 15) >> 1));
+        if constexpr (TYPE == 3 || TYPE == 7) r.m = lds_u16(blk + 2);
+        if constexpr (TYPE == 6) r.qh = lds_u16(blk + 2 + 2 * (j0 >> 4));
+        if constexpr (TYPE == 7) r.qh = lds_u16(blk + 4 + 2 * (j0 >> 4));
+    }
+}
+
 // Decode weights j0 .. j0+3 from their raw words, exactly as the reference's dequantizers do:
 // - the four codes are gathered into the four bytes of one word (Q5: the high bit of weight e is
 //   moved to bit 4 of byte e by one multiply, whose partial products fall in disjoint bits; Q8_0:
