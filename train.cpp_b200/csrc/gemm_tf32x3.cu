@@ -352,6 +352,10 @@ __device__ __forceinline__ void store_quad_head_tail(uint8_t* st, int off, const
 // PT = 1 (fused kernel on CTA pairs): the producer also stages each stage's packed weight bytes by
 // TMA through tmA (a uint8 map of the packed rows), and the split warps decode from shared memory;
 // PT = 0: the split warps load the packed words from global memory themselves.
+// The TMA-staged fused decode splits its warps into kPtGroups groups that take alternate stages,
+// so one group's waits, fence and arrival overlap the other group's decode.
+constexpr int kPtGroups = 2;
+
 template <int QTYPE, int QTRANS, int CG, int PT = 0>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -371,7 +375,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < G::STAGES; ++s) {
             mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->split[s], SPLIT_WARPS * CG);
+            mbar_init(&bars->split[s], (SPLIT_WARPS / (PTMA ? kPtGroups : 1)) * CG);
             mbar_init(&bars->empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -533,15 +537,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else mbar_arrive(&bars->split[s]);
         };
         if constexpr (PTMA) {
-            // Fused kernel, packed bytes staged by TMA: once the stage has landed, each thread decodes
-            // its A quads (2 per thread) from the stage's packed box into the head + tail tiles.
-            constexpr int NT = SPLIT_WARPS * 32;
+            // Fused kernel, packed bytes staged by TMA: once the stage has landed, each thread of the
+            // stage's warp group decodes its A quads from the stage's packed box into the head + tail
+            // tiles. Group g (warps g*4 .. g*4+3 of the split warps) takes the stages it with
+            // it % kPtGroups == g.
+            constexpr int NT = SPLIT_WARPS * 32 / kPtGroups;
             constexpr int QPT = A_QUADS / NT;
             static_assert(A_QUADS % NT == 0, "quads per thread");
             using PB = PackedBox<QTYPE, QTRANS>;
+            const int group = t / NT, tg = t - group * NT;
             int qoff[QPT];
 #pragma unroll
-            for (int i = 0; i < QPT; ++i) qoff[i] = quad_offset<QTRANS>(t + NT * i);
+            for (int i = 0; i < QPT; ++i) qoff[i] = quad_offset<QTRANS>(tg + NT * i);
             const int row_off = BM * static_cast<int>(rank);
             uint32_t it = 0;
             bool ok = true;
@@ -549,6 +556,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const UnitSpan us = unit_span(p, unit);
                 const int am0 = tile_coord<CG>(p, us.tile).m0 + row_off;
                 for (int kb = us.kv0; kb < us.kv1; ++kb, ++it) {
+                    if (static_cast<int>(it % kPtGroups) != group) continue;
                     const int s = it % G::STAGES;
                     if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
                         ok = false;
@@ -560,7 +568,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t box = smem_u32(st + G::OFF_PQ) + ((blk * PB::kBB) & 15);
 #pragma unroll
                     for (int i = 0; i < QPT; ++i) {
-                        const int q = t + NT * i;
+                        const int q = tg + NT * i;
                         float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                         // rows outside the matrix are zero-filled by TMA; they are written as +0 here
                         // exactly as the F32 operand's zero fill reads
@@ -583,7 +591,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                         store_quad_head_tail(st, qoff[i], w);
                     }
-                    if (!p.b_pretail) split_chunks<G, (nAll - nA + NT - 1) / NT>(st, nA + t, nAll, NT, nA);
+                    if (!p.b_pretail) split_chunks<G, (nAll - nA + NT - 1) / NT>(st, nA + tg, nAll, NT, nA);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) arrive_split(s);
