@@ -772,6 +772,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // pair on the last row tile): nothing to add or store, and no store box starts outside D
             const int n_groups = dm0 < p.M ? (n_valid + 31) / 32 : 0;
             const int c_begin = 4 * team, c_end = min(n_groups, 4 * team + 4);
+            // the final store goes by 16-column groups (two per 32-column group of the promotion)
+            const int n_groups16 = dm0 < p.M ? (n_valid + 15) / 16 : 0;
+            const int g_begin = 8 * team, g_end = min(n_groups16, 8 * team + 8);
             const uint32_t t_addr = tmem_base + lane_off + tb * BN;
             const uint32_t x_addr = tmem_base + lane_off + xb * BN;
             uses_t = tb ? uses1 : uses0;
@@ -808,37 +811,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (!ok) break;
 #pragma unroll 1
-            for (int c = c_begin; c < c_end; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_addr + c * 32, r);
+            for (int g = g_begin; g < g_end; ++g) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(t_addr + g * 16, r);
                 tmem_ld_wait();
                 if (p.tma_store) {
-                    // Stage the 128 x 32 group column-major (each column's 128 rows contiguous, the
-                    // layout of the TMA box) and let the team leader store or reduce-add it.
-                    if (gcount > 0) {
-                        if (team_leader) bulk_wait_group_read<0>();  // the previous store has read the buffer
+                    // Stage the 128 x 16 group column-major (each column's 128 rows contiguous, the
+                    // layout of the TMA box) in one of the team's two staging halves, and let the team
+                    // leader store or reduce-add it. A half is refilled once the store issued two
+                    // groups earlier has read it, so one store is always in flight while the next
+                    // group is staged.
+                    float* sb = reinterpret_cast<float*>(stage_buf) + (gcount & 1u) * (BM * 16);
+                    if (gcount >= 2) {
+                        if (team_leader) bulk_wait_group_read<1>();  // the store of group gcount - 2 has read sb
                         named_barrier_sync(team_bar, 128);
                     }
-                    float* sb = reinterpret_cast<float*>(stage_buf);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) sb[e * BM + row] = __uint_as_float(r[e]);
+                    for (int e = 0; e < 16; ++e) sb[e * BM + row] = __uint_as_float(r[e]);
                     fence_proxy_async_smem();
                     named_barrier_sync(team_bar, 128);
                     if (team_leader) {
-                        const uint32_t src = smem_u32(stage_buf);
+                        const uint32_t src = smem_u32(sb);
                         // parts 2 and 3 of a four-part split-K product go to the workspace
                         if (unit >= 2 * p.total_tiles)
-                            tma_reduce_add_4d(&tmW, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                            tma_reduce_add_4d(&tmW, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
                         else if (p.accumulate || p.splits > 1)
-                            tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
-                        else tma_store_4d(&tmD, src, dm0, tc.n0 + c * 32, tc.p2, tc.p3);
+                            tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
+                        else tma_store_4d(&tmD, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
                         bulk_commit_group();
                     }
                     ++gcount;
                 } else if (m < p.M) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const int n = tc.n0 + c * 32 + e;
+                    for (int e = 0; e < 16; ++e) {
+                        const int n = tc.n0 + g * 16 + e;
                         if (n < p.N) {
                             float* o = reinterpret_cast<float*>(drow + static_cast<int64_t>(n) * p.d_sn);
                             const float v = __uint_as_float(r[e]);
@@ -976,7 +982,7 @@ bool encode_output(void* data, int64_t M, int64_t N, int64_t P2, int64_t P3, int
         strides[2] = (strides[1] * dims[2] + 15) / 16 * 16;
     }
     if (strides[1] >= (cuuint64_t(1) << 40) || strides[2] >= (cuuint64_t(1) << 40)) return false;
-    const cuuint32_t box[4]  = {BM, 32, 1, 1};
+    const cuuint32_t box[4]  = {BM, 16, 1, 1};  // the epilogue's 128 x 16 staging group
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     auto enc = tensor_map_encoder();
     if (enc == nullptr) return false;
