@@ -856,12 +856,13 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True)
     torch.cuda.synchronize()
     dW.zero_()
-    # mul_mat_q's default at 2048 tokens: W dequantized into scratch, then the F32 kernel (the
-    # dequant is inside the timed call); the fused dequant-in-prologue kernel is timed beside it
+    # mul_mat_q's default for this weight: the fused dequant-in-prologue kernel (packed bytes staged
+    # by TMA; no F32 copy of W anywhere). Its two-step path (W dequantized into scratch inside the
+    # timed call, then the F32 kernel) is timed beside it.
     t_fwd = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y))
     t_dx = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX))
-    t_fwd_fused = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, fused=True))
-    t_dx_fused = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, fused=True))
+    t_fwd_two = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, two_step=True))
+    t_dx_two = timed(lambda: tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, two_step=True))
     # dW for an F32 LoRA-style copy: dW^T = mul_mat(T(dY), T(X)) accumulated into the grad buffer
     t_dw = timed(lambda: tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True))
     step_ms = t_fwd + t_dx + t_dw
@@ -873,9 +874,9 @@ def run_gemm_workloads(tc, torch, rank, world, barrier, max_over_ranks, peaks, a
         "frac_of_3xtf32_peak": round(3 * flops / step_ms / 1e9 / tf32x3_peak, 4) if tf32x3_peak else None,
         "frac_of_measured_tf32x3": round(3 * flops / step_ms / 1e9 / measured_x3, 4),
         "shape": "W q5_0 [4096,14336], X [4096,2048], dY [14336,2048]; replicas per rank",
-        "path": "mul_mat_q from packed W: dequant into pooled scratch + F32 tcgen05 kernel (N >= 1024), timed together",
-        "fused_kernel": {"fwd_tflops": round(flops / t_fwd_fused / 1e9, 2), "dx_tflops": round(flops / t_dx_fused / 1e9, 2),
-                         "frac_of_measured_tf32x3": round(2 * flops / (t_fwd_fused + t_dx_fused) / 1e9 / measured_x3, 4)},
+        "path": "mul_mat_q from packed W (default): fused dequant-in-prologue tcgen05 kernel, packed bytes staged by TMA",
+        "two_step": {"fwd_tflops": round(flops / t_fwd_two / 1e9, 2), "dx_tflops": round(flops / t_dx_two / 1e9, 2),
+                     "path": "W dequantized into pooled scratch + F32 tcgen05 kernel, timed together"},
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         out["linear_q5_0"]["cpu_reference"] = linear_cpu_rates(tc, torch, wq, K, M, X, dY)
@@ -935,11 +936,11 @@ def check_linear_slices(tc, torch, wq, K, M, X, dY, world: int) -> None:
     want_dx = oracle.mul_mat(np.ascontiguousarray(Wn.T), dYj, n_threads=threads)[0, 0]
     Y = torch.empty((N, M), device="cuda")
     dX = torch.empty((N, K), device="cuda")
-    for fused in (False, True):
-        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, fused=fused)
-        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, fused=fused)
+    for two_step in (False, True):
+        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, two_step=two_step)
+        tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, two_step=two_step)
         e_y, e_dx = _normwise(Y.cpu().numpy()[j], want_y), _normwise(dX.cpu().numpy()[j], want_dx)
-        assert e_y <= 1e-5 and e_dx <= 1e-5, f"Linear step parity (fused={fused}): fwd {e_y:.2e}, dX {e_dx:.2e}"
+        assert e_y <= 1e-5 and e_dx <= 1e-5, f"Linear step parity (two_step={two_step}): fwd {e_y:.2e}, dX {e_dx:.2e}"
     dW = torch.zeros((M, K), device="cuda")
     tc.mul_mat(dY.t(), X.t(), out=dW.t(), accumulate=True)
     k = np.arange(3, K, K // 16)[:16]

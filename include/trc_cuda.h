@@ -173,14 +173,18 @@ enum {
     TRC_CUDA_MM_ONE_CTA    = 4u, /* tcgen05 kernel with one CTA per 128 x 256 tile (cta_group::1); the
                                     default runs 256 x 256 tiles on CTA pairs (cta_group::2, a cluster
                                     of two SMs sharing the B tile) when M spans more than 128 rows */
-    TRC_CUDA_MM_NO_PRETAIL = 8u, /* fused trc_cuda_mul_mat_q: split B into TF32 head and tail inside
-                                    every tile instead of once before the launch (the default computes
+    TRC_CUDA_MM_NO_PRETAIL = 8u, /* fused trc_cuda_mul_mat_q whose split warps load the packed words
+                                    from global memory (single CTAs, or packed rows that are not
+                                    16-byte aligned): split B into TF32 head and tail inside every tile
+                                    instead of once before the launch (by default that kernel computes
                                     B's tails in one pass into stream-ordered scratch when B is reused
-                                    by two or more row tiles; same results) */
-    TRC_CUDA_MM_FUSED      = 16u /* trc_cuda_mul_mat_q: always run the fused dequant-in-prologue
-                                    kernel, which allocates no copy of W. By default, from 1024
-                                    columns of b on, W is dequantized into stream-ordered scratch and
-                                    the F32 kernel runs instead: faster there, the same results */
+                                    by two or more row tiles; same results). The TMA-staged fused
+                                    kernel always splits B in the loop */
+    TRC_CUDA_MM_FUSED      = 16u, /* trc_cuda_mul_mat_q: always run the fused dequant-in-prologue
+                                     kernel, which allocates no copy of W (the default wherever the
+                                     packed bytes can be staged by TMA; see trc_cuda_mul_mat_q) */
+    TRC_CUDA_MM_TWO_STEP   = 32u  /* trc_cuda_mul_mat_q: dequantize W into stream-ordered scratch, then
+                                     run the F32 kernel (same results as the fused kernel) */
 };
 
 /* ggml mul_mat: for every plane (i2, i3) of b,
@@ -221,13 +225,16 @@ int trc_cuda_mul_mat_kernel(const trc_cuda_view* a, const trc_cuda_view* b, cons
  * (the dX = W^T dY product of the backward). Two implementations, with the same results (W
  * dequantized bit-exactly, then the same tile and split-K plan of the tensor-core kernel):
  *   - fused: the GEMM's split warps decode the blocks into shared memory, and the F32 weight never
- *     exists in HBM. Used when b has fewer than 1024 columns, with TRC_CUDA_MM_FUSED, or when
- *     the scratch below cannot be allocated;
+ *     exists in HBM. On CTA pairs (more than 128 rows of a) with 16-byte aligned packed rows the
+ *     producer stages each stage's packed bytes by TMA; on B200 (Q5_0 4096 x 14336, 2048
+ *     columns) that kernel is faster than the two steps below (forward ~228 vs ~220 TFLOP/s, dX
+ *     ~235 vs ~222). The default wherever it applies, below 1024 columns, with TRC_CUDA_MM_FUSED,
+ *     and when the scratch below cannot be allocated;
  *   - two steps: W is dequantized into stream-ordered scratch from the device's memory pool
- *     (w_ne0 * w_ne1 * 4 bytes, freed on the stream), then trc_cuda_mul_mat runs. On B200 at
- *     2048 columns this is 12-20 % faster than the fused kernel: the dequant pass costs about
- *     88 / N of the GEMM, less than the fused kernel's in-loop decode. With TRC_CUDA_MM_SIMT the
- *     product is the SIMT kernel's, so the whole call is bit-exact with the reference. */
+ *     (w_ne0 * w_ne1 * 4 bytes, freed on the stream), then trc_cuda_mul_mat runs. The default from
+ *     1024 columns on where the fused kernel cannot stage the packed bytes by TMA (there the two
+ *     steps are faster), and with TRC_CUDA_MM_TWO_STEP. With TRC_CUDA_MM_SIMT the product is the
+ *     SIMT kernel's, so the whole call is bit-exact with the reference. */
 int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
                        const trc_cuda_view* b, const trc_cuda_view* d, uint32_t flags, void* stream);
 

@@ -111,6 +111,7 @@ def test_mul_mat_flag_values_match_header():
     assert int(flags["TRC_CUDA_MM_SIMT"]) == trc_cuda.MM_SIMT
     assert int(flags["TRC_CUDA_MM_ONE_CTA"]) == trc_cuda.MM_ONE_CTA
     assert int(flags["TRC_CUDA_MM_FUSED"]) == trc_cuda.MM_FUSED
+    assert int(flags["TRC_CUDA_MM_TWO_STEP"]) == trc_cuda.MM_TWO_STEP
 
 
 def test_loader_wrappers_reject_bad_destinations_on_host():

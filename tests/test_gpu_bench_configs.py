@@ -1,10 +1,10 @@
 """GPU parity on the exact GEMM configurations bench.py times, at their full sizes.
 
   * The Linear training step (Q5_0 weight ne=[4096,14336], 2048 tokens), through the same calls as
-    the bench: mul_mat_q's default forward (W dequantized into scratch, then the F32 kernel),
-    dX = transpose(W) . dY (K = 14336, split-K in four parts), the fused dequant-in-prologue kernel
-    for both, and dW for an F32 copy of W accumulated (ACCUMULATE) through the transposed view of
-    its gradient buffer on top of a nonzero start.
+    the bench: mul_mat_q's default (the fused dequant-in-prologue kernel) and its two-step path (W
+    dequantized into scratch, then the F32 kernel) for the forward and for dX = transpose(W) . dY
+    (K = 14336, split-K in four parts), and dW for an F32 copy of W accumulated (ACCUMULATE) through
+    the transposed view of its gradient buffer on top of a nonzero start.
   * The GQA batched broadcast step (A ne=[128,2048,8,p3], B ne=[128,2048,32,p3]) at p3 = 8 (one
     GPU) and p3 = 1 (one ne[3] plane per rank at 8 GPUs; another tile and split-K plan): forward,
     the plane-reducing dA and dB.
@@ -64,11 +64,11 @@ def linear(tc):
     return wq, W, X, dY, Wn
 
 
-@pytest.mark.parametrize("fused", [False, True], ids=["two_step", "fused"])
-def test_linear_forward_full_size(tc, linear, fused):
+@pytest.mark.parametrize("two_step", [False, True], ids=["default_fused", "two_step"])
+def test_linear_forward_full_size(tc, linear, two_step):
     wq, W, X, _, Wn = linear
     Y = torch.full((N, M), float("nan"), device="cuda")
-    tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, fused=fused)
+    tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, X, out=Y, two_step=two_step)
     torch.cuda.synchronize()
     assert tc.device_error() == 0
     assert err64(Y, X.double() @ W.double().t()) <= TOL_EXACT
@@ -80,20 +80,20 @@ def test_linear_forward_full_size(tc, linear, fused):
         assert normwise(got, oracle.ref_mul_mat(Wn, False, X[j[:8]].cpu().numpy(), False)[0, 0]) <= TOL_REF
 
 
-@pytest.mark.parametrize("fused", [False, True], ids=["two_step", "fused"])
-def test_linear_dx_full_size(tc, linear, fused):
-    """dX = mul_mat(transpose(W), dY): K = 14336, 4096 x 2048 outputs (64 pair tiles of 256 x 256
-    after the orientation swap), which the planner splits in four parts (two reduce into dX, two
-    into a workspace added by one more kernel)."""
+@pytest.mark.parametrize("two_step", [False, True], ids=["default_fused", "two_step"])
+def test_linear_dx_full_size(tc, linear, two_step):
+    """dX = mul_mat(transpose(W), dY): K = 14336, 4096 x 2048 outputs (128 pair tiles of 256 x 256),
+    which the planner splits in four parts (two reduce into dX, two into a workspace added by one
+    more kernel)."""
     wq, W, _, dY, Wn = linear
     dX = torch.full((N, K), float("nan"), device="cuda")
     torch.cuda.synchronize()
     n0 = tc.launch_count()
-    tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, fused=fused)
+    tc.mul_mat_q(synth.TYPE_Q5_0, wq, K, M, dY, transposed=True, out=dX, two_step=two_step)
     torch.cuda.synchronize()
     launched = tc.launch_count() - n0
-    # two steps: dequant, GEMM, workspace add; fused: B's tails, GEMM, workspace add
-    assert launched == 3, launched
+    # two steps: dequant, GEMM, workspace add; fused: GEMM, workspace add
+    assert launched == (3 if two_step else 2), launched
     assert tc.device_error() == 0
     assert err64(dX, dY.double() @ W.double()) <= TOL_EXACT
     j = cols(N, 64, 2)

@@ -694,7 +694,7 @@ private:
             }
             if (f.accumulate) flags |= TRC_CUDA_MM_ACCUMULATE;
         }
-        if ((flags & TRC_CUDA_MM_SIMT) == 0 && !packed_two_step()) flags |= TRC_CUDA_MM_FUSED;
+        if ((flags & TRC_CUDA_MM_SIMT) == 0) flags |= packed_two_step() ? TRC_CUDA_MM_TWO_STEP : TRC_CUDA_MM_FUSED;
         const int tr = u == PackedUse::transposed ? 1 : 0;
         int st = trc_cuda_mul_mat_q(static_cast<int>(w->type), w->blocks, w->ne0, w->ne1, tr, &b, &d, flags, stream_);
         if (st == TRC_CUDA_EUNSUPPORTED)  // a view TMA cannot address: dequant + the SIMT kernel
@@ -703,8 +703,8 @@ private:
         CB_TRC(st, "trc_cuda_mul_mat_q (packed weight)");
     }
 
-    // TRC_CUDA_PACKED_TWO_STEP=1: packed weights may take mul_mat_q's two-step path (W dequantized
-    // into scratch for one product) from 1024 columns on; by default no F32 copy of W is written.
+    // TRC_CUDA_PACKED_TWO_STEP=1: packed weights take mul_mat_q's two-step path (W dequantized into
+    // scratch for one product; same bits); by default no F32 copy of W is ever written.
     static bool packed_two_step() {
         static const bool on = [] {
             const char* e = std::getenv("TRC_CUDA_PACKED_TWO_STEP");

@@ -69,8 +69,8 @@ bool cuda_gguf_load_tensors(const GgufFile* f, const char* path, const char* con
 //     mul_mat with the weight (or its transpose) as the first operand, so graph_first_unsupported
 //     reports such graphs; tensor_get dequantizes (bit-exact with the reference's host
 //     dequantizers); tensor_set of F32 data is refused (the library does not quantize).
-// With TRC_CUDA_PACKED_TWO_STEP=1, products of 1024 or more columns may dequantize W into
-// stream-ordered scratch for the duration of one GEMM instead (same results, bit for bit).
+// With TRC_CUDA_PACKED_TWO_STEP=1, every product dequantizes W into stream-ordered scratch for the
+// duration of one GEMM instead (same results, bit for bit).
 BufferType* cuda_packed_buffer_type(int ordinal = 0);
 
 // True when t (or the root of the view t) lives on a packed-weight buffer.

@@ -140,7 +140,7 @@ int mul_mat_q_two_step(int type, const void* w_blocks, int64_t w_ne0, int64_t w_
         a.nb[0] = a_transposed ? 4 * w_ne0 : 4;
         a.nb[1] = a_transposed ? 4 : 4 * w_ne0;
         a.nb[2] = a.nb[3] = 4 * n;
-        st = trc_cuda_mul_mat(&a, &b, &d, flags & ~(TRC_CUDA_MM_FUSED | TRC_CUDA_MM_NO_PRETAIL), s);
+        st = trc_cuda_mul_mat(&a, &b, &d, flags & ~(TRC_CUDA_MM_FUSED | TRC_CUDA_MM_NO_PRETAIL | TRC_CUDA_MM_TWO_STEP), s);
     }
     cudaFreeAsync(wf, s);
     return st;
@@ -324,8 +324,14 @@ int trc_cuda_mul_mat_q(int type, const void* w_blocks, int64_t w_ne0, int64_t w_
         return TRC_CUDA_EINVAL;
     if (nelements(*d) == 0) return TRC_CUDA_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Two steps with TRC_CUDA_MM_SIMT (the bit-exact mode) or TRC_CUDA_MM_TWO_STEP, and by default from
+    // kTwoStepMinColumns columns on where the fused kernel cannot stage the packed bytes by TMA;
+    // the fused kernel otherwise (TRC_CUDA_MM_FUSED forces it).
     const bool fused = (flags & TRC_CUDA_MM_FUSED) != 0;
-    if (!fused && ((flags & TRC_CUDA_MM_SIMT) != 0 || b->ne[1] >= kTwoStepMinColumns)) {
+    const bool two_step = (flags & (TRC_CUDA_MM_SIMT | TRC_CUDA_MM_TWO_STEP)) != 0 ||
+                          (b->ne[1] >= kTwoStepMinColumns &&
+                           !mul_mat_q_tma_staged(type, w_blocks, w_ne0, w_ne1, a_transposed, flags));
+    if (!fused && two_step) {
         const int st = mul_mat_q_two_step(type, w_blocks, w_ne0, w_ne1, a_transposed, *b, *d, flags, s);
         if (st != TRC_CUDA_EUNSUPPORTED) return st;  // else: no scratch memory, the fused kernel runs
     }

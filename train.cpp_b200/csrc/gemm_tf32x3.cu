@@ -1302,11 +1302,13 @@ bool mul_mat_tc_eligible(const trc_cuda_view& a_in, const trc_cuda_view& b_in, c
 
 namespace {
 
-// The fused kernel takes B's tails precomputed (one extra pass over B) when B is reused by at least
-// two row tiles and the caller did not opt out: its split warps then only decode A. Measured on
-// B200 (Q5_0 4096 x 14336, 2048 tokens): forward +27 %, dX +16 %. The F32 kernel keeps splitting
-// B in the loop: with its split warps busy on A anyway, the tails' extra TMA traffic cost more than
-// the split work it saved (4096^3: -14 %).
+// The fused kernel whose split warps load the packed words from global memory takes B's tails
+// precomputed (one extra pass over B) when B is reused by at least two row tiles and the caller did
+// not opt out: its split warps then only decode A. Measured on B200 (Q5_0 4096 x 14336, 2048
+// tokens) for that kernel: forward +27 %, dX +16 %. The TMA-staged fused kernel (CTA pairs) and the
+// F32 kernel split B in the loop instead: there the tails' extra TMA traffic and the pass over B
+// cost more than the split work they save (TMA-staged fused: forward 228 vs 196-200 TFLOP/s, dX
+// 235-249 vs 180-198; F32 4096^3: -14 %).
 bool want_pretail(uint32_t flags, int m_tiles) { return (flags & TRC_CUDA_MM_NO_PRETAIL) == 0 && m_tiles >= 2; }
 
 template <int CG>
@@ -1427,13 +1429,12 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
         return sst;
     }
     const CUtensorMap& tmW = sp.ws ? sp.tmW : tmD;
-    Pretail pt;
-    if (want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
-    const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
-
     // CTA pairs stage the packed bytes by TMA where the packed rows allow a tensor map (16-byte
     // aligned base and row pitch); otherwise the split warps load them from global memory.
     const bool ptma = CG == 2 && encode_packed(w_blocks, p.q_row_bytes, w_ne1, type, a_transposed != 0, tmA);
+    Pretail pt;
+    if (!ptma && want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
+    const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
     int st = TRC_CUDA_EUNSUPPORTED;
 #define TRC_Q_CASE(T)                                                                                 \
     case T:                                                                                           \
@@ -1478,6 +1479,14 @@ int mul_mat_tc(const trc_cuda_view& a_in, const trc_cuda_view& b_in, const trc_c
     if ((K + BK - 1) / BK * red2 * red3 >= (int64_t(1) << 30)) return TRC_CUDA_EUNSUPPORTED;
     return use_pair(M, allow_pair) ? mul_mat_tc_impl<2>(a_in, b_in, d, flags, stream)
                                    : mul_mat_tc_impl<1>(a_in, b_in, d, flags, stream);
+}
+
+bool mul_mat_q_tma_staged(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed, uint32_t flags) {
+    const int64_t M = a_transposed ? w_ne0 : w_ne1;
+    const size_t bb = trc_cuda_block_bytes(type);
+    if (bb == 0 || w_ne0 % 32 != 0 || !use_pair(M, (flags & TRC_CUDA_MM_ONE_CTA) == 0)) return false;
+    const int64_t row_bytes = (w_ne0 / 32) * static_cast<int64_t>(bb);
+    return (reinterpret_cast<uint64_t>(w_blocks) & 15u) == 0 && row_bytes % 16 == 0;
 }
 
 int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,

@@ -75,6 +75,9 @@ int mul_mat_tc(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_vi
                cudaStream_t stream);
 // True when mul_mat_tc can address these views with TMA (no launch).
 bool mul_mat_tc_eligible(const trc_cuda_view& a, const trc_cuda_view& b, const trc_cuda_view& d);
+// True when the fused kernel runs on CTA pairs with the packed bytes staged by TMA (16-byte aligned
+// packed rows): the fastest implementation of trc_cuda_mul_mat_q for those weights.
+bool mul_mat_q_tma_staged(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed, uint32_t flags);
 int mul_mat_q_tc(int type, const void* w_blocks, int64_t w_ne0, int64_t w_ne1, int a_transposed,
                  const trc_cuda_view& b, const trc_cuda_view& d, uint32_t flags, cudaStream_t stream);
 

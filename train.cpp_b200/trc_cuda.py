@@ -36,7 +36,7 @@ TYPE_NAMES = {TYPE_Q4_0: "q4_0", TYPE_Q4_1: "q4_1", TYPE_Q5_0: "q5_0", TYPE_Q5_1
 BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_Q8_0: 34}
 QK = 32  # weights per block
 
-MM_ACCUMULATE, MM_SIMT, MM_ONE_CTA, MM_NO_PRETAIL, MM_FUSED = 1, 2, 4, 8, 16
+MM_ACCUMULATE, MM_SIMT, MM_ONE_CTA, MM_NO_PRETAIL, MM_FUSED, MM_TWO_STEP = 1, 2, 4, 8, 16, 32
 BIN_ADD, BIN_SUB, BIN_MUL, BIN_DIV = 0, 1, 2, 3
 
 
@@ -388,9 +388,10 @@ def mul_mat_out_ne(a: torch.Tensor, b: torch.Tensor) -> list[int]:
     return [na[1], nb_[1], nb_[2], nb_[3]]
 
 
-def _mm_flags(accumulate: bool, simt: bool, one_cta: bool, no_pretail: bool = False, fused: bool = False) -> int:
+def _mm_flags(accumulate: bool, simt: bool, one_cta: bool, no_pretail: bool = False, fused: bool = False,
+              two_step: bool = False) -> int:
     return ((MM_ACCUMULATE if accumulate else 0) | (MM_SIMT if simt else 0) | (MM_ONE_CTA if one_cta else 0) |
-            (MM_NO_PRETAIL if no_pretail else 0) | (MM_FUSED if fused else 0))
+            (MM_NO_PRETAIL if no_pretail else 0) | (MM_FUSED if fused else 0) | (MM_TWO_STEP if two_step else 0))
 
 
 def mul_mat(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False,
@@ -437,12 +438,13 @@ def mul_mat_kernel(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, simt: bo
 def mul_mat_q(qtype: int, w_blocks: torch.Tensor, w_ne0: int, w_ne1: int, b: torch.Tensor,
               transposed: bool = False, out: torch.Tensor | None = None, accumulate: bool = False,
               stream=None, one_cta: bool = False, no_pretail: bool = False, fused: bool = False,
-              simt: bool = False) -> torch.Tensor:
+              simt: bool = False, two_step: bool = False) -> torch.Tensor:
     """dequant + mul_mat with a = W (transposed=False) or a = transpose(W), W being the frozen
-    quantized weight of ggml shape [w_ne0, w_ne1] held as packed blocks on the device. From 1024
-    columns of b on, W is dequantized into scratch and the F32 kernel runs; fused=True keeps the
-    fused dequant-in-prologue kernel (no copy of W). simt=True: dequant + the SIMT kernel, bit-exact
-    with the reference."""
+    quantized weight of ggml shape [w_ne0, w_ne1] held as packed blocks on the device. The default
+    is the fused dequant-in-prologue kernel (no copy of W) wherever it can stage the packed bytes
+    by TMA, else, from 1024 columns of b on, W dequantized into scratch + the F32 kernel.
+    fused=True / two_step=True force one of the two (same results). simt=True: dequant + the SIMT
+    kernel, bit-exact with the reference."""
     K, M = (w_ne1, w_ne0) if transposed else (w_ne0, w_ne1)
     nb_ = ggml_ne(b)
     if nb_[0] != K:
@@ -452,7 +454,7 @@ def mul_mat_q(qtype: int, w_blocks: torch.Tensor, w_ne0: int, w_ne1: int, b: tor
     vb, vd = view_of(b), view_of(out)
     _check(lib().trc_cuda_mul_mat_q(qtype, w_blocks.data_ptr(), w_ne0, w_ne1, 1 if transposed else 0,
                                     ctypes.byref(vb), ctypes.byref(vd),
-                                    _mm_flags(accumulate, simt, one_cta, no_pretail, fused),
+                                    _mm_flags(accumulate, simt, one_cta, no_pretail, fused, two_step),
                                     _stream(stream)), "trc_cuda_mul_mat_q")
     return out
 
