@@ -21,7 +21,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <condition_variable>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -74,6 +76,15 @@ bool fake_alloc_failure() {
 
 class CudaDevice;
 
+// Host <-> device copies of one tensor through the device's two pinned chunks (below): the host
+// copy of one chunk overlaps the DMA of the other. Synchronous like cudaMemcpy. Measured on B200
+// for a 235 MB tensor: a pageable cudaMemcpy moves 10.9 GB/s, a pinned one 53.1 GB/s, and a host
+// memcpy into pinned memory 45.5 GB/s.
+constexpr size_t kStagedCopyMin = size_t(4) << 20;   // below this a plain cudaMemcpy
+constexpr size_t kStagedChunk   = size_t(8) << 20;
+void staged_h2d(CudaDevice* dev, void* dst, const void* src, size_t bytes);
+void staged_d2h(CudaDevice* dev, void* dst, const void* src, size_t bytes);
+
 class CudaBufferType : public BufferType {
 public:
     explicit CudaBufferType(CudaDevice* dev, int ordinal) : dev_(dev) {
@@ -105,15 +116,20 @@ public:
     void* base() override { return nullptr; }  // device-local: not mappable by the host
     bool is_host() const override { return false; }
 
+    // Large copies go through the device's pinned chunks (pageable host memory otherwise limits the
+    // copy to about a fifth of what PCIe carries): the reference's tensor_set / tensor_get, and with
+    // them gguf_load_tensor's and checkpoint_load's uploads, run at pinned-copy speed.
     void set_tensor(Tensor* t, size_t offset, const void* data, size_t size) override {
         check_range(t, offset, size, "set_tensor");
         CB_CUDA(trc_cuda_rt_set_device(ordinal_));
-        CB_CUDA(trc_cuda_rt_memcpy(dptr_ + t->data_offset + offset, data, size, 0));
+        if (size >= kStagedCopyMin) staged_h2d(device_of(), dptr_ + t->data_offset + offset, data, size);
+        else CB_CUDA(trc_cuda_rt_memcpy(dptr_ + t->data_offset + offset, data, size, 0));
     }
     void get_tensor(const Tensor* t, size_t offset, void* data, size_t size) const override {
         check_range(t, offset, size, "get_tensor");
         CB_CUDA(trc_cuda_rt_set_device(ordinal_));
-        CB_CUDA(trc_cuda_rt_memcpy(data, dptr_ + t->data_offset + offset, size, 1));
+        if (size >= kStagedCopyMin) staged_d2h(device_of(), data, dptr_ + t->data_offset + offset, size);
+        else CB_CUDA(trc_cuda_rt_memcpy(data, dptr_ + t->data_offset + offset, size, 1));
     }
     void clear() override {
         CB_CUDA(trc_cuda_rt_set_device(ordinal_));
@@ -122,6 +138,7 @@ public:
 
     char* device_ptr() const { return dptr_; }
     int   ordinal() const { return ordinal_; }
+    CudaDevice* device_of() const;
 
 private:
     void check_range(const Tensor* t, size_t offset, size_t size, const char* what) const {
@@ -390,6 +407,22 @@ public:
             scratch_bytes_ = bytes;
         }
         return scratch_;
+    }
+
+    // Two pinned chunks and their events for the staged tensor copies (created on first use, kept
+    // for the device's lifetime).
+    struct CopyRing {
+        void* host[2] = {nullptr, nullptr};
+        void* done[2] = {nullptr, nullptr};
+    };
+    CopyRing& copy_ring() {
+        if (ring_.host[0] == nullptr) {
+            for (int k = 0; k < 2; ++k) {
+                CB_CUDA(trc_cuda_rt_malloc_host(&ring_.host[k], kStagedChunk));
+                CB_CUDA(trc_cuda_rt_event_create(&ring_.done[k]));
+            }
+        }
+        return ring_;
     }
 
     // Pinned host staging for the single-tensor GGUF loader, grown on demand and kept for the
@@ -732,6 +765,7 @@ private:
     size_t         scratch_bytes_ = 0;
     void*          pinned_ = nullptr;
     size_t         pinned_bytes_ = 0;
+    CopyRing       ring_;
 };
 
 Device* CudaBufferType::device() const { return dev_; }
@@ -743,6 +777,113 @@ Buffer* CudaBufferType::alloc_buffer(size_t size) {
     void* p = nullptr;
     if (trc_cuda_rt_malloc(&p, size) != TRC_CUDA_OK) return nullptr;
     return new CudaBuffer(this, ordinal, static_cast<char*>(p), size);
+}
+
+CudaDevice* CudaBuffer::device_of() const { return static_cast<CudaDevice*>(buft_->device()); }
+
+// Host memcpy on several threads: one host thread copies about 10 GB/s, the pinned DMA it feeds
+// runs at 40-55 GB/s. A small pool of worker threads, created on first use, splits each copy into
+// slices; the calling thread copies one slice itself and waits for the rest.
+class CopyPool {
+public:
+    // Never destroyed: its workers wait on its condition variable for the life of the process, and
+    // destroying a condition variable that threads still wait on blocks (glibc) at exit.
+    static CopyPool& get() {
+        static CopyPool* pool = new CopyPool;
+        return *pool;
+    }
+    void copy(void* dst, const void* src, size_t bytes) {
+        const size_t slices = std::min<size_t>(workers_.size() + 1, std::max<size_t>(1, bytes / (size_t(1) << 20)));
+        if (slices <= 1) {
+            std::memcpy(dst, src, bytes);
+            return;
+        }
+        const size_t per = (bytes + slices - 1) / slices;
+        std::lock_guard<std::mutex> one_job(job_mu_);  // callers on several threads take turns
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            dst_ = static_cast<char*>(dst);
+            src_ = static_cast<const char*>(src);
+            bytes_ = bytes;
+            per_ = per;
+            next_ = 1;  // slice 0 is the caller's
+            total_ = slices;
+            pending_ = slices - 1;
+            ++generation_;
+        }
+        cv_.notify_all();
+        std::memcpy(dst, src, std::min(per, bytes));
+        std::unique_lock<std::mutex> lock(mu_);
+        done_cv_.wait(lock, [&] { return pending_ == 0; });
+    }
+
+private:
+    CopyPool() {
+        const unsigned hw = std::thread::hardware_concurrency();
+        const unsigned n = std::max(1u, std::min(7u, hw > 1 ? hw - 1 : 1u));
+        for (unsigned i = 0; i < n; ++i) workers_.emplace_back([this] { run(); });
+        for (auto& w : workers_) w.detach();  // process-lifetime workers
+    }
+    void run() {
+        uint64_t seen = 0;
+        for (;;) {
+            std::unique_lock<std::mutex> lock(mu_);
+            cv_.wait(lock, [&] { return generation_ != seen && next_ < total_; });
+            const size_t i = next_++;
+            if (next_ >= total_) seen = generation_;
+            char* d = dst_;
+            const char* s = src_;
+            const size_t off = i * per_, len = std::min(per_, bytes_ - std::min(bytes_, off));
+            lock.unlock();
+            if (len > 0) std::memcpy(d + off, s + off, len);
+            lock.lock();
+            if (--pending_ == 0) done_cv_.notify_one();
+        }
+    }
+    std::mutex job_mu_, mu_;
+    std::condition_variable cv_, done_cv_;
+    std::vector<std::thread> workers_;
+    char* dst_ = nullptr;
+    const char* src_ = nullptr;
+    size_t bytes_ = 0, per_ = 0, next_ = 0, total_ = 0, pending_ = 0;
+    uint64_t generation_ = 0;
+};
+
+void staged_h2d(CudaDevice* dev, void* dst, const void* src, size_t bytes) {
+    CudaDevice::CopyRing& r = dev->copy_ring();
+    const char* s = static_cast<const char*>(src);
+    char*       d = static_cast<char*>(dst);
+    size_t c = 0;
+    for (size_t off = 0; off < bytes; off += kStagedChunk, ++c) {
+        const int    k   = static_cast<int>(c & 1u);
+        const size_t len = std::min(kStagedChunk, bytes - off);
+        if (c >= 2) CB_CUDA(trc_cuda_rt_event_sync(r.done[k]));  // the DMA that read chunk k finished
+        CopyPool::get().copy(r.host[k], s + off, len);
+        CB_CUDA(trc_cuda_rt_memcpy_async(d + off, r.host[k], len, 0, dev->stream()));
+        CB_CUDA(trc_cuda_rt_event_record(r.done[k], dev->stream()));
+    }
+    CB_CUDA(trc_cuda_rt_stream_sync(dev->stream()));
+}
+
+void staged_d2h(CudaDevice* dev, void* dst, const void* src, size_t bytes) {
+    CudaDevice::CopyRing& r = dev->copy_ring();
+    const char* s = static_cast<const char*>(src);
+    char*       d = static_cast<char*>(dst);
+    const size_t n = (bytes + kStagedChunk - 1) / kStagedChunk;
+    auto issue = [&](size_t c) {
+        const int    k   = static_cast<int>(c & 1u);
+        const size_t off = c * kStagedChunk;
+        CB_CUDA(trc_cuda_rt_memcpy_async(r.host[k], s + off, std::min(kStagedChunk, bytes - off), 1, dev->stream()));
+        CB_CUDA(trc_cuda_rt_event_record(r.done[k], dev->stream()));
+    };
+    issue(0);
+    for (size_t c = 0; c < n; ++c) {
+        if (c + 1 < n) issue(c + 1);  // its chunk's previous contents were copied out in step c - 1
+        const int    k   = static_cast<int>(c & 1u);
+        const size_t off = c * kStagedChunk;
+        CB_CUDA(trc_cuda_rt_event_sync(r.done[k]));
+        CopyPool::get().copy(d + off, r.host[k], std::min(kStagedChunk, bytes - off));
+    }
 }
 
 Device* CudaPackedBufferType::device() const { return dev_; }
