@@ -203,3 +203,24 @@ def test_fused_tma_staged_and_global_load_paths_agree(tc, qtype, transposed):
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
     assert normwise(outs[0], want.reshape(outs[0].shape)) <= 1e-5
     assert bb in (18, 20, 22, 24, 34)
+
+
+@pytest.mark.parametrize("transposed", [False, True], ids=["W", "WT"])
+def test_fused_batched_and_strided_b(tc, transposed):
+    """b with ne[2] = 3, ne[3] = 2 planes (W broadcast over them, as nn::Linear on a [in, tokens,
+    batch] input), and b as an MN-major (transposed) view: the fused kernel on CTA pairs with the
+    TMA-staged packed bytes, within the bar of the reference on every plane."""
+    qtype, w_ne0, w_ne1, n = synth.TYPE_Q8_0, 512, 384, 72
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=130)
+    Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
+    a = np.swapaxes(Wf, -1, -2) if transposed else Wf
+    K = a.shape[-1]
+    x = np.random.default_rng(131).standard_normal((2, 3, n, K)).astype(np.float32)
+    want = oracle.mul_mat(a, x)
+    got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(x), transposed=transposed).cpu().numpy()
+    assert normwise(got, want) <= 1e-5
+    xt = np.ascontiguousarray(np.swapaxes(x[0, 0], -1, -2))           # (K, n): b = transpose view, MN-major
+    want_t = oracle.mul_mat(a, x[0, 0])
+    got_t = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(xt).t(), transposed=transposed).cpu().numpy()
+    assert normwise(got_t.reshape(want_t.shape), want_t) <= 1e-5
+    assert tc.device_error() == 0
