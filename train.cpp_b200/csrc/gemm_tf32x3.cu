@@ -89,7 +89,17 @@ constexpr int CHUNK_KB     = 16;   // k-blocks per fp32 promotion chunk (256 K)
 constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128-row x 32-column fp32 group of D, staged for a TMA store
 constexpr int EPI_BUFS      = 2;            // one staging buffer per epilogue team
 constexpr int EPI_BAR_TEAM0 = 1, EPI_BAR_ALL = 3;  // named barriers: per team (1, 2), all epilogue warps (3)
-constexpr int MAX_STAGES    = 6;
+constexpr int MAX_STAGES    = 12;
+constexpr int BARRIER_BYTES = 512;          // shared memory reserved for struct Barriers
+
+// The F32 kernel's separate raw and tail rings (index: CG): a slot holds 24 KiB of A+B for one CTA,
+// 16 KiB per CTA of a pair. Measured on B200 against tails beside every raw stage (4 stages, the
+// same 192 / 128 KiB): single CTAs (the GQA dA and dB, M = 128) 185-208 against 173-182 TFLOP/s with
+// 5 raw + 3 tail slots, 178 with 6 + 2 and 171-178 with 4 + 4; CTA pairs (Linear forward / dX / dW)
+// 237 / 240 / 214 against 226 / 231 / 212 with 8 + 4 slots, about 1 % less with 8 + 3 or 9 + 3,
+// and dW 195 with 10 + 2 (the split warps then run out of tail slots).
+constexpr int kRawStages[3]  = {0, 5, 8};
+constexpr int kTailStages[3] = {0, 3, 4};
 
 // Shared-memory geometry per CTA group. CG = 1: one CTA computes a 128 x 256 tile from a 128-row
 // A tile and a 256-row B tile. CG = 2 (tcgen05 cta_group::2): a cluster of two CTAs computes a
@@ -97,26 +107,31 @@ constexpr int MAX_STAGES    = 6;
 // leader's MMA reads both CTAs' shared memory, so each SM stages and splits half the B bytes.
 // PQ > 0: the fused kernel's stages also hold PQ bytes of the weight's packed blocks, loaded by TMA
 // (the slot follows the tiles; one stage fewer fits).
-template <int CG, int PQ = 0>
+// TS > 0 (the F32 kernel): the raw A/B tiles and their tails live in two rings of their own -- a
+// deep ring of STAGES raw slots that TMA fills, and a short ring of TS tail slots that the split
+// warps fill just ahead of the MMA -- so more raw bytes can be in flight than with tails beside
+// every stage.
+template <int CG, int PQ = 0, int TS = 0>
 struct Geo {
     static constexpr int BN_CTA      = BN / CG;                     // B rows staged by one CTA
-    // Measured on B200 (F32 products on CTA pairs, TFLOP/s at 6 / 5 / 4 stages): Linear forward
-    // 229.8 / 230.5 / 232.4, dX 233.0 / 232.4 / 238.2, dW 221.8 / 221.4 / 224.6; a deeper ring does
-    // not pay there. The fused kernel measured 255 (dX) with 5 stages and 243 with 4; single CTAs
-    // (GQA dA/dB) lose 7-10% going from 4 stages to 3.
-    static constexpr int STAGES      = CG == 2 ? (PQ ? 5 : 4) : 4;
+    // Stages with tails beside the raw tiles (the fused kernels): the fused dX measured 255 TFLOP/s
+    // with 5 stages and 243 with 4.
     static constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
     static constexpr int B_BYTES     = BN_CTA * BK * 4;             // 16 KiB (CG 1) / 8 KiB (CG 2)
-    static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES) + PQ;  // raw + tail (+ packed A)
-    static constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES, OFF_B_RAW = 2 * A_BYTES;
-    static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;
+    static constexpr int RAW_BYTES   = A_BYTES + B_BYTES;           // one raw (or one tail) A+B slot
+    static constexpr int STAGES      = TS ? kRawStages[CG] : (CG == 2 ? (PQ ? 5 : 4) : 4);
+    static constexpr int STAGE_BYTES = TS ? RAW_BYTES : 2 * RAW_BYTES + PQ;  // raw (+ tail + packed A)
+    static constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES;
+    static constexpr int OFF_B_RAW   = TS ? A_BYTES : 2 * A_BYTES;
+    static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;       // (TS = 0)
     static constexpr int OFF_PQ      = 2 * (A_BYTES + B_BYTES);
+    static constexpr int OFF_TAILS   = STAGES * STAGE_BYTES;        // (TS > 0) tail slot t: OFF_TAILS + t * RAW_BYTES
     static_assert(PQ % 1024 == 0 && (PQ == 0 || CG == 2), "packed slot: 1 KiB multiples, CTA pairs only");
     static constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
-    static constexpr int EPI_OFF     = STAGES * STAGE_BYTES;
-    static constexpr int SMEM_BYTES  = EPI_OFF + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int EPI_OFF     = STAGES * STAGE_BYTES + TS * RAW_BYTES;
+    static constexpr int SMEM_BYTES  = EPI_OFF + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + BARRIER_BYTES;
     static constexpr int TILE_M      = CG * BM;                     // D rows per tile
-    static_assert(STAGES <= MAX_STAGES, "barrier arrays");
+    static_assert(STAGES <= MAX_STAGES && TS <= MAX_STAGES, "barrier arrays");
     static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
@@ -151,11 +166,13 @@ struct Barriers {
     uint64_t full[MAX_STAGES];   // this CTA's TMA tiles of the stage have landed
     uint64_t split[MAX_STAGES];  // (leader) every split warp of the group has written its tails
     uint64_t empty[MAX_STAGES];  // the MMAs reading the stage have completed
+    uint64_t tail_empty[MAX_STAGES];  // (separate tail ring) the MMAs reading the tail slot have completed
     uint64_t acc_full[2];
     uint64_t acc_empty[2];       // (leader) every epilogue warp of the group has drained the buffer
     uint64_t mma_done;
     uint32_t tmem_slot;
 };
+static_assert(sizeof(Barriers) <= BARRIER_BYTES, "barrier reservation");
 
 __device__ __forceinline__ uint32_t tf32_tail_bits(uint32_t u) {
     const float x = __uint_as_float(u);
@@ -241,6 +258,30 @@ __device__ __forceinline__ void split_chunks(uint8_t* st, int i0, int i_end, int
             u.w = tf32_tail_bits(u.w);
             if (i < nA) reinterpret_cast<uint4*>(st + G::OFF_A_TAIL)[i] = u;
             else reinterpret_cast<uint4*>(st + G::OFF_B_TAIL)[i - nA] = u;
+        }
+    }
+}
+
+// split_chunks for the separate raw and tail rings: chunk i of the raw slot [A | B] -> chunk i of the
+// tail slot [A tail | B tail]. All loads are issued before the first store, as above.
+template <int PER>
+__device__ __forceinline__ void split_chunks_rings(const uint8_t* raw, uint8_t* tail, int i0, int i_end, int i_step) {
+    uint4 v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = i0 + j * i_step;
+        if (i < i_end) v[j] = reinterpret_cast<const uint4*>(raw)[i];
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = i0 + j * i_step;
+        if (i < i_end) {
+            uint4 u = v[j];
+            u.x = tf32_tail_bits(u.x);
+            u.y = tf32_tail_bits(u.y);
+            u.z = tf32_tail_bits(u.z);
+            u.w = tf32_tail_bits(u.w);
+            reinterpret_cast<uint4*>(tail)[i] = u;
         }
     }
 }
@@ -365,8 +406,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmD,
                        const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TcParams p) {
-    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value>;
+    constexpr int TS = QTYPE == 0 ? kTailStages[CG] : 0;
+    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value, TS>;
     constexpr bool PTMA = QTYPE != 0 && PT != 0;
+    constexpr int NSPLIT = TS ? TS : G::STAGES;  // slots of the split barriers
     constexpr bool PAIR = CG == 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -379,8 +422,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < G::STAGES; ++s) {
             mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->split[s], (SPLIT_WARPS / (PTMA ? kPtGroups : 1)) * CG);
             mbar_init(&bars->empty[s], 1);
+        }
+        for (int s = 0; s < NSPLIT; ++s) {
+            mbar_init(&bars->split[s], (SPLIT_WARPS / (PTMA ? kPtGroups : 1)) * CG);
+            mbar_init(&bars->tail_empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&bars->acc_full[a], 1);
@@ -447,7 +493,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                     }
                     // B raw, and with b_pretail B's precomputed tail through a map of the same geometry
-                    for (int part = 0; part < (p.b_pretail ? 2 : 1); ++part) {
+                    for (int part = 0; part < (!TS && p.b_pretail ? 2 : 1); ++part) {
                         const CUtensorMap* mb = part == 0 ? &tmB : &tmBt;
                         const uint32_t dstb = st + (part == 0 ? G::OFF_B_RAW : G::OFF_B_TAIL);
                         if (!p.b_mn) {
@@ -493,18 +539,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int kb1 = min(us.kv1, kb0 + CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = it % G::STAGES;
-                        if (!mbar_wait_scoped<PAIR>(&bars->split[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_XFORM)) {
+                        const int ts = TS ? static_cast<int>(it % NSPLIT) : s;  // tail slot / split barrier
+                        if (!mbar_wait_scoped<PAIR>(&bars->split[ts], (it / NSPLIT) & 1u, TRC_DEVERR_WAIT_XFORM)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint32_t st = smem_base + s * G::STAGE_BYTES;
+                        // tails: beside the raw tiles, or in tail slot ts of the separate ring
+                        const uint32_t ta = TS ? smem_base + G::OFF_TAILS + ts * G::RAW_BYTES : st + G::OFF_A_TAIL;
+                        const uint32_t tb = TS ? ta + G::A_BYTES : st + G::OFF_B_TAIL;
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
                             const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + G::OFF_A_RAW, kk) : desc_kmajor(st + G::OFF_A_RAW, kk);
-                            const uint64_t a_tail = p.a_mn ? desc_mnmajor(st + G::OFF_A_TAIL, kk) : desc_kmajor(st + G::OFF_A_TAIL, kk);
+                            const uint64_t a_tail = p.a_mn ? desc_mnmajor(ta, kk) : desc_kmajor(ta, kk);
                             const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + G::OFF_B_RAW, kk) : desc_kmajor(st + G::OFF_B_RAW, kk);
-                            const uint64_t b_tail = p.b_mn ? desc_mnmajor(st + G::OFF_B_TAIL, kk) : desc_kmajor(st + G::OFF_B_TAIL, kk);
+                            const uint64_t b_tail = p.b_mn ? desc_mnmajor(tb, kk) : desc_kmajor(tb, kk);
                             umma_tf32<CG>(d_tmem, a_tail, b_raw, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
                             umma_tf32<CG>(d_tmem, a_raw, b_tail, idesc, 1u);
                             umma_tf32<CG>(d_tmem, a_raw, b_raw, idesc, 1u);
@@ -512,8 +562,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         // frees the stage (in both CTAs) once these MMAs have read it
                         if constexpr (PAIR) {
                             umma_commit_pair_both(&bars->empty[s], 0x3);
+                            if constexpr (TS != 0) umma_commit_pair_both(&bars->tail_empty[ts], 0x3);
                         } else {
                             umma_commit(&bars->empty[s]);
+                            if constexpr (TS != 0) umma_commit(&bars->tail_empty[ts]);
                         }
                     }
                     if (!ok) break;
@@ -720,7 +772,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (p.splits > 1) run(std::true_type{});
             else run(std::false_type{});
         } else {
-            // F32 kernel: all split warps split the A and B tiles.
+            // F32 kernel: all split warps split the A and B tiles of each raw slot into the tail slot
+            // the stage uses, once the MMAs that last read that tail slot have completed.
             const int i_step = SPLIT_WARPS * 32;
             uint32_t it = 0;
             bool ok = true;
@@ -733,11 +786,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     uint8_t* st = smem + s * G::STAGE_BYTES;
-                    const int i_end = p.b_pretail ? nA : nAll;  // B's tails arrive precomputed
-                    split_chunks<G, (nAll + SPLIT_WARPS * 32 - 1) / (SPLIT_WARPS * 32)>(st, t, i_end, i_step, nA);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) arrive_split(s);
+                    if constexpr (TS != 0) {
+                        const int ts = static_cast<int>(it % NSPLIT);
+                        if (it >= static_cast<uint32_t>(NSPLIT) &&
+                            !mbar_wait_scoped<PAIR>(&bars->tail_empty[ts], ((it / NSPLIT) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        split_chunks_rings<(nAll + SPLIT_WARPS * 32 - 1) / (SPLIT_WARPS * 32)>(
+                            st, smem + G::OFF_TAILS + ts * G::RAW_BYTES, t, nAll, i_step);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) arrive_split(ts);
+                    } else {
+                        const int i_end = p.b_pretail ? nA : nAll;  // B's tails arrive precomputed
+                        split_chunks<G, (nAll + SPLIT_WARPS * 32 - 1) / (SPLIT_WARPS * 32)>(st, t, i_end, i_step, nA);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) arrive_split(s);
+                    }
                 }
             }
         }
@@ -1113,7 +1180,7 @@ bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
 template <int QTYPE, int QTRANS, int CG, int PT = 0>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBt, const CUtensorMap& tmD,
               const CUtensorMap& tmW, const TcParams& p, cudaStream_t stream) {
-    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value>;
+    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value, QTYPE == 0 ? kTailStages[CG] : 0>;
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
     static int        max_pairs[64] = {};
