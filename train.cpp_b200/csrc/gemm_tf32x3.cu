@@ -105,33 +105,47 @@ constexpr int kTailStages[3] = {0, 3, 4};
 // A tile and a 256-row B tile. CG = 2 (tcgen05 cta_group::2): a cluster of two CTAs computes a
 // 256 x 256 tile; each CTA stages its own 128 rows of A and 128 of the 256 rows of B, and the
 // leader's MMA reads both CTAs' shared memory, so each SM stages and splits half the B bytes.
-// PQ > 0: the fused kernel's stages also hold PQ bytes of the weight's packed blocks, loaded by TMA
-// (the slot follows the tiles; one stage fewer fits).
-// TS > 0 (the F32 kernel): the raw A/B tiles and their tails live in two rings of their own -- a
-// deep ring of STAGES raw slots that TMA fills, and a short ring of TS tail slots that the split
-// warps fill just ahead of the MMA -- so more raw bytes can be in flight than with tails beside
-// every stage.
+// PQ > 0: the fused kernel's stages also hold PQ bytes of the weight's packed blocks, loaded by TMA.
+// TS > 0: the raw tiles and the split warps' output live in two rings of their own -- a deep ring of
+// STAGES raw slots that TMA fills, and a short ring of TS tail slots that the split warps fill just
+// ahead of the MMA -- so more raw bytes can be in flight than with tails beside every stage.
+//   F32 kernel (PQ = 0): raw slot [A | B], tail slot [A tail | B tail].
+//   fused kernel (PQ > 0): raw slot [B | packed A], tail slot [A head | A tail | B tail].
+// TS = 0: one ring of STAGES slots [A | A tail | B | B tail | packed A].
 template <int CG, int PQ = 0, int TS = 0>
 struct Geo {
     static constexpr int BN_CTA      = BN / CG;                     // B rows staged by one CTA
-    // Stages with tails beside the raw tiles (the fused kernels): the fused dX measured 255 TFLOP/s
-    // with 5 stages and 243 with 4.
     static constexpr int A_BYTES     = BM * BK * 4;                 //  8 KiB
     static constexpr int B_BYTES     = BN_CTA * BK * 4;             // 16 KiB (CG 1) / 8 KiB (CG 2)
-    static constexpr int RAW_BYTES   = A_BYTES + B_BYTES;           // one raw (or one tail) A+B slot
-    static constexpr int STAGES      = TS ? kRawStages[CG] : (CG == 2 ? (PQ ? 5 : 4) : 4);
-    static constexpr int STAGE_BYTES = TS ? RAW_BYTES : 2 * RAW_BYTES + PQ;  // raw (+ tail + packed A)
-    static constexpr int OFF_A_RAW = 0, OFF_A_TAIL = A_BYTES;
-    static constexpr int OFF_B_RAW   = TS ? A_BYTES : 2 * A_BYTES;
-    static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;       // (TS = 0)
-    static constexpr int OFF_PQ      = 2 * (A_BYTES + B_BYTES);
-    static constexpr int OFF_TAILS   = STAGES * STAGE_BYTES;        // (TS > 0) tail slot t: OFF_TAILS + t * RAW_BYTES
+    static constexpr int RAW_BYTES   = A_BYTES + B_BYTES;
     static_assert(PQ % 1024 == 0 && (PQ == 0 || CG == 2), "packed slot: 1 KiB multiples, CTA pairs only");
-    static constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per stage
-    static constexpr int EPI_OFF     = STAGES * STAGE_BYTES + TS * RAW_BYTES;
+    // raw (TS > 0) or whole (TS = 0) stage
+    static constexpr int STAGE_BYTES = TS == 0 ? 2 * RAW_BYTES + PQ : (PQ ? B_BYTES + PQ : RAW_BYTES);
+    static constexpr int OFF_A_RAW   = 0;                           // (PQ = 0) A; (PQ > 0, TS > 0) unused
+    static constexpr int OFF_A_TAIL  = A_BYTES;                     // (TS = 0)
+    static constexpr int OFF_B_RAW   = TS == 0 ? 2 * A_BYTES : (PQ ? 0 : A_BYTES);
+    static constexpr int OFF_B_TAIL  = 2 * A_BYTES + B_BYTES;       // (TS = 0)
+    static constexpr int OFF_PQ      = TS == 0 ? 2 * RAW_BYTES : B_BYTES;
+    // tail slot (TS > 0)
+    static constexpr int TAIL_BYTES  = PQ ? 2 * A_BYTES + B_BYTES : RAW_BYTES;
+    static constexpr int T_A_HEAD    = 0;                           // (PQ > 0)
+    static constexpr int T_A_TAIL    = PQ ? A_BYTES : 0;
+    static constexpr int T_B_TAIL    = PQ ? 2 * A_BYTES : A_BYTES;
+    static constexpr int RING_BUDGET = 232448 - EPI_BUFS * EPI_BUF_BYTES - 1024 - BARRIER_BYTES;
+    static constexpr int fill_stages() {
+        const int n = (RING_BUDGET - TS * TAIL_BYTES) / STAGE_BYTES;
+        return n < MAX_STAGES ? n : MAX_STAGES;
+    }
+    // Stages with tails beside the raw tiles: the fused dX measured 255 TFLOP/s with 5 stages and
+    // 243 with 4. With separate rings the fused kernel takes as many raw slots as fit.
+    static constexpr int STAGES      = TS == 0 ? (CG == 2 ? (PQ ? 5 : 4) : 4) : (PQ ? fill_stages() : kRawStages[CG]);
+    static constexpr int OFF_TAILS   = STAGES * STAGE_BYTES;        // tail slot t: OFF_TAILS + t * TAIL_BYTES
+    static constexpr int RAW_TX_BYTES = A_BYTES + B_BYTES;          // bytes TMA delivers per F32 stage
+    static constexpr int EPI_OFF     = OFF_TAILS + TS * TAIL_BYTES;
     static constexpr int SMEM_BYTES  = EPI_OFF + EPI_BUFS * EPI_BUF_BYTES + 1024 /*align*/ + BARRIER_BYTES;
     static constexpr int TILE_M      = CG * BM;                     // D rows per tile
-    static_assert(STAGES <= MAX_STAGES && TS <= MAX_STAGES, "barrier arrays");
+    static_assert(STAGES >= 2 && STAGES <= MAX_STAGES && TS <= MAX_STAGES, "barrier arrays");
+    static_assert(STAGE_BYTES % 1024 == 0 && TAIL_BYTES % 1024 == 0, "1 KiB-aligned tiles");
     static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
@@ -322,6 +336,21 @@ struct PackedSlot<QTYPE, QTRANS, 1> {
     static constexpr int value = QTYPE == 0 ? 0 : PackedBox<QTYPE == 0 ? 2 : QTYPE, QTRANS>::kSlot;
 };
 
+// Tail slots of the TMA-staged fused kernel's separate rings (its raw slots fill the rest); 0 keeps
+// its tails beside the raw tiles of 5 stages. Measured on B200 (Q5_0 4096 x 14336, 2048 tokens,
+// forward / dX TFLOP/s): 5 stages with tails beside 239.9 / 257.0; 4 tail slots (6 / 9 raw)
+// 231.6 / 244.6; 3 tail slots the same; 2 tail slots 209.5 / 218.0. Its raw slots are small (B and
+// the packed box), so a deeper raw ring buys little, while the decode groups lose tail slots.
+constexpr int kPtTailStages = 0;
+
+// The shared-memory geometry of one kernel instantiation (the kernel and its launch agree on it).
+template <int QTYPE, int QTRANS, int CG, int PT>
+struct KernelGeo {
+    static constexpr int PQ = PackedSlot<QTYPE, QTRANS, PT>::value;
+    static constexpr int TS = QTYPE == 0 ? kTailStages[CG] : (PQ ? kPtTailStages : 0);
+    using type = Geo<CG, PQ, TS>;
+};
+
 // Per tile: the packed-row pointer of quad q (K-major: its W row; MN-major: its K-row offset and
 // block column), nullptr when the quad's rows lie outside the matrix.
 template <int QTYPE, int QTRANS>
@@ -406,8 +435,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmD,
                        const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TcParams p) {
-    constexpr int TS = QTYPE == 0 ? kTailStages[CG] : 0;
-    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value, TS>;
+    using G = typename KernelGeo<QTYPE, QTRANS, CG, PT>::type;
+    constexpr int TS = KernelGeo<QTYPE, QTRANS, CG, PT>::TS;
     constexpr bool PTMA = QTYPE != 0 && PT != 0;
     constexpr int NSPLIT = TS ? TS : G::STAGES;  // slots of the split barriers
     constexpr bool PAIR = CG == 2;
@@ -472,7 +501,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t st = smem_base + s * G::STAGE_BYTES;
                     constexpr int pq_tx = PTMA ? PackedBox<QTYPE, QTRANS>::kBytes : 0;
                     mbar_arrive_expect_tx(&bars->full[s], (QTYPE == 0 ? G::RAW_TX_BYTES : G::B_BYTES) +
-                                                              (p.b_pretail ? G::B_BYTES : 0) + pq_tx);
+                                                              (!TS && p.b_pretail ? G::B_BYTES : 0) + pq_tx);
                     const int k0 = kb * BK;
                     if constexpr (PTMA) {
                         // the stage's packed bytes: from the 16-byte boundary at or below the first one
@@ -546,12 +575,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                         tc_fence_after();
                         const uint32_t st = smem_base + s * G::STAGE_BYTES;
-                        // tails: beside the raw tiles, or in tail slot ts of the separate ring
-                        const uint32_t ta = TS ? smem_base + G::OFF_TAILS + ts * G::RAW_BYTES : st + G::OFF_A_TAIL;
-                        const uint32_t tb = TS ? ta + G::A_BYTES : st + G::OFF_B_TAIL;
+                        // tails: beside the raw tiles, or in tail slot ts of the separate ring (which
+                        // also holds the fused kernel's decoded A head)
+                        const uint32_t tsl = smem_base + G::OFF_TAILS + ts * G::TAIL_BYTES;
+                        const uint32_t ah = TS && QTYPE != 0 ? tsl + G::T_A_HEAD : st + G::OFF_A_RAW;
+                        const uint32_t ta = TS ? tsl + G::T_A_TAIL : st + G::OFF_A_TAIL;
+                        const uint32_t tb = TS ? tsl + G::T_B_TAIL : st + G::OFF_B_TAIL;
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
-                            const uint64_t a_raw  = p.a_mn ? desc_mnmajor(st + G::OFF_A_RAW, kk) : desc_kmajor(st + G::OFF_A_RAW, kk);
+                            const uint64_t a_raw  = p.a_mn ? desc_mnmajor(ah, kk) : desc_kmajor(ah, kk);
                             const uint64_t a_tail = p.a_mn ? desc_mnmajor(ta, kk) : desc_kmajor(ta, kk);
                             const uint64_t b_raw  = p.b_mn ? desc_mnmajor(st + G::OFF_B_RAW, kk) : desc_kmajor(st + G::OFF_B_RAW, kk);
                             const uint64_t b_tail = p.b_mn ? desc_mnmajor(tb, kk) : desc_kmajor(tb, kk);
@@ -619,6 +651,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     uint8_t* st = smem + s * G::STAGE_BYTES;
+                    // the decoded head / tail tiles go to tail slot ts once the MMAs that last read
+                    // it have completed (TS = 0: beside the raw tiles)
+                    const int ts = TS ? static_cast<int>(it % NSPLIT) : s;
+                    uint8_t* tsl = st;
+                    if constexpr (TS != 0) {
+                        if (it >= static_cast<uint32_t>(NSPLIT) &&
+                            !mbar_wait_scoped<PAIR>(&bars->tail_empty[ts], ((it / NSPLIT) & 1u) ^ 1u, TRC_DEVERR_WAIT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        tsl = smem + G::OFF_TAILS + ts * G::TAIL_BYTES;
+                    }
                     const int k0 = kb * BK;
                     const int blk = QTRANS ? (am0 >> 5) : (k0 >> 5);
                     const uint32_t box = smem_u32(st + G::OFF_PQ) + ((blk * PB::kBB) & 15);
@@ -645,12 +689,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             load_quad_words_smem<QTYPE>(bp, j0, wd);
                             decode_quad_words<QTYPE>(wd, j0, w);
                         }
-                        store_quad_head_tail(st, qoff[i], w);
+                        store_quad_head_tail(tsl, qoff[i], w);
                     }
-                    if (!p.b_pretail) split_chunks<G, (nAll - nA + NT - 1) / NT>(st, nA + tg, nAll, NT, nA);
+                    if constexpr (TS != 0) {
+                        split_chunks_rings<(nAll - nA + NT - 1) / NT>(st + G::OFF_B_RAW, tsl + G::T_B_TAIL, tg,
+                                                                      nAll - nA, NT);
+                    } else if (!p.b_pretail) {
+                        split_chunks<G, (nAll - nA + NT - 1) / NT>(st, nA + tg, nAll, NT, nA);
+                    }
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) arrive_split(s);
+                    if (lane == 0) arrive_split(ts);
                 }
             }
         } else if constexpr (QTYPE != 0) {
@@ -794,7 +843,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             break;
                         }
                         split_chunks_rings<(nAll + SPLIT_WARPS * 32 - 1) / (SPLIT_WARPS * 32)>(
-                            st, smem + G::OFF_TAILS + ts * G::RAW_BYTES, t, nAll, i_step);
+                            st, smem + G::OFF_TAILS + ts * G::TAIL_BYTES, t, nAll, i_step);
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) arrive_split(ts);
@@ -1180,7 +1229,7 @@ bool dense_extent(const trc_cuda_view& d, size_t& bytes) {
 template <int QTYPE, int QTRANS, int CG, int PT = 0>
 int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBt, const CUtensorMap& tmD,
               const CUtensorMap& tmW, const TcParams& p, cudaStream_t stream) {
-    using G = Geo<CG, PackedSlot<QTYPE, QTRANS, PT>::value, QTYPE == 0 ? kTailStages[CG] : 0>;
+    using G = typename KernelGeo<QTYPE, QTRANS, CG, PT>::type;
     static std::mutex mu;
     static uint64_t   configured = 0;  // bit per device ordinal
     static int        max_pairs[64] = {};
