@@ -84,7 +84,7 @@ def test_linear_forward_full_size(tc, linear, two_step):
 def test_linear_dx_full_size(tc, linear, two_step):
     """dX = mul_mat(transpose(W), dY): K = 14336, 4096 x 2048 outputs (128 pair tiles of 256 x 256),
     which the planner splits in four parts (two reduce into dX, two into a workspace added by one
-    more kernel)."""
+    more kernel). A stream plan is not taken: the bands its tiles share (352 MB) exceed L2."""
     wq, W, _, dY, Wn = linear
     dX = torch.full((N, K), float("nan"), device="cuda")
     torch.cuda.synchronize()

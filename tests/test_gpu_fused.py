@@ -51,8 +51,9 @@ def test_fused_matches_dequant_then_mul_mat(tc, qtype, transposed, one_cta):
 
 @pytest.mark.parametrize("one_cta", [False, True], ids=["pair", "one_cta"])
 def test_fused_split_k_fills_the_last_wave(tc, one_cta):
-    """The fused kernel split in K: 80 pair tiles (160 single tiles) on 148 SMs run as two parts
-    each, so the split warps' look-ahead of the packed words crosses units of both parts."""
+    """The fused kernel split in K: 80 pair tiles on 74 pairs take a stream plan (the TMA-staged
+    kernel); 160 single tiles on 148 SMs run as two parts each in the kernel whose split warps load
+    the packed words from global memory, so their look-ahead crosses units of both parts."""
     qtype, w_ne0, w_ne1, n = synth.TYPE_Q4_1, 1024, 2560, 2048
     blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=81)
     Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
@@ -66,18 +67,24 @@ def test_fused_split_k_fills_the_last_wave(tc, one_cta):
     assert np.array_equal(got.view(np.uint32), again.reshape(got.shape).view(np.uint32))  # deterministic
 
 
-def test_fused_transposed_split_k_four_parts(tc):
-    """dX's kind of product, transpose(W) . dY, on 75 pair tiles of 256 k-blocks: split in four parts
-    (two into D, two into a workspace added afterwards), deterministic and within the bar (all of it
-    against float64, 64 columns against the oracle)."""
-    qtype, w_ne0, w_ne1, n = synth.TYPE_Q5_0, 3840, 4096, 1280   # A = T(W): M 3840, K 4096
-    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=83)
+@pytest.mark.parametrize("w_ne0,w_ne1,n,launches", [
+    (3840, 4096, 1280, 1),    # 75 pair tiles of 256 k-blocks: stream plan, at most two pieces a tile
+    (2048, 8192, 1024, 2),    # 32 pair tiles of 512 k-blocks: stream plan, pieces 3-4 in the workspace
+    (1024, 16384, 1024, 2),   # 16 pair tiles of 1024 k-blocks: four parts (two in the workspace)
+], ids=["stream", "stream_workspace", "four_parts"])
+def test_fused_transposed_split_k(tc, w_ne0, w_ne1, n, launches):
+    """dX's kind of product, transpose(W) . dY (M = W's ne0, K = W's ne1), through the TMA-staged
+    fused kernel under each split plan: the GEMM, plus the workspace add where pieces or parts go
+    there. Deterministic, and within the bar (all of it against float64, 64 columns against the
+    oracle)."""
+    qtype = synth.TYPE_Q5_0
+    blocks = synth.random_blocks(qtype, w_ne0 * w_ne1 // 32, seed=83 + w_ne1)
     Wf = oracle.dequant(qtype, blocks).reshape(w_ne1, w_ne0)
     dy = (np.random.default_rng(84).standard_normal((n, w_ne1)) * 1e-2).astype(np.float32)
     torch.cuda.synchronize()
     n0 = tc.launch_count()
     got = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True)
-    assert tc.launch_count() - n0 == 2  # the GEMM (B split in the loop) and the workspace add
+    assert tc.launch_count() - n0 == launches
     want64 = (dev(dy).double() @ dev(Wf).double()).cpu().numpy()
     got = got.cpu().numpy().reshape(n, w_ne0)
     again = tc.mul_mat_q(qtype, dev(blocks), w_ne0, w_ne1, dev(dy), transposed=True, fused=True).cpu().numpy()

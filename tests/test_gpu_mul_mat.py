@@ -254,7 +254,10 @@ def test_cta_pair_transposed_output_accumulate_and_plane_reduction(tc, accumulat
 
 # ---- split-K (few tiles, long reductions): two CTAs per tile reduce-add into a zeroed D
 
-@pytest.mark.parametrize("k,m,n,one", [(8192, 128, 512, False), (4096, 256, 256, False), (4096, 256, 256, True)])
+# (1024, 1536, 1280): 30 pair tiles (60 single tiles) of 64 k-blocks, which stream runs would cut
+# into five pieces: two parts, one wave
+@pytest.mark.parametrize("k,m,n,one", [(8192, 128, 512, False), (4096, 256, 256, False), (4096, 256, 256, True),
+                                       (1024, 1536, 1280, False), (1024, 1536, 1280, True)])
 def test_split_k_few_tiles(tc, k, m, n, one):
     rng = np.random.default_rng(k + m + n)
     a = rng.standard_normal((m, k)).astype(np.float32)
@@ -270,15 +273,12 @@ def test_split_k_few_tiles(tc, k, m, n, one):
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))  # deterministic
 
 
-@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
-def test_split_k_four_parts(tc, one):
-    """75 pair tiles on 74 pairs (or 150 tiles on 148 SMs) of 256 k-blocks: two waves unsplit, five
-    quarter-length waves with four parts, which the planner takes (each unit's fixed cost included).
-    Parts 0 and 1 reduce into D, parts 2 and 3 into a workspace that one more kernel adds into D, so
-    the result does not depend on the order the parts land in. Checked in full against float64 and on
-    64 columns against the oracle."""
-    k, m, n = 4096, (3840 if not one else 1280), (1280 if not one else 3840)
-    rng = np.random.default_rng(75)
+def _split_case(tc, k, m, n, one, seed, launches):
+    """One split product: a (m, k) . b (n, k), D pre-filled with NaN (the plan zeroes what it
+    reduces into), the launch count of the library's own kernels, the whole result against float64,
+    64 columns against the oracle, and a second run bit-identical (the parts' order of arrival does
+    not change the sum)."""
+    rng = np.random.default_rng(seed)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = rng.standard_normal((n, k)).astype(np.float32)
     A, B = dev(a), dev(b)
@@ -287,7 +287,7 @@ def test_split_k_four_parts(tc, one):
     torch.cuda.synchronize()
     n0 = tc.launch_count()
     got = tc.mul_mat(A, B, out=out, one_cta=one)
-    assert tc.launch_count() - n0 == 2  # the GEMM and the workspace add
+    assert tc.launch_count() - n0 == launches
     want64 = (B.double() @ A.double().t()).cpu().numpy()
     got = got.cpu().numpy()
     again = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
@@ -299,23 +299,37 @@ def test_split_k_four_parts(tc, one):
 
 
 @pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
-def test_split_k_fills_the_last_wave(tc, one):
-    """More tiles than the grid, just past a multiple of it (80 pair tiles, or 160 single tiles, on
-    148 SMs): the product is split in two so the last wave is not left mostly idle, and each CTA
-    runs several units of both parts."""
-    k, m, n = 1024, 2560, 2048
-    rng = np.random.default_rng(80)
-    a = rng.standard_normal((m, k)).astype(np.float32)
-    b = rng.standard_normal((n, k)).astype(np.float32)
-    want = oracle.mul_mat(a, b)
-    A, B = dev(a), dev(b)
-    out = tc.ggml_empty(tc.mul_mat_out_ne(A, B))
-    out.fill_(float("nan"))
-    got = tc.mul_mat(A, B, out=out, one_cta=one).cpu().numpy()
-    again = tc.mul_mat(A, B, one_cta=one).cpu().numpy()
-    assert tc.device_error() == 0
-    assert normwise(got, want) <= TOL, normwise(got, want)
-    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+def test_split_k_four_parts(tc, one):
+    """16 pair tiles (or 32 single tiles) of 1024 k-blocks: a stream plan would cut a tile into six
+    pieces, so the planner takes four parts (one wave of quarter-length units). Parts 0 and 1 reduce
+    into D, parts 2 and 3 into a workspace that one more kernel adds into D."""
+    _split_case(tc, 16384, 1024, 1024, one, 75, launches=2)  # the GEMM and the workspace add
+
+
+@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
+def test_stream_k_last_wave(tc, one):
+    """75 pair tiles on 74 pairs (or 150 tiles on 148 SMs) of 256 k-blocks: two waves unsplit; the
+    stream plan deals the 75 x 16 k-chunks to the slots in equal runs of 16-17 chunks, so a tile is
+    cut into at most two pieces, both reduce-added into the zeroed D (one launch)."""
+    k, m, n = 4096, (3840 if not one else 1280), (1280 if not one else 3840)
+    _split_case(tc, k, m, n, one, 76, launches=1)
+
+
+@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
+def test_stream_k_workspace(tc, one):
+    """32 pair tiles on 74 pairs (or 64 tiles on 148 SMs) of 512 k-blocks (the GQA dA kind of
+    shape): runs of 13-14 chunks cut a tile of 32 chunks into up to four pieces; the first two
+    reduce into D, the third and fourth into the workspace added afterwards (two launches)."""
+    m, n = (2048, 1024) if not one else (1024, 2048)
+    _split_case(tc, 8192, m, n, one, 77, launches=2)
+
+
+@pytest.mark.parametrize("one", [False, True], ids=["pair", "one_cta"])
+def test_stream_k_after_whole_waves(tc, one):
+    """448 pair tiles on 74 pairs of 64 k-blocks (the Linear forward's tile count; 896 single tiles
+    on 148 SMs): five round-robin waves of whole tiles, stored, then the last 78 (or 156) tiles dealt
+    in chunk runs of about four chunks."""
+    _split_case(tc, 1024, 14336, 2048, one, 78, launches=1)
 
 
 def test_split_k_plane_reduction_one_plane_group(tc):

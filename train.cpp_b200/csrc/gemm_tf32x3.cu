@@ -48,6 +48,7 @@
 #include <cstring>
 #include <type_traits>
 #include <mutex>
+#include <unordered_map>
 
 #include "trc_internal.h"
 #include "trc_ptx.cuh"
@@ -165,7 +166,13 @@ struct TcParams {
     // split-K: each tile's kv range is cut into `splits` parts of kv_per_split k-blocks, computed by
     // different CTAs (work units) and reduce-added into D (zeroed beforehand by the host)
     int     splits, kv_per_split;
-    int64_t total_units;       // total_tiles x splits
+    int64_t total_units;       // units dealt round-robin to the slots: total_tiles x splits, or the
+                               // whole tiles of a stream plan's first waves
+    // stream plan (sk_chunks > 0): after its round-robin units, each slot (CTA or CTA pair of the
+    // grid) takes an equal run of the k-chunks of tiles sk_tile0 .. total_tiles - 1, in tile order
+    int     nck;               // k-chunks (CHUNK_KB k-blocks) per tile
+    int64_t sk_tile0, sk_chunks;
+    int64_t sk_slots;          // slots of the plan: the grid launches exactly this many
     char*   d;
     int64_t d_sm, d_sn, d_s2, d_s3;  // byte strides of D along M, N, plane2, plane3
     int     tma_store;               // 1: D is written (or reduce-added) by TMA from shared memory
@@ -204,14 +211,15 @@ struct TileCoord {
 constexpr int GROUP_M = 8;
 
 template <int CG>
-__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile) {
+__host__ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int64_t tile) {
     const int64_t per_plane = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
     const int64_t plane     = tile / per_plane;
     const int     r         = static_cast<int>(tile - plane * per_plane);
     const int     per_band  = GROUP_M * p.n_tiles;
     const int     band      = r / per_band;
     const int     rb        = r - band * per_band;
-    const int     band_m    = min(GROUP_M, p.m_tiles - band * GROUP_M);  // row tiles in this band
+    const int     left      = p.m_tiles - band * GROUP_M;
+    const int     band_m    = left < GROUP_M ? left : GROUP_M;           // row tiles in this band
     TileCoord c;
     c.m0 = (band * GROUP_M + rb % band_m) * Geo<CG>::TILE_M;
     c.n0 = (rb / band_m) * BN;
@@ -233,6 +241,69 @@ __device__ __forceinline__ UnitSpan unit_span(const TcParams& p, int64_t unit) {
     u.kv1  = min(p.kv_blocks, u.kv0 + p.kv_per_split);
     return u;
 }
+
+// Where a unit's tile goes.
+enum UnitDest { kStoreD = 0, kReduceD = 1, kReduceW = 2 };
+
+// The units of one slot (CTA or CTA pair), in order; every warp role walks the same sequence. First
+// the round-robin units slot, slot + nslots, ... below total_units; then, in a stream plan, the
+// slot's run of k-chunks [slot * sk_chunks / nslots, (slot + 1) * sk_chunks / nslots) of the stream
+// tiles, cut at tile boundaries into pieces. A piece that is a whole tile is stored; a tile cut into
+// pieces has its first two pieces (in k order) reduce-added into D and its third and fourth into
+// the workspace (the plan admits at most four), both zeroed beforehand, so the sum is
+// (a + b) + (c + d) whatever order the pieces land in. The host admits a stream plan only when
+// sk_chunks x nslots < 2^31, so the stream phase runs on 32-bit arithmetic.
+template <int CG>
+struct UnitCursor {
+    int64_t  pos;  // round-robin phase: unit index; stream phase: chunk index among the stream chunks
+    uint32_t end;  // stream phase: the end of this slot's run
+    bool     sk;   // in the stream phase
+
+    static __device__ __forceinline__ uint32_t slot() { return blockIdx.x / CG; }
+    static __device__ __forceinline__ uint32_t nslots() { return gridDim.x / CG; }
+    static __device__ __forceinline__ uint32_t sk_start(const TcParams& p, uint32_t s) {
+        return s * static_cast<uint32_t>(p.sk_chunks) / nslots();
+    }
+    __device__ __forceinline__ void enter_stream(const TcParams& p) {
+        sk  = true;
+        pos = sk_start(p, slot());
+        end = sk_start(p, slot() + 1);
+    }
+    __device__ __forceinline__ explicit UnitCursor(const TcParams& p) : pos(slot()), end(0), sk(false) {
+        if (pos >= p.total_units) enter_stream(p);
+    }
+    __device__ __forceinline__ bool live(const TcParams& p) const {
+        return sk ? static_cast<uint32_t>(pos) < end : pos < p.total_units;
+    }
+    __device__ __forceinline__ UnitSpan span(const TcParams& p) const {
+        if (!sk) return unit_span(p, pos);
+        const uint32_t c = static_cast<uint32_t>(pos), nck = static_cast<uint32_t>(p.nck);
+        const uint32_t lt = c / nck, c0 = c - lt * nck, c1 = min(nck, c0 + (end - c));
+        UnitSpan u;
+        u.tile = p.sk_tile0 + lt;
+        u.kv0  = static_cast<int>(c0) * CHUNK_KB;
+        u.kv1  = min(p.kv_blocks, static_cast<int>(c1) * CHUNK_KB);
+        return u;
+    }
+    __device__ __forceinline__ void next(const TcParams& p) {
+        if (!sk) {
+            pos += nslots();
+            if (pos >= p.total_units) enter_stream(p);
+        } else {
+            const uint32_t nck = static_cast<uint32_t>(p.nck);
+            pos = min(end, (static_cast<uint32_t>(pos) / nck + 1) * nck);
+        }
+    }
+    __device__ __forceinline__ UnitDest dest(const TcParams& p, const UnitSpan& u) const {
+        if (!sk) return pos >= 2 * p.total_tiles ? kReduceW : (p.accumulate || p.splits > 1 ? kReduceD : kStoreD);
+        if (u.kv0 == 0) return u.kv1 == p.kv_blocks ? kStoreD : kReduceD;  // the tile's first piece
+        // A piece that starts inside its tile starts this slot's run, so the previous slot holds the
+        // chunks just before it: the tile's first piece (this is the second) if it also holds the
+        // tile's first chunk, else a middle piece (this is the third or fourth).
+        const uint32_t first = static_cast<uint32_t>(u.tile - p.sk_tile0) * static_cast<uint32_t>(p.nck);
+        return sk_start(p, slot() - 1) <= first ? kReduceD : kReduceW;
+    }
+};
 
 // K-major tile (rows x 16 fp32, 64 B per row, 8-row swizzle atoms of 512 B): advance 32 B per K=8.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
@@ -484,8 +555,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
-                const UnitSpan us = unit_span(p, unit);
+            for (UnitCursor<CG> cur(p); cur.live(p) && ok; cur.next(p)) {
+                const UnitSpan us = cur.span(p);
                 const TileCoord tc = tile_coord<CG>(p, us.tile);
                 const int am0 = tc.m0 + BM * static_cast<int>(rank);              // this CTA's A rows
                 const int bn0 = tc.n0 + G::BN_CTA * static_cast<int>(rank);       // this CTA's B rows
@@ -553,8 +624,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // uses0/uses1: chunks committed so far into TMEM buffer 0/1 (scalars, kept in registers)
             uint32_t it = 0, tcount = 0, uses0 = 0, uses1 = 0;
             bool ok = true;
-            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step, ++tcount) {
-                const UnitSpan us = unit_span(p, unit);
+            for (UnitCursor<CG> cur(p); cur.live(p) && ok; cur.next(p), ++tcount) {
+                const UnitSpan us = cur.span(p);
                 const int tb = tcount & 1;  // this unit's running-total buffer; chunks >= 1 use tb ^ 1
                 for (int kb0 = us.kv0; kb0 < us.kv1 && ok; kb0 += CHUNK_KB) {
                     const int b = kb0 == us.kv0 ? tb : tb ^ 1;
@@ -640,8 +711,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int row_off = BM * static_cast<int>(rank);
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
-                const UnitSpan us = unit_span(p, unit);
+            for (UnitCursor<CG> cur(p); cur.live(p) && ok; cur.next(p)) {
+                const UnitSpan us = cur.span(p);
                 const int am0 = tile_coord<CG>(p, us.tile).m0 + row_off;
                 for (int kb = us.kv0; kb < us.kv1; ++kb, ++it) {
                     if (static_cast<int>(it % kPtGroups) != group) continue;
@@ -826,8 +897,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int i_step = SPLIT_WARPS * 32;
             uint32_t it = 0;
             bool ok = true;
-            for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step) {
-                const UnitSpan us = unit_span(p, unit);
+            for (UnitCursor<CG> cur(p); cur.live(p) && ok; cur.next(p)) {
+                const UnitSpan us = cur.span(p);
                 for (int kb = us.kv0; kb < us.kv1; ++kb, ++it) {
                     const int s = it % G::STAGES;
                     if (!mbar_wait(&bars->full[s], (it / G::STAGES) & 1u, TRC_DEVERR_WAIT_FULL)) {
@@ -879,8 +950,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else mbar_arrive(&bars->acc_empty[b]);
         };
         bool ok = true;
-        for (int64_t unit = tile0; unit < p.total_units && ok; unit += tile_step, ++tcount) {
-            const UnitSpan us = unit_span(p, unit);
+        for (UnitCursor<CG> cur(p); cur.live(p) && ok; cur.next(p), ++tcount) {
+            const UnitSpan us = cur.span(p);
+            const UnitDest dest = cur.dest(p, us);
             const int tb = tcount & 1, xb = tb ^ 1;
             const TileCoord tc = tile_coord<CG>(p, us.tile);
             const int dm0 = tc.m0 + BM * static_cast<int>(rank);  // this CTA's rows of D
@@ -952,11 +1024,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     named_barrier_sync(team_bar, 128);
                     if (team_leader) {
                         const uint32_t src = smem_u32(sb);
-                        // parts 2 and 3 of a four-part split-K product go to the workspace
-                        if (unit >= 2 * p.total_tiles)
-                            tma_reduce_add_4d(&tmW, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
-                        else if (p.accumulate || p.splits > 1)
-                            tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
+                        if (dest == kReduceW) tma_reduce_add_4d(&tmW, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
+                        else if (dest == kReduceD) tma_reduce_add_4d(&tmD, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
                         else tma_store_4d(&tmD, src, dm0, tc.n0 + g * 16, tc.p2, tc.p3);
                         bulk_commit_group();
                     }
@@ -1270,11 +1339,14 @@ int launch_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap&
         }
         if (CG == 2 && dev < 64 && max_pairs[dev] > 0) pairs = std::min(pairs, max_pairs[dev]);
     }
+    // a stream plan deals its chunks to exactly sk_slots slots (more than fit at once only queue; no
+    // slot waits for another); the fused kernel that loads packed words itself has no stream phase
+    if (p.sk_chunks > 0 && (p.sk_slots <= 0 || (QTYPE != 0 && PT == 0))) return TRC_CUDA_EINVAL;
     if constexpr (CG == 1) {
-        const int64_t grid = std::min<int64_t>(p.total_units, sms);
+        const int64_t grid = p.sk_chunks > 0 ? p.sk_slots : std::min<int64_t>(p.total_units, sms);
         kernel<<<static_cast<unsigned>(grid), NUM_THREADS, G::SMEM_BYTES, stream>>>(tmA, tmB, tmBt, tmD, tmW, p);
     } else {
-        const int64_t clusters = std::min<int64_t>(p.total_units, std::max(1, pairs));
+        const int64_t clusters = p.sk_chunks > 0 ? p.sk_slots : std::min<int64_t>(p.total_units, std::max(1, pairs));
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1319,27 +1391,72 @@ struct SplitPlan {
     CUtensorMap tmW;
 };
 
+// The bytes of operand bands that at least two of the tiles [t0, t1) read over their whole
+// reduction: an A band is a tile row's TILE_M rows of A, a B band a tile column's BN rows of B, per
+// output plane. Tiles of the round-robin waves run side by side at the same point of K, so a band
+// they share is read from HBM about once; the slots of a stream phase run at scattered points of
+// K, so a shared band stays in L2 between its readers only if all such bands fit there at once.
+template <int CG>
+int64_t shared_band_bytes(const TcParams& p, int64_t t0, int64_t t1) {
+    std::unordered_map<int64_t, int> a_uses, b_uses;
+    const int64_t per_plane = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+    for (int64_t t = t0; t < t1; ++t) {
+        const TileCoord c = tile_coord<CG>(p, t);
+        const int64_t plane = t / per_plane;
+        ++a_uses[plane * p.m_tiles + c.m0 / Geo<CG>::TILE_M];
+        ++b_uses[plane * p.n_tiles + c.n0 / BN];
+    }
+    const int64_t kbytes = static_cast<int64_t>(p.kv_blocks) * BK * 4;
+    int64_t bytes = 0;
+    for (const auto& u : a_uses)
+        if (u.second >= 2) bytes += Geo<CG>::TILE_M * kbytes;
+    for (const auto& u : b_uses)
+        if (u.second >= 2) bytes += BN * kbytes;
+    return bytes;
+}
+
+int64_t l2_bytes_current() {
+    int dev = 0, l2 = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return l2;
+}
+
 // Split K when it shortens the schedule. The persistent grid runs the units in waves of one unit
-// per CTA (or CTA pair), and a tile count just above a multiple of the grid leaves most of the last
-// wave idle: 256 tiles on 74 pairs take 4 waves for 3.46 waves of work. Cutting every tile's
-// reduction into s parts gives s times the units at 1/s the length each, but every unit also pays a
-// fixed cost (filling and draining the pipeline, storing or reduce-adding its tile, and with four
-// parts the workspace pass). The plan takes the part count s in {1, 2, 4} whose schedule is
-// shortest, costed as waves(s) x (k-blocks per part + kUnitCostKb), and splits only when that is at
-// least 1 % shorter than not splitting. kUnitCostKb = 12 k-blocks is fitted to timings on B200:
-// 4 parts lengthen the GQA dB at one ne[3] plane (256 tiles of 128 k-blocks on 148 SMs) by a
-// quarter although its waves shrink from 2 to 1.75, and shorten the Linear dX (128 tiles of 896
-// k-blocks on 74 pairs) by 7 %.
+// per slot (CTA or CTA pair), and a tile count just above a multiple of the grid leaves most of the
+// last wave idle: 448 tiles on 74 pairs take 7 waves for 6.05 waves of work. The plans:
+//   - s parts (s in {1, 2, 4}): every tile's reduction is cut into s parts, s times the units at
+//     1/s the length each;
+//   - stream: all but the last (partial) wave of whole tiles run round-robin as unsplit, and the
+//     remaining tiles' k-chunks are dealt to the slots in equal runs (UnitCursor), so every slot
+//     ends within a chunk of the others. Only where the bands the stream tiles share fit in 80 %
+//     of L2 (shared_band_bytes): measured on B200, the Linear forward's last 78 tiles (96 MB of
+//     shared bands) ran 2-6 % faster as a stream phase; the Linear dX (352 MB) 4-6 % slower than
+//     four parts, and the GQA dA at eight ne[3] planes (108 MB) 2 % slower than two.
+// Every unit also pays a fixed cost (filling and draining the pipeline, storing or reduce-adding its
+// tile, and with four parts the workspace pass). A plan is costed as the k-blocks its busiest slot
+// runs plus kUnitCostKb per unit; the shortest one is taken when it is at least 1 % shorter than
+// not splitting. kUnitCostKb = 12 k-blocks is fitted to timings on B200: 4 parts lengthen the GQA
+// dB at one ne[3] plane (256 tiles of 128 k-blocks on 148 SMs) by a quarter although its waves
+// shrink from 2 to 1.75, and shorten the Linear dX (128 tiles of 896 k-blocks on 74 pairs) by 7 %.
 // The result never depends on the order in which parts land:
 // - two parts reduce-add into a D zeroed here: 0 + a + b = 0 + b + a;
 // - with four, parts 0 and 1 go to D and parts 2 and 3 to the workspace, and finish_split() adds
-//   the two afterwards: (a + b) + (c + d).
-// No ACCUMULATE, since D + a + b would depend on the order.
+//   the two afterwards: (a + b) + (c + d);
+// - a stream plan cuts a tile into at most four pieces and routes them the same way.
+// No ACCUMULATE, since D + a + b would depend on the order. `allow_stream` is false for kernels whose
+// loops do not walk UnitCursor (the fused kernel that loads packed words from global memory).
 template <int CG>
-int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& sp, cudaStream_t stream) {
+int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& sp, cudaStream_t stream,
+               bool allow_stream = true) {
     p.splits = 1;
     p.kv_per_split = p.kv_blocks;
     p.total_units = p.total_tiles;
+    p.nck = 0;
+    p.sk_tile0 = 0;
+    p.sk_chunks = 0;
     const int sms = sm_count_current();
     const int64_t slots = CG == 2 ? sms / 2 : sms;
     size_t dense_bytes = 0;
@@ -1360,6 +1477,28 @@ int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& 
     }
     if (p.kv_blocks >= 4 * CHUNK_KB && 3 * per_part(4) < p.kv_blocks && length(4) <= 0.99 * unsplit &&
         length(4) < best) {
+        parts = 4;
+        best = length(4);
+    }
+    // stream plan: F round-robin waves of whole tiles, then the rest in equal chunk runs
+    const int nck = (p.kv_blocks + CHUNK_KB - 1) / CHUNK_KB;
+    const int64_t F = std::max<int64_t>(0, p.total_tiles / slots - 1);
+    const int64_t sk_tiles = p.total_tiles - F * slots;
+    const int64_t sk_chunks = sk_tiles * nck;
+    const int64_t run_min = sk_chunks / slots, run_max = (sk_chunks + slots - 1) / slots;
+    int max_pieces = 0;  // most pieces any stream tile is cut into
+    if (allow_stream && run_min >= 1 && sk_chunks * (slots + 1) < (int64_t(1) << 31) &&
+        shared_band_bytes<CG>(p, F * slots, p.total_tiles) * 5 <= l2_bytes_current() * 4) {
+        max_pieces = static_cast<int>((nck - 1) / run_min + 2);
+        const double len = double(F) * (p.kv_blocks + kUnitCostKb) + double(sk_tiles) * p.kv_blocks / slots +
+                           double((run_max - 1) / nck + 2) * kUnitCostKb;
+        if (max_pieces <= 4 && len <= 0.99 * unsplit && len < best) {
+            parts = 0;  // stream
+            best = len;
+        }
+    }
+    const bool need_ws = parts == 4 || (parts == 0 && max_pieces > 2);
+    if (need_ws) {
         retain_pool_once();
         if (cudaMallocAsync(&sp.ws, dense_bytes, stream) != cudaSuccess) {
             cudaGetLastError();
@@ -1371,13 +1510,21 @@ int plan_split(const trc_cuda_view& d, bool accumulate, TcParams& p, SplitPlan& 
             sp.ws = nullptr;
         } else {
             sp.bytes = dense_bytes;
-            parts = 4;
         }
+        if (sp.ws == nullptr) parts = length(2) <= 0.99 * unsplit ? 2 : 1;  // no workspace: at most two parts
     }
     if (parts == 1) return TRC_CUDA_OK;
-    p.splits = parts;
-    p.kv_per_split = per_part(parts);
-    p.total_units = p.total_tiles * parts;
+    if (parts == 0) {
+        p.total_units = F * slots;
+        p.nck = nck;
+        p.sk_tile0 = F * slots;
+        p.sk_chunks = sk_chunks;
+        p.sk_slots = slots;
+    } else {
+        p.splits = parts;
+        p.kv_per_split = per_part(parts);
+        p.total_units = p.total_tiles * parts;
+    }
     const cudaError_t e = cudaMemsetAsync(d.data, 0, dense_bytes, stream);
     return e == cudaSuccess ? TRC_CUDA_OK : cuda_fail(e);
 }
@@ -1542,16 +1689,16 @@ int mul_mat_q_tc_impl(int type, const void* w_blocks, int64_t w_ne0, int64_t w_n
     CUtensorMap tmD;
     std::memset(&tmD, 0, sizeof(tmD));
     p.tma_store = encode_output(d.data, M, N, b.ne[2], b.ne[3], p.d_sm, p.d_sn, p.d_s2, p.d_s3, tmD) ? 1 : 0;
+    // CTA pairs stage the packed bytes by TMA where the packed rows allow a tensor map (16-byte
+    // aligned base and row pitch); otherwise the split warps load them from global memory.
+    const bool ptma = CG == 2 && encode_packed(w_blocks, p.q_row_bytes, w_ne1, type, a_transposed != 0, tmA);
     SplitPlan sp;
-    const int sst = plan_split<CG>(d, accumulate, p, sp, stream);
+    const int sst = plan_split<CG>(d, accumulate, p, sp, stream, /*allow_stream=*/ptma);
     if (sst != TRC_CUDA_OK) {
         finish_split(sp, d.data, false, stream);
         return sst;
     }
     const CUtensorMap& tmW = sp.ws ? sp.tmW : tmD;
-    // CTA pairs stage the packed bytes by TMA where the packed rows allow a tensor map (16-byte
-    // aligned base and row pitch); otherwise the split warps load them from global memory.
-    const bool ptma = CG == 2 && encode_packed(w_blocks, p.q_row_bytes, w_ne1, type, a_transposed != 0, tmA);
     Pretail pt;
     if (!ptma && want_pretail(flags, p.m_tiles) && make_pretail(b, G::BN_CTA, b_mn, b5, stream, pt)) p.b_pretail = 1;
     const CUtensorMap& tmBt = p.b_pretail ? pt.map : tmB;
