@@ -99,14 +99,21 @@ int load_quant_pipelined(int type, const uint8_t* host, int64_t n_blocks, uint8_
         if ((e = cudaEventCreateWithFlags(&u.landed, cudaEventDisableTiming)) != cudaSuccess) return cuda_fail(e);
         u.ready = true;
     }
-    const int64_t total_bytes = n_blocks * static_cast<int64_t>(bb);
-    const int64_t n_chunks    = (total_bytes + static_cast<int64_t>(kUploadChunkBytes) - 1) / kUploadChunkBytes;
-    int64_t chunk = (n_blocks + n_chunks - 1) / n_chunks;
+    // Chunks of about kUploadChunkBytes, then a tapered tail of a quarter and about an eighth of
+    // that: only the last chunk's dequant runs with no copy beside it, so it is kept small. Every
+    // chunk starts on a whole run (the last one ends with the tensor's ragged end).
+    const auto blocks_of = [&](size_t bytes) {
+        return std::max<int64_t>(kRunBlocks, static_cast<int64_t>(bytes / bb) / kRunBlocks * kRunBlocks);
+    };
+    const int64_t tail1 = blocks_of(kUploadChunkBytes / 4);
+    const int64_t front = (n_blocks - tail1 - blocks_of(kUploadChunkBytes / 8)) / kRunBlocks * kRunBlocks;
+    const int64_t n_front = (front + blocks_of(kUploadChunkBytes) - 1) / blocks_of(kUploadChunkBytes);
+    int64_t chunk = (front + n_front - 1) / n_front;
     chunk = (chunk + kRunBlocks - 1) / kRunBlocks * kRunBlocks;
     if ((e = cudaEventRecord(u.start, s)) != cudaSuccess) return cuda_fail(e);
     if ((e = cudaStreamWaitEvent(u.copy, u.start, 0)) != cudaSuccess) return cuda_fail(e);
-    for (int64_t b0 = 0; b0 < n_blocks; b0 += chunk) {
-        const int64_t nb = std::min(chunk, n_blocks - b0);
+    for (int64_t b0 = 0; b0 < n_blocks;) {
+        const int64_t nb = b0 < front ? std::min(chunk, front - b0) : b0 == front ? tail1 : n_blocks - b0;
         const size_t off = static_cast<size_t>(b0) * bb;
         e = cudaMemcpyAsync(staging + off, host + off, static_cast<size_t>(nb) * bb, cudaMemcpyHostToDevice, u.copy);
         if (e != cudaSuccess) return cuda_fail(e);
@@ -114,6 +121,7 @@ int load_quant_pipelined(int type, const uint8_t* host, int64_t n_blocks, uint8_
         if ((e = cudaStreamWaitEvent(s, u.landed, 0)) != cudaSuccess) return cuda_fail(e);
         const int st = trc_cuda_dequant(type, staging + off, nb, out + b0 * 32, s);
         if (st != TRC_CUDA_OK) return st;
+        b0 += nb;
     }
     return TRC_CUDA_OK;
 }
