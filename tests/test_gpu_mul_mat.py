@@ -332,6 +332,43 @@ def test_stream_k_after_whole_waves(tc, one):
     _split_case(tc, 1024, 14336, 2048, one, 78, launches=1)
 
 
+# Shapes around the last partial wave, where the planner takes stream plans: ragged M, N and K
+# (edge tiles, a partial last k-chunk), broadcast planes, MN-major operands, both tile shapes, and
+# a plan that cuts tiles into up to four pieces (pieces 3-4 in the workspace) or four parts.
+# (M, N, K, one_cta, (a2, a3), (b2, b3), A MN-major, B MN-major)
+SPLIT_SWEEP = [
+    (2560, 1900, 1536, False, (1, 1), (1, 1), False, False),  # 80 pair tiles, ragged N
+    (2300, 2300, 1024, False, (1, 1), (1, 1), True, False),   # 81 pair tiles, ragged M and N, MN-major A
+    (1280, 3800, 2048, True, (1, 1), (1, 1), False, True),    # 150 single tiles, MN-major B
+    (1000, 1024, 4096, True, (2, 1), (4, 2), False, False),   # 256 single tiles over 8 broadcast planes
+    (512, 1536, 3072, False, (2, 2), (4, 2), False, False),   # 96 pair tiles over 8 planes
+    (4096, 2600, 640, False, (1, 1), (1, 1), True, True),     # 176 pair tiles of 3 chunks, both MN-major
+    (2400, 2048, 1000, False, (1, 1), (1, 1), False, False),  # K = 1000: a partial last k-block
+    (1000, 2000, 8192, True, (1, 1), (1, 1), False, False),   # 64 single tiles cut into up to 4 pieces
+    (300, 2048, 8192, True, (1, 1), (1, 1), False, False),    # 24 single tiles: four parts
+]
+
+
+@pytest.mark.parametrize("m,n,k,one,ap,bp,ta,tb", SPLIT_SWEEP)
+def test_split_plans_sweep(tc, m, n, k, one, ap, bp, ta, tb):
+    """Every plan the planner takes on these shapes gives the product within the float64 bar and
+    the same bits on a second run. D starts as NaN: every element must be written."""
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a2, a3 = ap
+    b2, b3 = bp
+    a_store = torch.randn((a3, a2, k, m) if ta else (a3, a2, m, k), generator=g, device="cuda")
+    b_store = torch.randn((b3, b2, k, n) if tb else (b3, b2, n, k), generator=g, device="cuda")
+    A, B = op(a_store, ta), op(b_store, tb)                                # logical (.., rows, K)
+    out = torch.full((b3, b2, n, m), float("nan"), device="cuda")
+    got = tc.mul_mat(A, B, out=out, one_cta=one).clone()
+    again = tc.mul_mat(A, B, out=out, one_cta=one)
+    assert tc.device_error() == 0
+    Ar = A.double().repeat(b3 // a3, b2 // a2, 1, 1)
+    want = B.double() @ Ar.transpose(-1, -2)                               # (b3, b2, n, m)
+    assert ((got.double() - want).abs().max() / want.abs().max()).item() <= 5e-6
+    assert torch.equal(got.view(torch.int32), again.view(torch.int32))
+
+
 def test_split_k_plane_reduction_one_plane_group(tc):
     """The GQA dA product at one ne[3] plane per rank (the 8-GPU shape, reduced in size): M = 128
     after the orientation swap, few tiles, K = 2048 x 4 source planes."""
