@@ -381,9 +381,11 @@ def run_ours(args) -> None:
 
     def per_format_launch_us(reps: int) -> dict:
         """Per-format launch times (one tensor per launch), CUDA events on the launching stream
-        around each launch. A 256 MB read before every launch evicts L2, so the 25-48 MB of packed
-        input come from HBM, not from the previous launch's L2 lines. (A read, not a write: a write
-        would leave L2 full of dirty lines, whose write-back the timed launch would pay for.)"""
+        around each launch; the median of the reps (one slow launch, such as the first after the
+        warm-up, would otherwise carry a mean). A 256 MB read before every launch evicts L2, so the
+        25-48 MB of packed input come from HBM, not from the previous launch's L2 lines. (A read,
+        not a write: a write would leave L2 full of dirty lines, whose write-back the timed launch
+        would pay for.)"""
         scrub = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
         for t in FORMATS:
             for _ in range(2):
@@ -399,7 +401,7 @@ def run_ours(args) -> None:
                 pairs[t].append((a, b))
         torch.cuda.synchronize()
         del scrub
-        return {t: sum(a.elapsed_time(b) for a, b in pairs[t]) / reps for t in FORMATS}
+        return {t: statistics.median(a.elapsed_time(b) for a, b in pairs[t]) for t in FORMATS}
 
     # correctness guard for the measured configuration (first tensor of each format, a slice)
     step()
