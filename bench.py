@@ -987,18 +987,28 @@ def _ref_gflops(a_base, a_trans, b_base, b_trans, flops: float) -> float | None:
     return round(flops / best / 1e9, 3)
 
 
+def _extrapolated_s(rates: dict, flops_per_product: float) -> float | None:
+    """Seconds the reference CPU backend would take for the whole step (each product's FLOPs at
+    its measured slice rate)."""
+    vals = [rates[k] for k in rates if k.endswith("_gflops")]
+    if any(v is None or v <= 0 for v in vals):
+        return None
+    return round(sum(flops_per_product / (v * 1e9) for v in vals), 1)
+
+
 def linear_cpu_rates(tc, torch, wq, K, M, X, dY) -> dict:
     """The reference CPU backend on deterministic slices of the Linear step (it would take hours
     in full): forward on 16 token columns, dX on 4, dW on 4 of its K columns."""
     W = tc.gguf_tensor_to_f32(synth.TYPE_Q5_0, wq).view(M, K).cpu().numpy()
     Xn, dYn = X.cpu().numpy(), dY.cpu().numpy()
-    return {
+    rates = {
         "fwd_gflops": _ref_gflops(W, False, Xn[:16], False, 2.0 * K * M * 16),
         "dx_gflops": _ref_gflops(W, True, dYn[:4], False, 2.0 * K * M * 4),
         "dw_gflops": _ref_gflops(dYn, True, np.ascontiguousarray(Xn[:, :4]), True, 2.0 * X.shape[0] * M * 4),
-        "cores": 1, "kind": "reference",
-        "sample": "forward: 16 of 2048 token columns; dX: 4 columns; dW: 4 of 4096 output columns",
     }
+    return {**rates, "extrapolated_step_s": _extrapolated_s(rates, 2.0 * K * M * X.shape[0]),
+            "cores": 1, "kind": "reference",
+            "sample": "forward: 16 of 2048 token columns; dX: 4 columns; dW: 4 of 4096 output columns"}
 
 
 def gqa_cpu_rates(A, B, G) -> dict:
@@ -1007,13 +1017,15 @@ def gqa_cpu_rates(A, B, G) -> dict:
     a = A[0, 0].cpu().numpy()          # [2048, 128]: ne [128, 2048]
     b = B[0, 0].cpu().numpy()
     g = G[0, 0].cpu().numpy()          # [2048, 2048]
-    return {
+    rates = {
         "fwd_gflops": _ref_gflops(a, False, b, False, 2.0 * 128 * 2048 * 2048),
         "da_gflops": _ref_gflops(g, True, np.ascontiguousarray(b[:, :16]), True, 2.0 * 2048 * 2048 * 16),
         "db_gflops": _ref_gflops(a, True, np.ascontiguousarray(g[:64]), False, 2.0 * 2048 * 128 * 64),
-        "cores": 1, "kind": "reference",
-        "sample": "one plane; forward in full, dA on 16 of 128 columns, dB on 64 of 2048 columns",
     }
+    planes = G.shape[0] * G.shape[1]  # the rank's (i2, i3) planes
+    return {**rates, "extrapolated_step_s": _extrapolated_s(rates, 2.0 * 128 * 2048 * 2048 * planes),
+            "cores": 1, "kind": "reference",
+            "sample": "one plane; forward in full, dA on 16 of 128 columns, dB on 64 of 2048 columns"}
 
 
 def main() -> None:
