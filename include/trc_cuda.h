@@ -134,9 +134,9 @@ int trc_cuda_dequant_many_to_peers(const trc_cuda_dequant_job* jobs, int n_jobs,
  * the caller's device staging buffer (>= n_blocks*block_bytes bytes, 16-byte aligned), then
  * dequantizes into `out`. Only the packed bytes cross PCIe (the reference copies the 4-8x larger
  * F32 result). Pinned host memory makes the copy asynchronous; pageable memory is also accepted.
- * Tensors of 16 MB packed or more are uploaded in chunks of about 8 MB (the last two about 2 MB and
- * 1 MB) on the library's own copy stream, and `stream` dequantizes each chunk once it has landed,
- * so copy and dequant overlap.
+ * Tensors of 16 MB packed or more are uploaded in chunks of up to 32 MB (the last two about 2 MB
+ * and 1 MB) on the library's own copy stream, and `stream` dequantizes each chunk once it has
+ * landed, so copy and dequant overlap.
  * The first chunk waits for the work already queued on `stream`, so the staging buffer may be
  * reused by consecutive calls on one stream. */
 int trc_cuda_load_quant(int type, const void* host_blocks, int64_t n_blocks, void* staging, float* out,
