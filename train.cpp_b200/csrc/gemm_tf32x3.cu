@@ -21,11 +21,16 @@
 // double buffering survives: tile i keeps its total in buffer i%2 and its chunks in buffer
 // (i+1)%2, and tile i+1's first chunk can start while tile i's total is being stored.
 //
+// Schedule: persistent; each CTA (or CTA pair) walks its units (UnitCursor): whole tiles round-robin,
+// the parts of a split-K plan, or a stream plan's run of k-chunks (plan_split).
+//
 // Structure (persistent, 18 warps per CTA):
-//   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (a ring of 4-6 stages)
+//   warp 0      TMA producer: raw fp32 A/B tiles -> shared memory (F32 kernel: a ring of raw
+//               slots; fused kernel: a ring of 5 stages that also holds the packed weight bytes)
 //   warp 1      TMEM allocator + single-thread UMMA issuer (tcgen05.mma.kind::tf32)
-//   warps 2-9   split warps: write the tails tA, tB of each stage next to the raw tiles (fused
-//               variant: also decode the packed weight tile into head + tail)
+//   warps 2-9   split warps: write the tails tA, tB of each stage (F32 kernel: into a short ring
+//               of tail slots of their own; fused kernel: next to the raw tiles, after decoding
+//               the packed weight tile into head + tail)
 //   warps 10-17 epilogue, two teams of four (one per column half): TMEM -> registers (tcgen05.ld)
 //               -> shared memory -> TMA store (or strided stores when TMA cannot address D)
 // CTA pairs (default when M spans more than 128 rows): a cluster of two CTAs computes a 256 x 256
