@@ -43,7 +43,9 @@ constexpr int kMaxPeers  = 8;         // copies of each output written to other 
 // CTAs per SM of the bulk-store kernel (5 would fit). Measured on B200, five-tensor step: 3 per SM
 // 5.98 TB/s, 4 per SM 5.77, 5 per SM 5.57; a plain streaming probe with the same bulk stores
 // peaked at 3 per SM as well. A third input buffer (packed bytes two runs ahead instead of one)
-// measured 5.71 against 5.97 TB/s.
+// measured 5.71 against 5.97 TB/s, and a warp-asynchronous output path (each warp bulk-storing its
+// own 2 KiB slice, input slots released through an mbarrier, no CTA-wide barrier per run) 5.38
+// against 5.99: one 16 KiB bulk store per run beats eight of 2 KiB.
 constexpr int kBulkCtasPerSm = 3;
 
 struct DqJob {
