@@ -214,3 +214,36 @@ def test_loader_wrappers_reject_bad_device_destinations(tc):
     with pytest.raises(tc.TrcCudaError):
         tc.gguf_tensor_to_f32(synth.TYPE_Q4_0, dev(host.numpy()), out=torch.empty(64, dtype=torch.float16, device="cuda"))
     assert tc.device_error() == 0
+
+
+def test_peer_store_kernel_on_one_gpu(tc):
+    """The dequant variant that writes every output also at the same offset of other buffers
+    (trc_cuda_dequant_many_to_peers: the all-gather fused into the dequant, one peer per other
+    GPU). Here the "peer" is a second buffer on the same GPU, so the kernel runs on one device:
+    all five formats, a ragged tail, both copies bit-exact with the reference dequantizers."""
+    import ctypes
+
+    jobs, total = [], 0
+    for i, qtype in enumerate(synth.BLOCK_BYTES):
+        n_blocks = 3000 + 77 * i                                  # not a multiple of a run
+        jobs.append((qtype, synth.random_blocks(qtype, n_blocks, seed=300 + i), total, n_blocks))
+        total += n_blocks * 32
+    local = torch.full((total,), float("nan"), device="cuda")
+    mirror = torch.full((total,), float("nan"), device="cuda")
+    packed = [dev(b) for _, b, _, _ in jobs]
+    arr = (tc.DequantJob * len(jobs))()
+    for k, ((qtype, _, off, n_blocks), p) in enumerate(zip(jobs, packed)):
+        arr[k].blocks = p.data_ptr()
+        arr[k].out = local.data_ptr() + 4 * off
+        arr[k].n_blocks = n_blocks
+        arr[k].type = qtype
+    peers = (ctypes.c_void_p * 1)(mirror.data_ptr())
+    st = tc.lib().trc_cuda_dequant_many_to_peers(arr, len(jobs), ctypes.c_void_p(local.data_ptr()), peers, 1, None)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert tc.device_error() == 0
+    got_l, got_m = local.cpu().numpy(), mirror.cpu().numpy()
+    for qtype, blocks, off, n_blocks in jobs:
+        want = oracle.dequant(qtype, blocks, n_blocks)
+        assert bits_equal(got_l[off:off + n_blocks * 32], want), qtype
+        assert bits_equal(got_m[off:off + n_blocks * 32], want), qtype

@@ -4,19 +4,20 @@
 // 320-417 of train.cpp). HBM-bound: per 32 weights it reads 18..34 packed bytes and writes 128.
 //
 // Layout and schedule
-//   * A "run" is 128 consecutive blocks of one tensor (2.25-4.25 KiB packed, 16 KiB of F32 out).
-//   * Persistent CTAs of 256 threads walk the runs of all jobs of a launch (one launch can cover a
-//     whole model shard). Each CTA double-buffers its runs in shared memory: while it decodes run r
-//     it already has the bulk copy (cp.async.bulk, TMA engine) of its next run in flight.
-//   * Decode: warp w owns blocks 16w..16w+15 of the run. In each of 4 steps a lane decodes 4
+//   * A "run" is 256 consecutive blocks of one tensor (4.5-8.5 KiB packed, 32 KiB of F32 out).
+//   * Persistent CTAs of 256 threads (two per SM) walk the runs of all jobs of a launch (one launch
+//     can cover a whole model shard). Each CTA double-buffers its runs in shared memory: while it
+//     decodes run r it already has the bulk copy (cp.async.bulk, TMA engine) of its next run in
+//     flight.
+//   * Decode: warp w owns blocks 32w..32w+31 of the run. In each of 8 steps a lane decodes 4
 //     weights (a quad) of one of 4 blocks, and the warp writes 4 x 128 B = 512 contiguous bytes.
 //   * Output: the decoded run goes to one of two F32 buffers in shared memory, and one bulk copy
 //     (cp.async.bulk global <- shared) writes it to HBM while the CTA decodes the next run. On
-//     B200 this writes the dequant's 1:5.4 read:write mix at 5.98 TB/s of algorithmic traffic
-//     (five 4096 x 11008 tensors of all formats in one launch), 91 % of the 6.55 TB/s copy peak,
+//     B200 this writes the dequant's 1:5.4 read:write mix at 6.20-6.23 TB/s of algorithmic traffic
+//     (five 4096 x 11008 tensors of all formats in one launch), 95 % of the 6.55 TB/s copy peak,
 //     against 5.55 TB/s with 16-byte streaming st.global stores from registers.
-//   * The peer variant (all-gather fused into the dequant) keeps the register stores: it writes
-//     every quad to the local buffer and to each peer's buffer over NVLink.
+//   * The peer variant (all-gather fused into the dequant) keeps the register stores and runs of
+//     128 blocks: it writes every quad to the local buffer and to each peer's buffer over NVLink.
 //   * A run whose packed bytes are not 16-byte aligned / sized (a tensor's ragged tail, or an
 //     unaligned tensor) is staged by ordinary loads instead of the bulk copy, and a run whose output
 //     is not 16-byte aligned is written from shared memory with ordinary stores.
@@ -35,18 +36,26 @@ namespace trc {
 namespace {
 
 constexpr int kThreads   = 256;
-constexpr int kRun       = 128;       // blocks per run
+// Blocks per run: 256 for the bulk-store kernel (one 32 KiB bulk store of F32 per run), 128 for the
+// peer-store kernel.
+template <bool PEERS>
+constexpr int kRunOf = PEERS ? 128 : 256;
 constexpr int kMaxBlk    = 34;        // largest block (Q8_0)
 constexpr int kMaxJobs   = 256;       // jobs per launch (kernel parameter of ~10 KiB)
-constexpr int kBufBytes  = kRun * kMaxBlk;
+template <bool PEERS>
+constexpr int kBufBytesOf = kRunOf<PEERS> * kMaxBlk;
+// Dynamic shared memory of dequant_kernel<PEERS>: two input slots, two output buffers (bulk-store
+// kernel), two mbarriers.
+template <bool PEERS>
+constexpr int kSmemOf = 2 * kBufBytesOf<PEERS> + (PEERS ? 0 : 2 * kRunOf<PEERS> * 32 * 4) + 16;
 constexpr int kMaxPeers  = 8;         // copies of each output written to other GPUs' buffers
-// CTAs per SM of the bulk-store kernel (5 would fit). Measured on B200, five-tensor step: 3 per SM
-// 5.98 TB/s, 4 per SM 5.77, 5 per SM 5.57; a plain streaming probe with the same bulk stores
-// peaked at 3 per SM as well. A third input buffer (packed bytes two runs ahead instead of one)
-// measured 5.71 against 5.97 TB/s, and a warp-asynchronous output path (each warp bulk-storing its
-// own 2 KiB slice, input slots released through an mbarrier, no CTA-wide barrier per run) 5.38
-// against 5.99: one 16 KiB bulk store per run beats eight of 2 KiB.
-constexpr int kBulkCtasPerSm = 3;
+// CTAs per SM of the bulk-store kernel. Measured on B200, five-tensor step (TB/s): runs of 256
+// blocks at 2 CTAs per SM 6.20-6.23; runs of 128 at 3 per SM 5.97-6.00 (4 per SM 5.77, 5 per SM
+// 5.57); 192 at 3 per SM 5.78; 320 at 2 per SM 5.84; 512 at 1 per SM 5.67. A third input buffer
+// (packed bytes two runs ahead instead of one) measured 5.71 against 5.97, and a warp-asynchronous
+// output path (each warp bulk-storing its own 2 KiB slice, input slots released through an
+// mbarrier, no CTA-wide barrier per run) 5.38 against 5.99: few large bulk stores win.
+constexpr int kBulkCtasPerSm = 2;
 
 struct DqJob {
     const uint8_t* src;
@@ -65,9 +74,10 @@ struct DqBatch {
     int64_t peer_delta[kMaxPeers];  // byte distance from a job's out to its copy in peer p's buffer
 };
 
+template <int RUN>
 __device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
-    const int64_t b0    = local_run * kRun;
-    const int64_t nblk  = min(static_cast<int64_t>(kRun), J.n_blocks - b0);
+    const int64_t b0    = local_run * RUN;
+    const int64_t nblk  = min(static_cast<int64_t>(RUN), J.n_blocks - b0);
     const uint64_t addr = reinterpret_cast<uint64_t>(J.src) + static_cast<uint64_t>(b0) * J.block_bytes;
     const int64_t bytes = nblk * J.block_bytes;
     return (addr & 15u) == 0 && (bytes & 15) == 0;
@@ -77,17 +87,17 @@ __device__ __forceinline__ bool run_bulk_ok(const DqJob& J, int64_t local_run) {
 // addresses, plain stores over NVLink), which fuses the all-gather of a sharded tensor into its
 // dequantization.
 // Decodes a staged run into the CTA's output buffer in shared memory (F32, the run's layout), from
-// where one bulk copy writes it to HBM. Warp w owns blocks (kRun/8)w .. (kRun/8)(w+1)-1; in each step a
+// where one bulk copy writes it to HBM. Warp w owns blocks (RUN/8)w .. (RUN/8)(w+1)-1; in each step a
 // lane decodes 4 weights of one of 4 blocks, so a warp writes 512 contiguous bytes (no bank
 // conflicts).
-template <int TYPE>
+template <int TYPE, int RUN>
 __device__ __forceinline__ void decode_run_smem(const uint8_t* buf, float* obuf, int nblk) {
     constexpr int kBB = QuantTraits<TYPE>::kBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = lane & 7;
 #pragma unroll 2
-    for (int step = 0; step < kRun / 32; ++step) {
-        const int lb = warp * (kRun / 8) + step * 4 + (lane >> 3);
+    for (int step = 0; step < RUN / 32; ++step) {
+        const int lb = warp * (RUN / 8) + step * 4 + (lane >> 3);
         if (lb < nblk) {
             float w[4];
             QuadWords r;
@@ -105,9 +115,10 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = lane & 7;
     const bool vec_ok = (reinterpret_cast<uint64_t>(J.out) & 15u) == 0;
+    constexpr int RUN = kRunOf<PEERS>;
 #pragma unroll 2
-    for (int step = 0; step < kRun / 32; ++step) {
-        const int lb = warp * (kRun / 8) + step * 4 + (lane >> 3);
+    for (int step = 0; step < RUN / 32; ++step) {
+        const int lb = warp * (RUN / 8) + step * 4 + (lane >> 3);
         if (lb < nblk) {
             float w[4];
             QuadWords r;
@@ -139,10 +150,13 @@ __device__ __forceinline__ void decode_run(const uint8_t* buf, const DqJob& J, i
 // CTAs than can be resident would run a ragged second wave).
 template <bool PEERS>
 __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DqBatch batch) {
-    __shared__ __align__(128) uint8_t buf[2][kBufBytes];
-    // decoded runs, written to HBM by bulk copies (two, so one can drain while the next fills)
-    __shared__ __align__(128) float obuf[PEERS ? 1 : 2][PEERS ? 4 : kRun * 32];
-    __shared__ __align__(8) uint64_t bar[2];
+    constexpr int RUN = kRunOf<PEERS>, BUF = kBufBytesOf<PEERS>;
+    // (dynamic) two input slots; the bulk-store kernel's decoded runs, written to HBM by bulk copies
+    // (two, so one can drain while the next fills); two mbarriers
+    extern __shared__ __align__(128) uint8_t dq_smem[];
+    uint8_t (*buf)[BUF] = reinterpret_cast<uint8_t (*)[BUF]>(dq_smem);
+    float (*obuf)[RUN * 32] = reinterpret_cast<float (*)[RUN * 32]>(dq_smem + 2 * BUF);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(dq_smem + 2 * BUF + (PEERS ? 0 : 2 * RUN * 32 * 4));
 
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
@@ -161,8 +175,8 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     };
     auto issue = [&](int64_t run, int j, int slot) {
         const DqJob&  J     = batch.job[j];
-        const int64_t b0    = (run - J.run_begin) * kRun;
-        const int64_t nblk  = min(static_cast<int64_t>(kRun), J.n_blocks - b0);
+        const int64_t b0    = (run - J.run_begin) * RUN;
+        const int64_t nblk  = min(static_cast<int64_t>(RUN), J.n_blocks - b0);
         const uint32_t bytes = static_cast<uint32_t>(nblk * J.block_bytes);
         mbar_arrive_expect_tx(&bar[slot], bytes);
         bulk_load(smem_u32(buf[slot]), J.src + b0 * J.block_bytes, bytes, &bar[slot]);
@@ -173,7 +187,7 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
     bool    ok  = true;
     if (run < batch.total_runs) {
         locate(run, jcur);
-        if (run_bulk_ok(batch.job[jcur], run - batch.job[jcur].run_begin)) {
+        if (run_bulk_ok<RUN>(batch.job[jcur], run - batch.job[jcur].run_begin)) {
             if (threadIdx.x == 0) issue(run, jcur, 0);
             pending_bits |= 1u;
         }
@@ -183,8 +197,8 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
         locate(run, jcur);
         const DqJob&  J     = batch.job[jcur];
         const int64_t local = run - J.run_begin;
-        const int64_t b0    = local * kRun;
-        const int     nblk  = static_cast<int>(min(static_cast<int64_t>(kRun), J.n_blocks - b0));
+        const int64_t b0    = local * RUN;
+        const int     nblk  = static_cast<int>(min(static_cast<int64_t>(RUN), J.n_blocks - b0));
 
         // Prefetch the next run into the other slot (its previous contents were consumed in the
         // previous iteration, which ended with __syncthreads()).
@@ -192,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
         if (next < batch.total_runs) {
             int jn = jcur;
             locate(next, jn);
-            if (run_bulk_ok(batch.job[jn], next - batch.job[jn].run_begin)) {
+            if (run_bulk_ok<RUN>(batch.job[jn], next - batch.job[jn].run_begin)) {
                 if (threadIdx.x == 0) issue(next, jn, slot ^ 1);
                 pending_bits |= 1u << (slot ^ 1);
             }
@@ -227,11 +241,11 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant
             // run's, from the other buffer (each run ends by waiting for all older ones).
             float* ob = obuf[slot];
             switch (J.type) {
-                case 2: decode_run_smem<2>(buf[slot], ob, nblk); break;
-                case 3: decode_run_smem<3>(buf[slot], ob, nblk); break;
-                case 6: decode_run_smem<6>(buf[slot], ob, nblk); break;
-                case 7: decode_run_smem<7>(buf[slot], ob, nblk); break;
-                case 8: decode_run_smem<8>(buf[slot], ob, nblk); break;
+                case 2: decode_run_smem<2, RUN>(buf[slot], ob, nblk); break;
+                case 3: decode_run_smem<3, RUN>(buf[slot], ob, nblk); break;
+                case 6: decode_run_smem<6, RUN>(buf[slot], ob, nblk); break;
+                case 7: decode_run_smem<7, RUN>(buf[slot], ob, nblk); break;
+                case 8: decode_run_smem<8, RUN>(buf[slot], ob, nblk); break;
                 default: break;
             }
             float* dst = J.out + b0 * 32;
@@ -275,7 +289,10 @@ int resident_ctas() {
     std::lock_guard<std::mutex> lock(mu);
     if (cached[dev] == 0) {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, dequant_kernel<PEERS>, kThreads, 0) != cudaSuccess)
+        if (cudaFuncSetAttribute(dequant_kernel<PEERS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOf<PEERS>) !=
+                cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, dequant_kernel<PEERS>, kThreads, kSmemOf<PEERS>) !=
+                cudaSuccess)
             return 0;
         cached[dev] = n;
     }
@@ -336,7 +353,8 @@ int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void*
             J.run_begin   = runs;
             J.type        = in.type;
             J.block_bytes = static_cast<int32_t>(bb);
-            runs += (in.n_blocks + kRun - 1) / kRun;
+            const int run_blocks = n_peers > 0 ? kRunOf<true> : kRunOf<false>;
+            runs += (in.n_blocks + run_blocks - 1) / run_blocks;
         }
         if (batch.n_jobs == 0) continue;
         batch.total_runs = runs;
@@ -344,8 +362,8 @@ int dequant_jobs_peers(const trc_cuda_dequant_job* jobs, int n_jobs, const void*
         if (n_peers == 0) per_sm = std::min(per_sm, kBulkCtasPerSm);
         if (per_sm <= 0) return TRC_CUDA_ECUDA;
         const int64_t grid = std::min<int64_t>(runs, static_cast<int64_t>(sms) * per_sm);
-        if (n_peers > 0) dequant_kernel<true><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
-        else dequant_kernel<false><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(batch);
+        if (n_peers > 0) dequant_kernel<true><<<static_cast<unsigned>(grid), kThreads, kSmemOf<true>, stream>>>(batch);
+        else dequant_kernel<false><<<static_cast<unsigned>(grid), kThreads, kSmemOf<false>, stream>>>(batch);
         note_launch();
         const int st = check_launch();
         if (st != TRC_CUDA_OK) return st;
